@@ -1,0 +1,42 @@
+"""Shared fixtures. GPU tests are marked `gpu`; everything else runs on CPU."""
+
+from __future__ import annotations
+
+import os
+import sys
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA device (B200, sm_100a)")
+
+
+@pytest.fixture(scope="session")
+def tiny_prepared(tmp_path_factory):
+    """Seeded synthetic Qwen2 model with the 0.5B head geometry (14q/2kv/64)
+    at a size the CPU oracle runs in milliseconds."""
+    from cheetah_b200.prepared import TINY, write_prepared
+
+    root = tmp_path_factory.mktemp("tiny_qwen2")
+    write_prepared(root, TINY, seed=0)
+    return root
+
+
+@pytest.fixture(scope="session")
+def tiny7b_prepared(tmp_path_factory):
+    """Seeded synthetic model with the 7B head geometry (28q/4kv/128), untied."""
+    from cheetah_b200.prepared import TINY_7B_HEADS, write_prepared
+
+    root = tmp_path_factory.mktemp("tiny_qwen2_7bheads")
+    write_prepared(root, TINY_7B_HEADS, seed=0)
+    return root
+
+
+def reference_tree() -> Path:
+    return Path(os.environ.get("CHEETAH_REFERENCE", "/root/reference"))
