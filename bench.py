@@ -1,0 +1,370 @@
+#!/usr/bin/env python
+"""Benchmark of the Cheetah decoder hot path on B200 (driver contract).
+
+Default workload: Qwen2-0.5B-architecture decoder,
+seeded random-init bf16 weights in the prepared (`cheetah init`) layout,
+batch 1, a 512-token uniform-random prompt, then greedy decode. A timed
+"step" is one decode token through the whole model (embedding, 24 layers,
+final norm, lm_head, greedy argmax).
+
+  value  device-resident decode tok/s: K greedy steps chained on the device
+         (cheetah_cuda_generate_greedy), CUDA events on the sequence stream.
+  e2e    the same tokens through the public ModelForward call
+         (cheetah_cuda_forward_ex): host token in, host logits (vocab f32) +
+         greedy id out, every step, host wall clock.
+  roofline  the dominant kernel (bf16 weight-streaming GEMV) timed live with
+         CUDA events against MEASURED_PEAKS.json's copy bandwidth.
+  cpu_baseline  the C++ restatement of the reference AVX2 path (oracle/),
+         all host threads, on a bounded sample of the same workload.
+
+`--impl reference` times that CPU restatement alone (the reference is Rust
+and cannot be built in this image). Under torchrun (N>1) each rank decodes
+its own sequence on its own GPU (sequence-sharded replicas, no collective on
+the data path); value = all ranks' tokens / max-over-ranks time.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+PROMPT_LEN = 512
+METRIC = "decode tok/s (B=1 & batched) + GQA attn HBM GB/s vs peak; prefill tok/s"
+
+
+def peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return float(data["hbm_gbs"]), float(data.get("bf16_tflops", 1634.5)), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int, interval_ms: int = 50):
+        self.device_index = device_index
+        self.proc = None
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(device_index), f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", str(interval_ms)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, ValueError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": float(np.median(sm)) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "samples": len(sm), "reasons": sorted(reasons)}
+
+
+def cpu_baseline(model_dir, cfg, decode_steps: int):
+    """Oracle (C++ restatement of the reference AVX2 path) decode tok/s on a
+    bounded sample: 512-token prompt (untimed prefill) + decode steps."""
+    import oracle as O
+    from cheetah_b200.prepared import PreparedModel
+
+    O.set_threads(os.cpu_count() or 1)
+    pm = PreparedModel(model_dir)
+    ref = O.OracleModel(pm, cfg, "bf16")
+    prompt = np.random.default_rng(1).integers(0, cfg["vocab_size"], PROMPT_LEN).astype(np.uint32)
+    logits = ref.forward(prompt, 0)
+    tok = int(np.argmax(logits))
+    t0 = time.perf_counter()
+    for i in range(decode_steps):
+        logits = ref.forward([tok], PROMPT_LEN + i)
+        tok = int(np.argmax(logits))
+    dt = time.perf_counter() - t0
+    return {"value": decode_steps / dt, "unit": "tok/s", "cores": O.threads(), "kind": "port",
+            "sample": f"Qwen2-0.5B B=1: {decode_steps} greedy decode steps after a {PROMPT_LEN}-token "
+                      f"prompt (C++ restatement of the reference AVX2 path, -O3)",
+            "ms_per_token": 1e3 * dt / decode_steps}
+
+
+def run_reference(args):
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return 0
+    from cheetah_b200.prepared import PreparedModel, cached_synthetic, resolve_config
+    model_dir = cached_synthetic("qwen2-0.5b")
+    cfg = resolve_config(PreparedModel(model_dir))
+    per_step = []
+    import oracle as O
+    O.set_threads(os.cpu_count() or 1)
+    ref = O.OracleModel(PreparedModel(model_dir), cfg, "bf16")
+    prompt = np.random.default_rng(1).integers(0, cfg["vocab_size"], PROMPT_LEN).astype(np.uint32)
+    tok = int(np.argmax(ref.forward(prompt, 0)))
+    pos = PROMPT_LEN
+    for i in range(args.warmup + args.steps):
+        t0 = time.perf_counter()
+        tok = int(np.argmax(ref.forward([tok], pos)))
+        pos += 1
+        if i >= args.warmup:
+            per_step.append(time.perf_counter() - t0)
+    total = sum(per_step)
+    value = len(per_step) / total
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / len(per_step),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded random-init bf16 weights, uniform-random prompt ids)",
+        "config": {"workload": "qwen2-0.5b decode B=1 (512-token prompt, greedy)", "batch": 1,
+                   "prompt": PROMPT_LEN, "parallelism": "single process (CPU)"},
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": O.threads(), "kind": "port",
+                         "sample": f"{args.steps} decode steps after a {PROMPT_LEN}-token prompt; the "
+                                   "reference is Rust (no toolchain here), so its AVX2 path runs as the "
+                                   "C++ restatement in oracle/"},
+        "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def gemv_roofline(torch, R, hbm_peak, reps=20):
+    """Time the lm_head-shaped bf16 GEMV (151936 x 896, 272 MB > L2) with CUDA
+    events on its launching stream."""
+    rows, cols = 151936, 896
+    w = (torch.randn(rows, cols, device="cuda", dtype=torch.float32) * 0.02).to(torch.bfloat16)
+    x = torch.randn(1, cols, device="cuda")
+    stream = torch.cuda.current_stream()
+    for _ in range(3):
+        R.gemv_bf16(w, x, stream=stream)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    start.record(stream)
+    for _ in range(reps):
+        R.gemv_bf16(w, x, stream=stream)
+    end.record(stream)
+    end.synchronize()
+    sec = start.elapsed_time(end) / 1e3 / reps
+    bytes_ = rows * cols * 2 + cols * 4 + rows * 4
+    achieved = bytes_ / sec / 1e9
+    return {"bound": "hbm", "kernel": "gemv_bf16_kernel (lm_head 151936x896)", "achieved": achieved,
+            "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak, "traffic": None,
+            "bytes_per_launch": bytes_, "us_per_launch": sec * 1e6}
+
+
+def attention_microbench(torch, R, hbm_peak, quick: bool):
+    """Config 2: paged GQA decode attention, bf16 K/V ~N(0,1), shuffled pages."""
+    rows = []
+    shapes = [(14, 2, 64), (28, 4, 128)]
+    batches = [1, 8, 32, 64]
+    lengths = [1024, 4096, 16384, 32768]
+    if quick:
+        batches, lengths = [1, 64], [1024, 32768]
+    page = 64
+    for qh, kvh, D in shapes:
+        for B in batches:
+            for L in lengths:
+                pages_per = L // page
+                total = B * pages_per
+                gen = torch.Generator(device="cuda").manual_seed(B * 100003 + L + D)
+                k = torch.randn(total, kvh, page, D, device="cuda", dtype=torch.bfloat16, generator=gen)
+                v = torch.randn(total, kvh, page, D, device="cuda", dtype=torch.bfloat16, generator=gen)
+                perm = torch.randperm(total, device="cuda", generator=gen).to(torch.int32)
+                table = perm.view(B, pages_per).contiguous()
+                q = torch.randn(B, qh, D, device="cuda", generator=gen)
+                lens = torch.full((B,), L, dtype=torch.int32, device="cuda")
+                out = torch.empty_like(q)
+                stream = torch.cuda.current_stream()
+                for _ in range(3):
+                    R.decode_attention(q, k, v, table, lens, L, out=out, stream=stream)
+                reps = 10
+                s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                torch.cuda.synchronize()
+                s.record(stream)
+                for _ in range(reps):
+                    R.decode_attention(q, k, v, table, lens, L, out=out, stream=stream)
+                e.record(stream)
+                e.synchronize()
+                sec = s.elapsed_time(e) / 1e3 / reps
+                bytes_ = B * kvh * L * D * 2 * 2 + B * qh * D * 4 * 2
+                gbs = bytes_ / sec / 1e9
+                rows.append({"shape": f"{qh}/{kvh}/{D}", "B": B, "L": L, "us": round(sec * 1e6, 2),
+                             "GBps": round(gbs, 1), "frac_measured": round(gbs / hbm_peak, 4),
+                             "frac_8TBps": round(gbs / 8000.0, 4)})
+                del k, v, q, out, table, perm
+                torch.cuda.empty_cache()
+    return rows
+
+
+def run_ours(args):
+    import torch
+    from cheetah_b200 import runtime as R
+    from cheetah_b200.prepared import PreparedModel, cached_synthetic, resolve_config
+
+    world, rank, local = dist_env()
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120))
+    else:
+        torch.cuda.set_device(local)
+    hbm_peak, _, peak_kind = peaks()
+
+    model_dir = cached_synthetic("qwen2-0.5b")
+    cfg = resolve_config(PreparedModel(model_dir))
+    total_positions = PROMPT_LEN + args.warmup + args.steps + 8
+    model = R.CudaModel(model_dir, device=local, max_positions=max(4096, total_positions + 64))
+    prompt = np.random.default_rng(1 + rank).integers(0, cfg["vocab_size"], PROMPT_LEN).astype(np.uint32)
+
+    # ---- value: device-resident greedy chain ----
+    seq = model.new_sequence()
+    first = int(np.argmax(seq.forward(prompt, 0)))
+    warm = seq.generate_greedy(first, PROMPT_LEN, max(args.warmup, 3))
+    next_tok = int(warm[-1])
+    pos = PROMPT_LEN + max(args.warmup, 3)
+    stream = torch.cuda.ExternalStream(seq.stream_handle())
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    seq.generate_greedy(next_tok, pos, args.steps, wait=False)
+    end.record(stream)
+    end.synchronize()
+    torch.cuda.synchronize()
+    clock_info = clocks.stop()
+    elapsed = start.elapsed_time(end) / 1e3
+    if world > 1:
+        t = torch.tensor([elapsed], device="cuda", dtype=torch.float64)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        elapsed = float(t.item())
+    value = world * args.steps / elapsed
+    ms_per_step = 1e3 * elapsed / args.steps
+
+    # ---- e2e: public ModelForward call, host buffers, every step ----
+    seq2 = model.new_sequence()
+    logits = np.empty(cfg["vocab_size"], dtype=np.float32)
+    tok = int(np.argmax(seq2.forward(prompt, 0, out=logits)))
+    pos2 = PROMPT_LEN
+    for _ in range(max(args.warmup, 3)):
+        tok = seq2.forward_greedy([tok], pos2, logits_out=logits)
+        pos2 += 1
+    if world > 1:
+        torch.distributed.barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        tok = seq2.forward_greedy([tok], pos2, logits_out=logits)
+        pos2 += 1
+    e2e_elapsed = time.perf_counter() - t0
+    if world > 1:
+        t = torch.tensor([e2e_elapsed], device="cuda", dtype=torch.float64)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        e2e_elapsed = float(t.item())
+    e2e = {"value": world * args.steps / e2e_elapsed, "unit": "tok/s",
+           "h2d_bytes_per_step": 4, "d2h_bytes_per_step": cfg["vocab_size"] * 4 + 4,
+           "ms_per_step": 1e3 * e2e_elapsed / args.steps,
+           "api": "cheetah_cuda_forward_ex (host token in, host logits + greedy id out)"}
+    del seq2
+
+    # Algorithmic bytes per decode token at the mean context of the timed run.
+    info = model.info()
+    mean_ctx = pos + args.steps / 2
+    kv_bytes_per_pos = cfg["num_layers"] * cfg["kv_heads"] * cfg["head_dim"] * 2 * 2
+    weight_bytes = info["weight_bytes"]
+    step_bytes = weight_bytes + kv_bytes_per_pos * mean_ctx
+    step_gbs = step_bytes / (elapsed / args.steps * world) / 1e9 if world == 1 else \
+        step_bytes / (elapsed / args.steps) / 1e9
+
+    line = {
+        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded random-init bf16 N(0,0.02) weights in the cheetah-init layout; "
+                "uniform-random prompt ids)",
+        "config": {"workload": "qwen2-0.5b decode B=1 (config 1: 512-token prompt, greedy decode)",
+                   "model": "Qwen2-0.5B architecture", "global_batch": world, "seq_len": PROMPT_LEN,
+                   "parallelism": f"sequence-sharded replicas x{world}" if world > 1 else "single GPU",
+                   "kv_cache": "paged bf16, 64-token pages", "l2": "inputs larger than L2 "
+                   f"(weights {weight_bytes / 1e6:.0f} MB per step > 126 MB L2)"},
+        "e2e": e2e,
+        "gpu_launches": args.steps * (2 + 5 * cfg["num_layers"]),
+        "clocks": clock_info,
+        "step_roofline": {"bytes_per_token": step_bytes, "achieved_GBps": step_gbs,
+                          "frac_measured": step_gbs / hbm_peak, "frac_8TBps": step_gbs / 8000.0},
+    }
+
+    if rank == 0:
+        line["roofline"] = gemv_roofline(torch, R, hbm_peak)
+        line["roofline"]["peak_kind"] = peak_kind
+        if not args.no_attention:
+            line["attention"] = attention_microbench(torch, R, hbm_peak, quick=args.quick_attention)
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(model_dir, cfg, args.cpu_steps)
+        print(json.dumps(line), flush=True)
+    del seq
+    model.close()
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=128)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-steps", type=int, default=32)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-attention", action="store_true")
+    ap.add_argument("--quick-attention", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

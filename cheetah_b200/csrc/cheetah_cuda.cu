@@ -1,0 +1,1112 @@
+// libcheetah_cuda: the C-ABI backend (include/cheetah_cuda.h).
+//
+// Model: every unit of a prepared directory HBM-resident (QKV rows fused into
+// one [q+2kv, hidden] matrix, norms/biases widened to f32), a rotary table
+// built with the reference's own float math (`ops.rs:693-715`: powf, then
+// position*freq, sinf/cosf) and a paged KV pool shared by all sequences.
+// Sequence: page table + activations + one captured CUDA graph per sequence
+// for the decode step (embed -> 24 x [qkv, attention, o_proj, gate/up, down]
+// -> lm_head), launched with programmatic dependent launch so each kernel's
+// weight stream starts while its predecessor drains.
+#include <cuda_runtime.h>
+#include <math.h>
+#include <string.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstdlib>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "cheetah_cuda.h"
+#include "attention.cuh"
+#include "common.cuh"
+#include "gemv.cuh"
+#include "kernels_misc.cuh"
+#include "store.h"
+
+namespace cheetah {
+
+namespace {
+thread_local std::string g_last_error;
+}
+void set_error(const std::string &message) { g_last_error = message; }
+const char *last_error() { return g_last_error.c_str(); }
+
+namespace {
+
+bool env_flag(const char *name, bool fallback) {
+    const char *v = std::getenv(name);
+    if (v == nullptr || v[0] == '\0') return fallback;
+    return !(v[0] == '0' || v[0] == 'n' || v[0] == 'N' || v[0] == 'f' || v[0] == 'F');
+}
+
+int sm_count(int device) {
+    int count = 0;
+    cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, device);
+    return count > 0 ? count : 148;
+}
+
+template <typename Kernel, typename... Args>
+cudaError_t launch_ex(Kernel kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                      bool pdl, Args... args) {
+    cudaLaunchConfig_t config = {};
+    config.gridDim = grid;
+    config.blockDim = block;
+    config.dynamicSmemBytes = smem;
+    config.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    config.attrs = attr;
+    config.numAttrs = 1;
+    return cudaLaunchKernelEx(&config, kernel, args...);
+}
+
+int pick_ksplit(int cols) {
+    const int nvec = cols / 8;
+    if (nvec <= 160) return 1;
+    if (nvec <= 320) return 2;
+    if (nvec <= 640) return 4;
+    return 8;
+}
+
+template <int NB, int EPI, int KS>
+int launch_gemv_ks(const GemvParams &p, cudaStream_t stream, bool pdl, int sms) {
+    auto kernel = gemv_bf16_kernel<NB, EPI, KS>;
+    const size_t smem = (size_t)NB * p.cols * sizeof(float) + (size_t)kGemvWarps * 2 * NB * sizeof(float);
+    if (smem > 48 * 1024) {
+        CH_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    }
+    int per_sm = 0;
+    CH_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kGemvThreads, smem));
+    per_sm = std::max(1, std::min(per_sm, 4));
+    const int groups_per_cta = kGemvWarps / KS;
+    int groups;
+    if (EPI == kEpiQkv) groups = p.rows / 2;
+    else if (EPI == kEpiSwiglu) groups = p.rows;
+    else groups = (p.rows + 1) / 2;
+    const int needed = (groups + groups_per_cta - 1) / groups_per_cta;
+    const int grid = std::max(1, std::min(needed, sms * per_sm));
+    CH_CUDA_TRY(launch_ex(kernel, dim3(grid), dim3(kGemvThreads), smem, stream, pdl, p));
+    return 0;
+}
+
+template <int NB, int EPI>
+int launch_gemv(const GemvParams &p, cudaStream_t stream, bool pdl, int sms) {
+    switch (pick_ksplit(p.cols)) {
+    case 1: return launch_gemv_ks<NB, EPI, 1>(p, stream, pdl, sms);
+    case 2: return launch_gemv_ks<NB, EPI, 2>(p, stream, pdl, sms);
+    case 4: return launch_gemv_ks<NB, EPI, 4>(p, stream, pdl, sms);
+    default: return launch_gemv_ks<NB, EPI, 8>(p, stream, pdl, sms);
+    }
+}
+
+int launch_attention(const AttnParams &p, int head_dim, bool kv_f32, cudaStream_t stream, bool pdl) {
+    dim3 grid(p.splits, p.kv_heads, p.batch);
+    cudaError_t err;
+    if (head_dim == 64) {
+        err = kv_f32 ? launch_ex(decode_attention_kernel<64, true>, grid, dim3(kAttnThreads), 0, stream, pdl, p)
+                     : launch_ex(decode_attention_kernel<64, false>, grid, dim3(kAttnThreads), 0, stream, pdl, p);
+    } else {
+        err = kv_f32 ? launch_ex(decode_attention_kernel<128, true>, grid, dim3(kAttnThreads), 0, stream, pdl, p)
+                     : launch_ex(decode_attention_kernel<128, false>, grid, dim3(kAttnThreads), 0, stream, pdl, p);
+    }
+    CH_CUDA_TRY(err);
+    return 0;
+}
+
+int attention_splits(int batch, int kv_heads, int max_len, int sms) {
+    const int target = std::max(1, (2 * sms) / std::max(1, batch * kv_heads));
+    const int by_len = std::max(1, (max_len + kWarp - 1) / kWarp);
+    return std::max(1, std::min(std::min(target, by_len), 512));
+}
+
+struct LayerWeights {
+    const uint16_t *wqkv = nullptr;
+    const uint16_t *wo = nullptr;
+    const uint16_t *wgate = nullptr;
+    const uint16_t *wup = nullptr;
+    const uint16_t *wdown = nullptr;
+    const float *ln1 = nullptr;
+    const float *ln2 = nullptr;
+    const float *bqkv = nullptr;
+    const float *bo = nullptr;
+};
+
+}  // namespace
+
+struct Model {
+    CheetahCudaConfig cfg{};
+    int device = 0;
+    int quant = 0;
+    int sms = 148;
+    bool pdl = true;
+    uint8_t *arena = nullptr;
+    size_t arena_bytes = 0;
+    size_t arena_used = 0;
+    std::vector<LayerWeights> layers;
+    const uint16_t *embed = nullptr;
+    const uint16_t *lm_head = nullptr;
+    const float *final_norm = nullptr;
+    float *rope_cos = nullptr;
+    float *rope_sin = nullptr;
+    uint8_t *k_pool = nullptr;
+    uint8_t *v_pool = nullptr;
+    long long page_bytes = 0;
+    long long layer_stride_bytes = 0;
+    int num_pages = 0;
+    int page_tokens = 64;
+    int kv_f32 = 0;
+    std::mutex pool_mutex;
+    std::vector<int> free_pages;
+    std::atomic<int> refs{1};
+
+    void *take(size_t bytes) {
+        size_t offset = (arena_used + 255) & ~size_t(255);
+        if (offset + bytes > arena_bytes) return nullptr;
+        arena_used = offset + bytes;
+        return arena + offset;
+    }
+
+    int alloc_page() {
+        std::lock_guard<std::mutex> lock(pool_mutex);
+        if (free_pages.empty()) return -1;
+        int page = free_pages.back();
+        free_pages.pop_back();
+        return page;
+    }
+
+    void release_pages(std::vector<int> &pages) {
+        std::lock_guard<std::mutex> lock(pool_mutex);
+        for (int page : pages) free_pages.push_back(page);
+        pages.clear();
+    }
+
+    ~Model() {
+        cudaSetDevice(device);
+        cudaFree(arena);
+        cudaFree(rope_cos);
+        cudaFree(rope_sin);
+        cudaFree(k_pool);
+        cudaFree(v_pool);
+    }
+};
+
+void model_unref(Model *m) {
+    if (m != nullptr && m->refs.fetch_sub(1) == 1) delete m;
+}
+
+struct Seq {
+    Model *m = nullptr;
+    cudaStream_t stream = nullptr;
+    std::vector<int> pages;
+    size_t positions = 0;
+    int max_pages = 0;
+    int32_t *page_table = nullptr;
+    float *hidden = nullptr, *q = nullptr, *attn_out = nullptr, *act = nullptr, *logits = nullptr;
+    unsigned long long *argmax = nullptr;
+    StepState *d_step = nullptr;
+    StepState *h_step = nullptr;
+    float *h_logits = nullptr;
+    unsigned long long *h_argmax = nullptr;
+    float *part_o = nullptr, *part_ml = nullptr;
+    unsigned int *tickets = nullptr;
+    int *d_error = nullptr;
+    int splits = 1;
+    int32_t *token_log = nullptr;
+    cudaGraphExec_t graph = nullptr;
+    cudaGraphExec_t chain_graph = nullptr;
+
+    ~Seq() {
+        cudaSetDevice(m->device);
+        if (stream) cudaStreamSynchronize(stream);
+        if (graph) cudaGraphExecDestroy(graph);
+        if (chain_graph) cudaGraphExecDestroy(chain_graph);
+        cudaFree(token_log);
+        if (stream) cudaStreamDestroy(stream);
+        cudaFree(page_table);
+        cudaFree(hidden);
+        cudaFree(q);
+        cudaFree(attn_out);
+        cudaFree(act);
+        cudaFree(logits);
+        cudaFree(argmax);
+        cudaFree(d_step);
+        cudaFree(part_o);
+        cudaFree(part_ml);
+        cudaFree(tickets);
+        cudaFree(d_error);
+        cudaFreeHost(h_step);
+        cudaFreeHost(h_logits);
+        cudaFreeHost(h_argmax);
+        m->release_pages(pages);
+        model_unref(m);
+    }
+};
+
+struct Snapshot {
+    Model *m = nullptr;
+    std::vector<int> pages;
+    size_t positions = 0;
+    ~Snapshot() {
+        m->release_pages(pages);
+        model_unref(m);
+    }
+};
+
+namespace {
+
+// Enqueue one decode step (B = 1) on the sequence stream.
+int enqueue_decode_step(Seq &s, bool chain) {
+    Model &m = *s.m;
+    const CheetahCudaConfig &c = m.cfg;
+    const int hidden = c.hidden_size, inter = c.intermediate_size;
+    const int q_dim = c.q_heads * c.head_dim, kv_dim = c.kv_heads * c.head_dim;
+    const bool pdl = m.pdl;
+    cudaStream_t st = s.stream;
+
+    CH_CUDA_TRY(launch_ex(embed_kernel, dim3(1), dim3(256), 0, st, pdl, m.embed, hidden, s.d_step,
+                          s.hidden, s.argmax, s.page_table, chain ? 1 : 0, s.token_log));
+    const int32_t *positions = &s.d_step->position;
+    const int32_t *seq_lens = &s.d_step->seq_len;
+
+    for (uint32_t layer = 0; layer < c.num_layers; ++layer) {
+        const LayerWeights &w = m.layers[layer];
+        uint8_t *k_layer = m.k_pool + layer * m.layer_stride_bytes;
+        uint8_t *v_layer = m.v_pool + layer * m.layer_stride_bytes;
+
+        GemvParams qkv = {};
+        qkv.w0 = w.wqkv;
+        qkv.rows = q_dim + 2 * kv_dim;
+        qkv.cols = hidden;
+        qkv.batch = 1;
+        qkv.x = s.hidden;
+        qkv.x_stride = hidden;
+        qkv.norm_w = w.ln1;
+        qkv.eps = c.rms_eps;
+        qkv.bias = w.bqkv;
+        qkv.y = s.q;
+        qkv.y_stride = q_dim;
+        qkv.q_heads = c.q_heads;
+        qkv.kv_heads = c.kv_heads;
+        qkv.head_dim = c.head_dim;
+        qkv.rope_cos = m.rope_cos;
+        qkv.rope_sin = m.rope_sin;
+        qkv.positions = positions;
+        qkv.page_table = s.page_table;
+        qkv.max_pages = s.max_pages;
+        qkv.num_pages = m.num_pages;
+        qkv.page_tokens = m.page_tokens;
+        qkv.k_cache = k_layer;
+        qkv.v_cache = v_layer;
+        qkv.kv_f32 = m.kv_f32;
+        if (launch_gemv<1, kEpiQkv>(qkv, st, pdl, m.sms) != 0) return -1;
+
+        AttnParams at = {};
+        at.q = s.q;
+        at.k_pool = k_layer;
+        at.v_pool = v_layer;
+        at.page_table = s.page_table;
+        at.seq_lens = seq_lens;
+        at.max_pages = s.max_pages;
+        at.num_pages = m.num_pages;
+        at.page_tokens = m.page_tokens;
+        at.batch = 1;
+        at.q_heads = c.q_heads;
+        at.kv_heads = c.kv_heads;
+        at.window = c.sliding_window;
+        at.splits = s.splits;
+        at.scale = 1.0f / sqrtf((float)c.head_dim);
+        at.out = s.attn_out;
+        at.part_o = s.part_o;
+        at.part_ml = s.part_ml;
+        at.tickets = s.tickets;
+        at.error = s.d_error;
+        if (launch_attention(at, c.head_dim, m.kv_f32 != 0, st, pdl) != 0) return -1;
+
+        GemvParams o = {};
+        o.w0 = w.wo;
+        o.rows = hidden;
+        o.cols = q_dim;
+        o.batch = 1;
+        o.x = s.attn_out;
+        o.x_stride = q_dim;
+        o.bias = w.bo;
+        o.y = s.hidden;
+        o.y_stride = hidden;
+        if (launch_gemv<1, kEpiResidual>(o, st, pdl, m.sms) != 0) return -1;
+
+        GemvParams gu = {};
+        gu.w0 = w.wgate;
+        gu.w1 = w.wup;
+        gu.rows = inter;
+        gu.cols = hidden;
+        gu.batch = 1;
+        gu.x = s.hidden;
+        gu.x_stride = hidden;
+        gu.norm_w = w.ln2;
+        gu.eps = c.rms_eps;
+        gu.y = s.act;
+        gu.y_stride = inter;
+        if (launch_gemv<1, kEpiSwiglu>(gu, st, pdl, m.sms) != 0) return -1;
+
+        GemvParams dn = {};
+        dn.w0 = w.wdown;
+        dn.rows = hidden;
+        dn.cols = inter;
+        dn.batch = 1;
+        dn.x = s.act;
+        dn.x_stride = inter;
+        dn.y = s.hidden;
+        dn.y_stride = hidden;
+        if (launch_gemv<1, kEpiResidual>(dn, st, pdl, m.sms) != 0) return -1;
+    }
+
+    GemvParams lm = {};
+    lm.w0 = m.lm_head;
+    lm.rows = c.vocab_size;
+    lm.cols = hidden;
+    lm.batch = 1;
+    lm.x = s.hidden;
+    lm.x_stride = hidden;
+    lm.norm_w = m.final_norm;
+    lm.eps = c.rms_eps;
+    lm.y = s.logits;
+    lm.y_stride = c.vocab_size;
+    lm.argmax = s.argmax;
+    return launch_gemv<1, kEpiLogits>(lm, st, pdl, m.sms);
+}
+
+// chain = false: per-token graph (step state copied from pinned host memory).
+// chain = true: greedy-chain graph (step state advanced on the device).
+int build_decode_graph(Seq &s, bool chain, cudaGraphExec_t *exec) {
+    cudaGraph_t graph = nullptr;
+    CH_CUDA_TRY(cudaStreamBeginCapture(s.stream, cudaStreamCaptureModeThreadLocal));
+    cudaError_t copy = chain ? cudaSuccess
+                             : cudaMemcpyAsync(s.d_step, s.h_step, sizeof(StepState), cudaMemcpyHostToDevice, s.stream);
+    int rc = copy == cudaSuccess ? enqueue_decode_step(s, chain) : -1;
+    cudaError_t end = cudaStreamEndCapture(s.stream, &graph);
+    if (copy != cudaSuccess) {
+        set_error(std::string("step state copy failed: ") + cudaGetErrorString(copy));
+        rc = -1;
+    }
+    if (rc != 0 || end != cudaSuccess) {
+        if (graph) cudaGraphDestroy(graph);
+        if (rc == 0) set_error(std::string("graph capture failed: ") + cudaGetErrorString(end));
+        return -1;
+    }
+    cudaError_t inst = cudaGraphInstantiate(exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (inst != cudaSuccess) {
+        set_error(std::string("graph instantiate failed: ") + cudaGetErrorString(inst));
+        *exec = nullptr;
+        return -1;
+    }
+    return 0;
+}
+
+// Make sure the page holding `position` exists; fills the step's page fields.
+int ensure_page(Seq &s, size_t position) {
+    const size_t index = position / s.m->page_tokens;
+    s.h_step->page_index = -1;
+    s.h_step->page_id = -1;
+    if (index < s.pages.size()) return 0;
+    if ((int)index >= s.max_pages) {
+        set_error("CUDA backend: position " + std::to_string(position) +
+                  " exceeds the sequence capacity " + std::to_string(s.m->cfg.max_positions) + ".");
+        return -1;
+    }
+    const int page = s.m->alloc_page();
+    if (page < 0) {
+        set_error("CUDA backend: KV page pool exhausted (raise kv_pool_tokens).");
+        return -1;
+    }
+    s.pages.push_back(page);
+    s.h_step->page_index = (int32_t)index;
+    s.h_step->page_id = page;
+    return 0;
+}
+
+int run_decode_step(Seq &s, uint32_t token, size_t position) {
+    if (ensure_page(s, position) != 0) return -1;
+    s.h_step->token = (int32_t)token;
+    s.h_step->position = (int32_t)position;
+    s.h_step->seq_len = (int32_t)(position + 1);
+    if (s.graph == nullptr) {
+        if (env_flag("CHEETAH_CUDA_GRAPH", true)) {
+            if (build_decode_graph(s, false, &s.graph) != 0) return -1;
+        }
+    }
+    if (s.graph != nullptr) {
+        CH_CUDA_TRY(cudaGraphLaunch(s.graph, s.stream));
+    } else {
+        CH_CUDA_TRY(cudaMemcpyAsync(s.d_step, s.h_step, sizeof(StepState), cudaMemcpyHostToDevice, s.stream));
+        if (enqueue_decode_step(s, false) != 0) return -1;
+    }
+    s.positions = position + 1;
+    return 0;
+}
+
+// Host rotary table with the reference's float arithmetic (`ops.rs:693-715`).
+void build_rope_table(int max_positions, int head_dim, float theta, std::vector<float> &cos_t,
+                      std::vector<float> &sin_t) {
+    const int half = head_dim / 2;
+    std::vector<float> freq(half);
+    for (int i = 0; i < half; ++i) {
+        const float exponent = (-2.0f * (float)i) / (float)head_dim;
+        freq[i] = powf(theta, exponent);
+    }
+    cos_t.resize((size_t)max_positions * half);
+    sin_t.resize((size_t)max_positions * half);
+    for (int pos = 0; pos < max_positions; ++pos) {
+        for (int i = 0; i < half; ++i) {
+            const volatile float angle = (float)pos * freq[i];
+            cos_t[(size_t)pos * half + i] = cosf(angle);
+            sin_t[(size_t)pos * half + i] = sinf(angle);
+        }
+    }
+}
+
+float bf16_bits_to_float(uint16_t bits) {
+    uint32_t w = (uint32_t)bits << 16;
+    float f;
+    memcpy(&f, &w, 4);
+    return f;
+}
+
+int open_model(const char *prepared_dir, const CheetahCudaConfig *config, const char *quant,
+               int device, Model **out) {
+    CH_REQUIRE(prepared_dir != nullptr && config != nullptr && out != nullptr,
+               "cheetah_cuda_model_open: null argument");
+    const std::string q = quant ? quant : "bf16";
+    CH_REQUIRE(q == "bf16", "CUDA backend: quantisation '" + q + "' is not available in this build yet.");
+    CheetahCudaConfig c = *config;
+    if (c.rotary_dim == 0) c.rotary_dim = c.head_dim;
+    if (c.kv_page_tokens == 0) {
+        const char *env = std::getenv("CHEETAH_CUDA_KV_PAGE");
+        c.kv_page_tokens = env ? (uint32_t)std::atoi(env) : 64;
+    }
+    if (c.max_positions == 0) c.max_positions = 32768;
+    CH_REQUIRE(c.head_dim == 64 || c.head_dim == 128, "CUDA backend: head_dim must be 64 or 128.");
+    CH_REQUIRE(c.rotary_dim == c.head_dim, "CUDA backend: partial rotary is not supported.");
+    CH_REQUIRE(c.kv_heads > 0 && c.q_heads % c.kv_heads == 0 && c.q_heads / c.kv_heads <= kMaxGroup,
+               "CUDA backend: q_heads must be a multiple of kv_heads with at most 8 per group.");
+    CH_REQUIRE(c.hidden_size % 8 == 0 && c.intermediate_size % 8 == 0 && (c.q_heads * c.head_dim) % 8 == 0,
+               "CUDA backend: hidden/intermediate/q widths must be multiples of 8.");
+    CH_REQUIRE(c.kv_page_tokens >= 16 && c.kv_page_tokens % 16 == 0,
+               "CUDA backend: kv_page_tokens must be a positive multiple of 16.");
+    CH_REQUIRE(c.kv_dtype == CHEETAH_CUDA_KV_BF16 || c.kv_dtype == CHEETAH_CUDA_KV_F32,
+               "CUDA backend: unknown kv_dtype.");
+    int count = 0;
+    CH_CUDA_TRY(cudaGetDeviceCount(&count));
+    CH_REQUIRE(device >= 0 && device < count, "CUDA backend: no such device " + std::to_string(device));
+    CH_CUDA_TRY(cudaSetDevice(device));
+
+    PreparedStore store;
+    std::string error;
+    if (!store.open(prepared_dir, &error)) {
+        set_error(error);
+        return -1;
+    }
+
+    Model *m = new Model();
+    m->cfg = c;
+    m->device = device;
+    m->sms = sm_count(device);
+    m->pdl = env_flag("CHEETAH_CUDA_PDL", true);
+    m->page_tokens = (int)c.kv_page_tokens;
+    m->kv_f32 = c.kv_dtype == CHEETAH_CUDA_KV_F32;
+
+    const size_t H = c.hidden_size, I = c.intermediate_size, V = c.vocab_size;
+    const size_t QD = (size_t)c.q_heads * c.head_dim, KD = (size_t)c.kv_heads * c.head_dim;
+    auto fail = [&](const std::string &msg) {
+        set_error(msg);
+        delete m;
+        return -1;
+    };
+    auto check_unit = [&](const std::string &id, std::vector<uint64_t> shape, const uint8_t **bytes) -> bool {
+        const UnitRecord *rec = store.record(id);
+        if (rec == nullptr) {
+            error = "Native backend: unknown unit '" + id + "'.";
+            return false;
+        }
+        if (rec->dtype != "BF16" && rec->dtype != "bf16") {
+            error = "CUDA backend: unit '" + id + "' is " + rec->dtype + "; bf16 weights are required.";
+            return false;
+        }
+        if (rec->shape != shape) {
+            error = "CUDA backend: unit '" + id + "' has an unexpected shape.";
+            return false;
+        }
+        *bytes = store.slice(id, &error);
+        return *bytes != nullptr;
+    };
+
+    // Size the arena: bf16 matrices + f32 norms/biases.
+    const bool tied = c.tie_word_embeddings != 0;
+    size_t total = V * H * 2 + (tied ? 0 : V * H * 2) + H * 4 + 4096;
+    const size_t per_layer = ((QD + 2 * KD) * H + H * QD + 2 * I * H + H * I) * 2 +
+                             (2 * H + (QD + 2 * KD) + H) * 4 + 8 * 256;
+    total += per_layer * c.num_layers;
+    cudaError_t err = cudaMalloc(&m->arena, total);
+    if (err != cudaSuccess) return fail(std::string("CUDA backend: weight allocation failed: ") + cudaGetErrorString(err));
+    m->arena_bytes = total;
+
+    auto upload = [&](void *dst, const void *src, size_t bytes) -> bool {
+        cudaError_t e = cudaMemcpy(dst, src, bytes, cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) {
+            error = std::string("CUDA backend: weight upload failed: ") + cudaGetErrorString(e);
+            return false;
+        }
+        return true;
+    };
+    auto upload_f32_from_bf16 = [&](float *dst, const uint8_t *src, size_t n) -> bool {
+        std::vector<float> tmp(n);
+        for (size_t i = 0; i < n; ++i) {
+            uint16_t bits;
+            memcpy(&bits, src + 2 * i, 2);
+            tmp[i] = bf16_bits_to_float(bits);
+        }
+        return upload(dst, tmp.data(), n * 4);
+    };
+
+    const uint8_t *bytes = nullptr;
+    if (!check_unit("model.embed_tokens.weight", {V, H}, &bytes)) return fail(error);
+    uint16_t *embed = (uint16_t *)m->take(V * H * 2);
+    if (!upload(embed, bytes, V * H * 2)) return fail(error);
+    m->embed = embed;
+    if (tied) {
+        m->lm_head = embed;
+    } else {
+        if (!check_unit("lm_head.weight", {V, H}, &bytes)) {
+            return fail("Native backend: neither tied embeddings nor a separate 'lm_head.weight' tensor are present.");
+        }
+        uint16_t *head = (uint16_t *)m->take(V * H * 2);
+        if (!upload(head, bytes, V * H * 2)) return fail(error);
+        m->lm_head = head;
+    }
+    if (!check_unit("model.norm.weight", {H}, &bytes)) return fail(error);
+    float *fn = (float *)m->take(H * 4);
+    if (!upload_f32_from_bf16(fn, bytes, H)) return fail(error);
+    m->final_norm = fn;
+
+    m->layers.resize(c.num_layers);
+    for (uint32_t layer = 0; layer < c.num_layers; ++layer) {
+        const std::string p = "model.layers." + std::to_string(layer) + ".";
+        LayerWeights &w = m->layers[layer];
+        uint16_t *wqkv = (uint16_t *)m->take((QD + 2 * KD) * H * 2);
+        if (!check_unit(p + "self_attn.q_proj.weight", {QD, H}, &bytes) || !upload(wqkv, bytes, QD * H * 2)) return fail(error);
+        if (!check_unit(p + "self_attn.k_proj.weight", {KD, H}, &bytes) || !upload(wqkv + QD * H, bytes, KD * H * 2)) return fail(error);
+        if (!check_unit(p + "self_attn.v_proj.weight", {KD, H}, &bytes) || !upload(wqkv + (QD + KD) * H, bytes, KD * H * 2)) return fail(error);
+        w.wqkv = wqkv;
+        uint16_t *wo = (uint16_t *)m->take(H * QD * 2);
+        if (!check_unit(p + "self_attn.o_proj.weight", {H, QD}, &bytes) || !upload(wo, bytes, H * QD * 2)) return fail(error);
+        w.wo = wo;
+        uint16_t *wg = (uint16_t *)m->take(I * H * 2);
+        if (!check_unit(p + "mlp.gate_proj.weight", {I, H}, &bytes) || !upload(wg, bytes, I * H * 2)) return fail(error);
+        w.wgate = wg;
+        uint16_t *wu = (uint16_t *)m->take(I * H * 2);
+        if (!check_unit(p + "mlp.up_proj.weight", {I, H}, &bytes) || !upload(wu, bytes, I * H * 2)) return fail(error);
+        w.wup = wu;
+        uint16_t *wd = (uint16_t *)m->take(H * I * 2);
+        if (!check_unit(p + "mlp.down_proj.weight", {H, I}, &bytes) || !upload(wd, bytes, H * I * 2)) return fail(error);
+        w.wdown = wd;
+        float *ln1 = (float *)m->take(H * 4);
+        if (!check_unit(p + "input_layernorm.weight", {H}, &bytes) || !upload_f32_from_bf16(ln1, bytes, H)) return fail(error);
+        w.ln1 = ln1;
+        float *ln2 = (float *)m->take(H * 4);
+        if (!check_unit(p + "post_attention_layernorm.weight", {H}, &bytes) || !upload_f32_from_bf16(ln2, bytes, H)) return fail(error);
+        w.ln2 = ln2;
+        // Biases are unit-optional (`ops.rs:1156-1166`); absent ones add zero.
+        const bool has_qkv_bias = store.contains(p + "self_attn.q_proj.bias") ||
+                                  store.contains(p + "self_attn.k_proj.bias") ||
+                                  store.contains(p + "self_attn.v_proj.bias");
+        if (has_qkv_bias) {
+            std::vector<float> b(QD + 2 * KD, 0.0f);
+            const char *names[3] = {"self_attn.q_proj.bias", "self_attn.k_proj.bias", "self_attn.v_proj.bias"};
+            const size_t offs[3] = {0, QD, QD + KD};
+            const size_t lens[3] = {QD, KD, KD};
+            for (int k = 0; k < 3; ++k) {
+                if (!store.contains(p + names[k])) continue;
+                if (!check_unit(p + names[k], {lens[k]}, &bytes)) return fail(error);
+                for (size_t i = 0; i < lens[k]; ++i) {
+                    uint16_t bits;
+                    memcpy(&bits, bytes + 2 * i, 2);
+                    b[offs[k] + i] = bf16_bits_to_float(bits);
+                }
+            }
+            float *bq = (float *)m->take(b.size() * 4);
+            if (!upload(bq, b.data(), b.size() * 4)) return fail(error);
+            w.bqkv = bq;
+        }
+        if (store.contains(p + "self_attn.o_proj.bias")) {
+            if (!check_unit(p + "self_attn.o_proj.bias", {H}, &bytes)) return fail(error);
+            float *bo = (float *)m->take(H * 4);
+            if (!upload_f32_from_bf16(bo, bytes, H)) return fail(error);
+            w.bo = bo;
+        }
+    }
+
+    // Rotary table.
+    std::vector<float> cos_t, sin_t;
+    build_rope_table((int)c.max_positions, (int)c.head_dim, c.rope_theta, cos_t, sin_t);
+    if (cudaMalloc(&m->rope_cos, cos_t.size() * 4) != cudaSuccess ||
+        cudaMalloc(&m->rope_sin, sin_t.size() * 4) != cudaSuccess ||
+        !upload(m->rope_cos, cos_t.data(), cos_t.size() * 4) ||
+        !upload(m->rope_sin, sin_t.data(), sin_t.size() * 4)) {
+        return fail(error.empty() ? "CUDA backend: rotary table allocation failed" : error);
+    }
+
+    // KV pool.
+    uint32_t pool_tokens = c.kv_pool_tokens ? c.kv_pool_tokens : std::max<uint32_t>(c.max_positions, 65536);
+    m->num_pages = (int)((pool_tokens + m->page_tokens - 1) / m->page_tokens);
+    const size_t elem = m->kv_f32 ? 4 : 2;
+    m->page_bytes = (long long)c.kv_heads * m->page_tokens * c.head_dim * elem;
+    m->layer_stride_bytes = m->page_bytes * m->num_pages;
+    const size_t pool_bytes = (size_t)m->layer_stride_bytes * c.num_layers;
+    if (cudaMalloc(&m->k_pool, pool_bytes) != cudaSuccess || cudaMalloc(&m->v_pool, pool_bytes) != cudaSuccess) {
+        return fail("CUDA backend: KV pool allocation failed (" + std::to_string(pool_bytes * 2) + " bytes).");
+    }
+    cudaMemset(m->k_pool, 0, pool_bytes);
+    cudaMemset(m->v_pool, 0, pool_bytes);
+    m->free_pages.reserve(m->num_pages);
+    for (int i = m->num_pages - 1; i >= 0; --i) m->free_pages.push_back(i);
+    err = cudaDeviceSynchronize();
+    if (err != cudaSuccess) return fail(std::string("CUDA backend: ") + cudaGetErrorString(err));
+    *out = m;
+    return 0;
+}
+
+int new_seq(Model *m, Seq **out) {
+    CH_REQUIRE(m != nullptr && out != nullptr, "cheetah_cuda_seq_new: null argument");
+    CH_CUDA_TRY(cudaSetDevice(m->device));
+    const CheetahCudaConfig &c = m->cfg;
+    Seq *s = new Seq();
+    m->refs.fetch_add(1);
+    s->m = m;
+    s->max_pages = (int)((c.max_positions + m->page_tokens - 1) / m->page_tokens);
+    s->splits = attention_splits(1, c.kv_heads, c.max_positions, m->sms);
+    const size_t QD = (size_t)c.q_heads * c.head_dim;
+    bool ok = cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking) == cudaSuccess &&
+              cudaMalloc(&s->page_table, s->max_pages * sizeof(int32_t)) == cudaSuccess &&
+              cudaMalloc(&s->hidden, c.hidden_size * 4) == cudaSuccess &&
+              cudaMalloc(&s->q, QD * 4) == cudaSuccess &&
+              cudaMalloc(&s->attn_out, QD * 4) == cudaSuccess &&
+              cudaMalloc(&s->act, c.intermediate_size * 4) == cudaSuccess &&
+              cudaMalloc(&s->logits, (size_t)c.vocab_size * 4) == cudaSuccess &&
+              cudaMalloc(&s->argmax, 8) == cudaSuccess &&
+              cudaMalloc(&s->d_step, sizeof(StepState)) == cudaSuccess &&
+              cudaMalloc(&s->part_o, (size_t)c.kv_heads * s->splits * kMaxGroup * c.head_dim * 4) == cudaSuccess &&
+              cudaMalloc(&s->part_ml, (size_t)c.kv_heads * s->splits * kMaxGroup * 2 * 4) == cudaSuccess &&
+              cudaMalloc(&s->tickets, c.kv_heads * 4) == cudaSuccess &&
+              cudaMalloc(&s->d_error, 4) == cudaSuccess &&
+              cudaMalloc(&s->token_log, (size_t)c.max_positions * 4) == cudaSuccess &&
+              cudaMallocHost(&s->h_step, sizeof(StepState)) == cudaSuccess &&
+              cudaMallocHost(&s->h_logits, (size_t)c.vocab_size * 4) == cudaSuccess &&
+              cudaMallocHost(&s->h_argmax, 8) == cudaSuccess;
+    if (!ok) {
+        delete s;
+        set_error("CUDA backend: sequence allocation failed.");
+        return -1;
+    }
+    cudaMemset(s->page_table, 0xFF, s->max_pages * sizeof(int32_t));
+    cudaMemset(s->tickets, 0, c.kv_heads * 4);
+    cudaMemset(s->d_error, 0, 4);
+    cudaMemset(s->hidden, 0, c.hidden_size * 4);
+    memset(s->h_step, 0, sizeof(StepState));
+    cudaError_t err = cudaDeviceSynchronize();
+    if (err != cudaSuccess) {
+        delete s;
+        set_error(std::string("CUDA backend: ") + cudaGetErrorString(err));
+        return -1;
+    }
+    *out = s;
+    return 0;
+}
+
+int forward(Seq *s, const uint32_t *tokens, size_t n, size_t offset, float *logits_out,
+            uint32_t *argmax_out) {
+    CH_REQUIRE(s != nullptr, "cheetah_cuda_forward: null sequence");
+    const CheetahCudaConfig &c = s->m->cfg;
+    CH_REQUIRE(n > 0 && tokens != nullptr, "Native backend: empty token input.");
+    for (size_t i = 0; i < n; ++i) {
+        if (tokens[i] >= c.vocab_size) {
+            set_error("Native backend: token id " + std::to_string(tokens[i]) +
+                      " exceeds the vocabulary size " + std::to_string(c.vocab_size) + ".");
+            return -1;
+        }
+    }
+    CH_REQUIRE(offset == s->positions,
+               "CUDA backend: offset " + std::to_string(offset) + " does not match the " +
+                   std::to_string(s->positions) + " cached positions.");
+    CH_REQUIRE(offset + n <= c.max_positions,
+               "CUDA backend: position " + std::to_string(offset + n - 1) +
+                   " exceeds the sequence capacity " + std::to_string(c.max_positions) + ".");
+    CH_CUDA_TRY(cudaSetDevice(s->m->device));
+    for (size_t i = 0; i < n; ++i) {
+        if (run_decode_step(*s, tokens[i], offset + i) != 0) return -1;
+        if (i + 1 < n) CH_CUDA_TRY(cudaStreamSynchronize(s->stream));  // h_step is reused
+    }
+    if (logits_out) {
+        CH_CUDA_TRY(cudaMemcpyAsync(s->h_logits, s->logits, (size_t)c.vocab_size * 4,
+                                    cudaMemcpyDeviceToHost, s->stream));
+    }
+    if (argmax_out) {
+        CH_CUDA_TRY(cudaMemcpyAsync(s->h_argmax, s->argmax, 8, cudaMemcpyDeviceToHost, s->stream));
+    }
+    CH_CUDA_TRY(cudaStreamSynchronize(s->stream));
+    if (logits_out) memcpy(logits_out, s->h_logits, (size_t)c.vocab_size * 4);
+    if (argmax_out) *argmax_out = (uint32_t)(*s->h_argmax & 0xFFFFFFFFull);
+    return 0;
+}
+
+// Greedy decode entirely on the device: step i consumes the argmax of step
+// i-1 (step 0 consumes `first_token`) at position offset+i. Pages for the
+// whole run are allocated up front; nothing returns to the host between steps.
+int generate_greedy(Seq *s, uint32_t first_token, size_t offset, size_t steps, uint32_t *tokens_out) {
+    CH_REQUIRE(s != nullptr, "cheetah_cuda_generate_greedy: null sequence");
+    const CheetahCudaConfig &c = s->m->cfg;
+    CH_REQUIRE(steps > 0, "cheetah_cuda_generate_greedy: steps must be positive");
+    CH_REQUIRE(first_token < c.vocab_size,
+               "Native backend: token id " + std::to_string(first_token) + " exceeds the vocabulary size " +
+                   std::to_string(c.vocab_size) + ".");
+    CH_REQUIRE(offset == s->positions,
+               "CUDA backend: offset " + std::to_string(offset) + " does not match the " +
+                   std::to_string(s->positions) + " cached positions.");
+    CH_REQUIRE(offset + steps <= c.max_positions,
+               "CUDA backend: position " + std::to_string(offset + steps - 1) +
+                   " exceeds the sequence capacity " + std::to_string(c.max_positions) + ".");
+    CH_CUDA_TRY(cudaSetDevice(s->m->device));
+    CH_CUDA_TRY(cudaStreamSynchronize(s->stream));
+    // Pages for every position of the run.
+    const size_t first_page = s->pages.size();
+    const size_t last_page = (offset + steps - 1) / s->m->page_tokens;
+    for (size_t p = first_page; p <= last_page; ++p) {
+        const int page = s->m->alloc_page();
+        if (page < 0) {
+            set_error("CUDA backend: KV page pool exhausted (raise kv_pool_tokens).");
+            return -1;
+        }
+        s->pages.push_back(page);
+    }
+    if (last_page + 1 > first_page) {
+        std::vector<int32_t> ids(s->pages.begin() + first_page, s->pages.end());
+        CH_CUDA_TRY(cudaMemcpy(s->page_table + first_page, ids.data(), ids.size() * 4, cudaMemcpyHostToDevice));
+    }
+    if (s->chain_graph == nullptr && build_decode_graph(*s, true, &s->chain_graph) != 0) return -1;
+    StepState init = {};
+    init.token = (int32_t)first_token;
+    init.position = (int32_t)offset - 1;
+    init.seq_len = (int32_t)offset;
+    init.page_index = -1;
+    init.page_id = -1;
+    init.chain_index = 0;
+    const unsigned long long seed_key = (0xFFFFFFFFull << 32) | first_token;
+    *s->h_step = init;
+    *s->h_argmax = seed_key;
+    CH_CUDA_TRY(cudaMemcpyAsync(s->d_step, s->h_step, sizeof(StepState), cudaMemcpyHostToDevice, s->stream));
+    CH_CUDA_TRY(cudaMemcpyAsync(s->argmax, s->h_argmax, 8, cudaMemcpyHostToDevice, s->stream));
+    CH_CUDA_TRY(cudaStreamSynchronize(s->stream));
+    for (size_t i = 0; i < steps; ++i) CH_CUDA_TRY(cudaGraphLaunch(s->chain_graph, s->stream));
+    s->positions = offset + steps;
+    if (tokens_out == nullptr) return 0;  // asynchronous: caller synchronises the stream
+    std::vector<int32_t> log(steps);
+    CH_CUDA_TRY(cudaMemcpyAsync(log.data(), s->token_log, steps * 4, cudaMemcpyDeviceToHost, s->stream));
+    CH_CUDA_TRY(cudaMemcpyAsync(s->h_argmax, s->argmax, 8, cudaMemcpyDeviceToHost, s->stream));
+    CH_CUDA_TRY(cudaStreamSynchronize(s->stream));
+    for (size_t i = 0; i + 1 < steps; ++i) tokens_out[i] = (uint32_t)log[i + 1];
+    tokens_out[steps - 1] = (uint32_t)(*s->h_argmax & 0xFFFFFFFFull);
+    return 0;
+}
+
+}  // namespace
+}  // namespace cheetah
+
+using cheetah::Model;
+using cheetah::Seq;
+using cheetah::Snapshot;
+
+extern "C" {
+
+const char *cheetah_cuda_last_error(void) { return cheetah::last_error(); }
+int cheetah_cuda_abi_version(void) { return CHEETAH_CUDA_ABI_VERSION; }
+
+int cheetah_cuda_device_count(int *count) {
+    CH_REQUIRE(count != nullptr, "cheetah_cuda_device_count: null argument");
+    int n = 0;
+    cudaError_t err = cudaGetDeviceCount(&n);
+    if (err != cudaSuccess) n = 0;
+    *count = n;
+    return 0;
+}
+
+int cheetah_cuda_model_open(const char *prepared_dir, const CheetahCudaConfig *config, const char *quant,
+                            int device, CheetahCudaModel **out) {
+    Model *m = nullptr;
+    if (cheetah::open_model(prepared_dir, config, quant, device, &m) != 0) return -1;
+    *out = reinterpret_cast<CheetahCudaModel *>(m);
+    return 0;
+}
+
+int cheetah_cuda_model_free(CheetahCudaModel *model) {
+    if (model != nullptr) cheetah::model_unref(reinterpret_cast<Model *>(model));
+    return 0;
+}
+
+int cheetah_cuda_model_info(const CheetahCudaModel *model, CheetahCudaModelInfo *info) {
+    CH_REQUIRE(model != nullptr && info != nullptr, "cheetah_cuda_model_info: null argument");
+    Model *m = const_cast<Model *>(reinterpret_cast<const Model *>(model));
+    info->weight_bytes = m->arena_used;
+    info->kv_pool_bytes = (uint64_t)m->layer_stride_bytes * m->cfg.num_layers * 2;
+    info->kv_pages_total = (uint32_t)m->num_pages;
+    {
+        std::lock_guard<std::mutex> lock(m->pool_mutex);
+        info->kv_pages_free = (uint32_t)m->free_pages.size();
+    }
+    info->device = m->device;
+    info->quant = m->quant;
+    return 0;
+}
+
+int cheetah_cuda_seq_new(CheetahCudaModel *model, CheetahCudaSeq **out) {
+    Seq *s = nullptr;
+    if (cheetah::new_seq(reinterpret_cast<Model *>(model), &s) != 0) return -1;
+    *out = reinterpret_cast<CheetahCudaSeq *>(s);
+    return 0;
+}
+
+int cheetah_cuda_seq_free(CheetahCudaSeq *seq) {
+    delete reinterpret_cast<Seq *>(seq);
+    return 0;
+}
+
+int cheetah_cuda_seq_clear(CheetahCudaSeq *seq) {
+    CH_REQUIRE(seq != nullptr, "cheetah_cuda_seq_clear: null sequence");
+    Seq *s = reinterpret_cast<Seq *>(seq);
+    CH_CUDA_TRY(cudaSetDevice(s->m->device));
+    CH_CUDA_TRY(cudaStreamSynchronize(s->stream));
+    s->m->release_pages(s->pages);
+    s->positions = 0;
+    return 0;
+}
+
+int cheetah_cuda_seq_positions(const CheetahCudaSeq *seq, size_t *positions) {
+    CH_REQUIRE(seq != nullptr && positions != nullptr, "cheetah_cuda_seq_positions: null argument");
+    *positions = reinterpret_cast<const Seq *>(seq)->positions;
+    return 0;
+}
+
+int cheetah_cuda_forward(CheetahCudaSeq *seq, const uint32_t *tokens, size_t n, size_t offset,
+                         float *logits_out) {
+    return cheetah::forward(reinterpret_cast<Seq *>(seq), tokens, n, offset, logits_out, nullptr);
+}
+
+int cheetah_cuda_forward_ex(CheetahCudaSeq *seq, const uint32_t *tokens, size_t n, size_t offset,
+                            float *logits_out, uint32_t *argmax_out) {
+    return cheetah::forward(reinterpret_cast<Seq *>(seq), tokens, n, offset, logits_out, argmax_out);
+}
+
+int cheetah_cuda_generate_greedy(CheetahCudaSeq *seq, uint32_t first_token, size_t offset, size_t steps,
+                                 uint32_t *tokens_out) {
+    return cheetah::generate_greedy(reinterpret_cast<Seq *>(seq), first_token, offset, steps, tokens_out);
+}
+
+int cheetah_cuda_seq_stream(const CheetahCudaSeq *seq, void **stream) {
+    CH_REQUIRE(seq != nullptr && stream != nullptr, "cheetah_cuda_seq_stream: null argument");
+    *stream = reinterpret_cast<const Seq *>(seq)->stream;
+    return 0;
+}
+
+static int copy_pages(Model *m, const std::vector<int> &src, const std::vector<int> &dst, cudaStream_t stream) {
+    if (src.empty()) return 0;
+    int32_t *d_ids = nullptr;
+    CH_CUDA_TRY(cudaMalloc(&d_ids, src.size() * 2 * sizeof(int32_t)));
+    std::vector<int32_t> ids(src.begin(), src.end());
+    ids.insert(ids.end(), dst.begin(), dst.end());
+    cudaError_t err = cudaMemcpyAsync(d_ids, ids.data(), ids.size() * 4, cudaMemcpyHostToDevice, stream);
+    if (err == cudaSuccess) {
+        cheetah::copy_pages_kernel<<<4 * m->sms, 256, 0, stream>>>(
+            d_ids, d_ids + src.size(), (int)src.size(), m->k_pool, m->v_pool, m->layer_stride_bytes,
+            (int)m->cfg.num_layers, m->page_bytes);
+        err = cudaGetLastError();
+    }
+    if (err == cudaSuccess) err = cudaStreamSynchronize(stream);
+    cudaFree(d_ids);
+    CH_CUDA_TRY(err);
+    return 0;
+}
+
+int cheetah_cuda_seq_snapshot(const CheetahCudaSeq *seq, CheetahCudaSnapshot **out) {
+    CH_REQUIRE(seq != nullptr && out != nullptr, "cheetah_cuda_seq_snapshot: null argument");
+    Seq *s = const_cast<Seq *>(reinterpret_cast<const Seq *>(seq));
+    CH_CUDA_TRY(cudaSetDevice(s->m->device));
+    Snapshot *snap = new Snapshot();
+    snap->m = s->m;
+    s->m->refs.fetch_add(1);
+    snap->positions = s->positions;
+    for (size_t i = 0; i < s->pages.size(); ++i) {
+        int page = s->m->alloc_page();
+        if (page < 0) {
+            delete snap;
+            cheetah::set_error("CUDA backend: KV page pool exhausted while snapshotting.");
+            return -1;
+        }
+        snap->pages.push_back(page);
+    }
+    if (copy_pages(s->m, s->pages, snap->pages, s->stream) != 0) {
+        delete snap;
+        return -1;
+    }
+    *out = reinterpret_cast<CheetahCudaSnapshot *>(snap);
+    return 0;
+}
+
+int cheetah_cuda_snapshot_positions(const CheetahCudaSnapshot *snapshot, size_t *positions) {
+    CH_REQUIRE(snapshot != nullptr && positions != nullptr, "cheetah_cuda_snapshot_positions: null argument");
+    *positions = reinterpret_cast<const Snapshot *>(snapshot)->positions;
+    return 0;
+}
+
+int cheetah_cuda_seq_restore_prefix(CheetahCudaSeq *seq, const CheetahCudaSnapshot *snapshot, size_t positions) {
+    CH_REQUIRE(seq != nullptr && snapshot != nullptr, "cheetah_cuda_seq_restore_prefix: null argument");
+    Seq *s = reinterpret_cast<Seq *>(seq);
+    const Snapshot *snap = reinterpret_cast<const Snapshot *>(snapshot);
+    CH_REQUIRE(snap->m == s->m, "CUDA backend: snapshot belongs to another model.");
+    CH_CUDA_TRY(cudaSetDevice(s->m->device));
+    CH_CUDA_TRY(cudaStreamSynchronize(s->stream));
+    s->m->release_pages(s->pages);
+    s->positions = 0;
+    const size_t keep = std::min(positions, snap->positions);
+    const size_t pages = (keep + s->m->page_tokens - 1) / s->m->page_tokens;
+    std::vector<int> src(snap->pages.begin(), snap->pages.begin() + pages);
+    for (size_t i = 0; i < pages; ++i) {
+        int page = s->m->alloc_page();
+        if (page < 0) {
+            s->m->release_pages(s->pages);
+            cheetah::set_error("CUDA backend: KV page pool exhausted while restoring.");
+            return -1;
+        }
+        s->pages.push_back(page);
+    }
+    if (copy_pages(s->m, src, s->pages, s->stream) != 0) return -1;
+    std::vector<int32_t> table(s->pages.begin(), s->pages.end());
+    if (!table.empty()) {
+        CH_CUDA_TRY(cudaMemcpy(s->page_table, table.data(), table.size() * 4, cudaMemcpyHostToDevice));
+    }
+    s->positions = keep;
+    return 0;
+}
+
+int cheetah_cuda_snapshot_free(CheetahCudaSnapshot *snapshot) {
+    delete reinterpret_cast<Snapshot *>(snapshot);
+    return 0;
+}
+
+int cheetah_cuda_seq_export_kv(const CheetahCudaSeq *seq, size_t layer, float *k_out, float *v_out) {
+    CH_REQUIRE(seq != nullptr && k_out != nullptr && v_out != nullptr, "cheetah_cuda_seq_export_kv: null argument");
+    const Seq *s = reinterpret_cast<const Seq *>(seq);
+    const Model *m = s->m;
+    CH_REQUIRE(layer < m->cfg.num_layers, "cheetah_cuda_seq_export_kv: layer out of range");
+    CH_CUDA_TRY(cudaSetDevice(m->device));
+    CH_CUDA_TRY(cudaStreamSynchronize(s->stream));
+    const size_t n = s->positions * m->cfg.kv_heads * m->cfg.head_dim;
+    if (n == 0) return 0;
+    float *d_out = nullptr;
+    int32_t *d_pages = nullptr;
+    CH_CUDA_TRY(cudaMalloc(&d_out, n * 4));
+    cudaError_t err = cudaMalloc(&d_pages, s->pages.size() * 4);
+    std::vector<int32_t> pages(s->pages.begin(), s->pages.end());
+    if (err == cudaSuccess) err = cudaMemcpy(d_pages, pages.data(), pages.size() * 4, cudaMemcpyHostToDevice);
+    for (int which = 0; which < 2 && err == cudaSuccess; ++which) {
+        const uint8_t *pool = (which ? m->v_pool : m->k_pool) + layer * m->layer_stride_bytes;
+        cheetah::export_kv_kernel<<<256, 256, 0, s->stream>>>(pool, m->kv_f32, d_pages, (int)s->positions,
+                                                              (int)m->cfg.kv_heads, m->page_tokens,
+                                                              (int)m->cfg.head_dim, d_out);
+        err = cudaGetLastError();
+        if (err == cudaSuccess) err = cudaStreamSynchronize(s->stream);
+        if (err == cudaSuccess) err = cudaMemcpy(which ? v_out : k_out, d_out, n * 4, cudaMemcpyDeviceToHost);
+    }
+    cudaFree(d_out);
+    cudaFree(d_pages);
+    CH_CUDA_TRY(err);
+    return 0;
+}
+
+int cheetah_cuda_op_gemv_bf16(const void *weight, size_t rows, size_t cols, const float *x, size_t batch,
+                              float *y, void *stream) {
+    CH_REQUIRE(weight != nullptr && x != nullptr && y != nullptr, "cheetah_cuda_op_gemv_bf16: null argument");
+    CH_REQUIRE(cols % 8 == 0 && cols > 0 && rows > 0, "cheetah_cuda_op_gemv_bf16: cols must be a positive multiple of 8");
+    CH_REQUIRE(((uintptr_t)weight & 15) == 0 && ((uintptr_t)x & 15) == 0,
+               "cheetah_cuda_op_gemv_bf16: weight and x must be 16-byte aligned");
+    CH_REQUIRE(rows < (1u << 31) && cols < (1u << 24), "cheetah_cuda_op_gemv_bf16: shape too large");
+    int device = 0;
+    CH_CUDA_TRY(cudaGetDevice(&device));
+    const int sms = cheetah::sm_count(device);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    for (size_t b0 = 0; b0 < batch; ++b0) {
+        cheetah::GemvParams p = {};
+        p.w0 = static_cast<const uint16_t *>(weight);
+        p.rows = (int)rows;
+        p.cols = (int)cols;
+        p.batch = 1;
+        p.x = x + b0 * cols;
+        p.x_stride = (long long)cols;
+        p.y = y + b0 * rows;
+        p.y_stride = (long long)rows;
+        if (cheetah::launch_gemv<1, cheetah::kEpiStore>(p, st, false, sms) != 0) return -1;
+    }
+    return 0;
+}
+
+int cheetah_cuda_op_decode_attention(const CheetahCudaDecodeAttention *a, void *stream) {
+    CH_REQUIRE(a != nullptr && a->q && a->k_pool && a->v_pool && a->page_table && a->seq_lens && a->out,
+               "cheetah_cuda_op_decode_attention: null argument");
+    CH_REQUIRE(a->head_dim == 64 || a->head_dim == 128, "cheetah_cuda_op_decode_attention: head_dim must be 64 or 128");
+    CH_REQUIRE(a->kv_heads > 0 && a->q_heads % a->kv_heads == 0 && a->q_heads / a->kv_heads <= (uint32_t)cheetah::kMaxGroup,
+               "cheetah_cuda_op_decode_attention: q_heads must be a multiple of kv_heads (group <= 8)");
+    CH_REQUIRE(a->page_tokens > 0 && a->batch > 0 && a->num_pages > 0, "cheetah_cuda_op_decode_attention: empty shape");
+    CH_REQUIRE(a->kv_dtype == CHEETAH_CUDA_KV_BF16 || a->kv_dtype == CHEETAH_CUDA_KV_F32,
+               "cheetah_cuda_op_decode_attention: unknown kv_dtype");
+    int device = 0;
+    CH_CUDA_TRY(cudaGetDevice(&device));
+    const int sms = cheetah::sm_count(device);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    cheetah::AttnParams p = {};
+    p.q = a->q;
+    p.k_pool = a->k_pool;
+    p.v_pool = a->v_pool;
+    p.page_table = a->page_table;
+    p.seq_lens = a->seq_lens;
+    p.max_pages = (int)a->max_pages_per_seq;
+    p.num_pages = (int)a->num_pages;
+    p.page_tokens = (int)a->page_tokens;
+    p.batch = (int)a->batch;
+    p.q_heads = (int)a->q_heads;
+    p.kv_heads = (int)a->kv_heads;
+    p.window = (int)a->sliding_window;
+    p.splits = cheetah::attention_splits((int)a->batch, (int)a->kv_heads, (int)std::max<uint32_t>(1, a->max_seq_len), sms);
+    p.scale = 1.0f / sqrtf((float)a->head_dim);
+    p.out = a->out;
+    const size_t parts = (size_t)a->batch * a->kv_heads * p.splits;
+    const size_t o_bytes = parts * cheetah::kMaxGroup * a->head_dim * 4;
+    const size_t ml_bytes = parts * cheetah::kMaxGroup * 2 * 4;
+    const size_t t_bytes = (size_t)a->batch * a->kv_heads * 4;
+    uint8_t *scratch = nullptr;
+    CH_CUDA_TRY(cudaMallocAsync((void **)&scratch, o_bytes + ml_bytes + t_bytes + 512, st));
+    p.part_o = reinterpret_cast<float *>(scratch);
+    p.part_ml = reinterpret_cast<float *>(scratch + ((o_bytes + 255) & ~size_t(255)));
+    p.tickets = reinterpret_cast<unsigned int *>(scratch + ((o_bytes + 255) & ~size_t(255)) + ((ml_bytes + 255) & ~size_t(255)));
+    p.error = nullptr;
+    cudaError_t err = cudaMemsetAsync(p.tickets, 0, t_bytes, st);
+    int rc = 0;
+    if (err == cudaSuccess) {
+        rc = cheetah::launch_attention(p, (int)a->head_dim, a->kv_dtype == CHEETAH_CUDA_KV_F32, st, false);
+    }
+    cudaFreeAsync(scratch, st);
+    CH_CUDA_TRY(err);
+    return rc;
+}
+
+}  // extern "C"

@@ -390,3 +390,28 @@ def resolve_config(model: PreparedModel, max_positions: Optional[int] = None) ->
         "tie_word_embeddings": 1 if tie else 0, "sliding_window": window,
         "max_positions": int(max_pos),
     }
+
+
+SHAPES = {"qwen2-0.5b": QWEN2_0_5B, "qwen2-7b": QWEN2_7B, "tiny": TINY, "tiny-7b-heads": TINY_7B_HEADS}
+
+
+def cached_synthetic(name: str, seed: int = 0, root: Optional[os.PathLike] = None) -> Path:
+    """Seeded synthetic prepared model, written once per machine under
+    `$CHEETAH_MODEL_CACHE` (default /tmp/cheetah_models) and reused."""
+    base = Path(root or os.environ.get("CHEETAH_MODEL_CACHE", "/tmp/cheetah_models"))
+    target = base / f"{name}_seed{seed}"
+    marker = target / ".complete"
+    if marker.exists():
+        return target
+    tmp = base / f".{name}_seed{seed}.{os.getpid()}"
+    if tmp.exists():
+        import shutil
+        shutil.rmtree(tmp)
+    write_prepared(tmp, SHAPES[name], seed)
+    (tmp / ".complete").write_text("ok")
+    try:
+        os.rename(tmp, target)
+    except OSError:
+        import shutil
+        shutil.rmtree(tmp, ignore_errors=True)
+    return target

@@ -1,0 +1,173 @@
+/* cheetah_cuda — B200 (sm_100a) backend for Cheetah's decoder hot path.
+ *
+ * A C-ABI shared library (libcheetah_cuda.so) that the reference's Rust host
+ * binds beside its Vulkan substrate (`src/native.rs:927` `mod vulkan` is the
+ * sibling; this is `mod cuda`). Style follows `cheetah_vulkan.h`: opaque
+ * handles, `int` status (0 = success, negative = failure) and a thread-local
+ * last-error string. No function aborts or exits the process.
+ *
+ * Two layers:
+ *  - Model / sequence entries implement the reference's `ModelForward`
+ *    boundary (`src/chat/registry.rs:57-85`): `forward(tokens, offset)` returns
+ *    the final position's vocabulary logits; `clear_cache`, `kv_snapshot`,
+ *    `restore_kv_prefix`. Host buffers in and out; the library owns all
+ *    device memory (weights HBM-resident, paged KV pool).
+ *  - Op entries (`cheetah_cuda_op_*`) expose single kernels over caller-owned
+ *    DEVICE buffers on a caller stream (`cudaStream_t` passed as void*), one
+ *    per reference math kernel they replace.
+ */
+#ifndef CHEETAH_CUDA_H
+#define CHEETAH_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CHEETAH_CUDA_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define CHEETAH_CUDA_API __attribute__((visibility("default")))
+#else
+#define CHEETAH_CUDA_API
+#endif
+
+/* KV cache element types. BF16 halves KV traffic; F32 mirrors the
+ * reference's f32 cache (`ops.rs:995-999`) for parity runs. */
+enum { CHEETAH_CUDA_KV_BF16 = 0, CHEETAH_CUDA_KV_F32 = 1 };
+
+/* Resolved decoder hyper-parameters. Replaces the fields of the reference's
+ * `DecoderConfig` (`src/chat/native/decoder.rs:29-92`) that the Qwen2 path
+ * reads; the Rust loader fills it from `DecoderConfig::resolve`
+ * (`decoder.rs:260-486`). */
+typedef struct CheetahCudaConfig {
+    uint32_t hidden_size;
+    uint32_t num_layers;
+    uint32_t q_heads;
+    uint32_t kv_heads;
+    uint32_t head_dim;
+    uint32_t rotary_dim;
+    uint32_t intermediate_size;
+    uint32_t vocab_size;
+    float rms_eps;
+    float rope_theta;
+    int32_t tie_word_embeddings;
+    uint32_t sliding_window;   /* 0 = full attention */
+    uint32_t max_positions;    /* per-sequence capacity (rope table, page table) */
+    uint32_t kv_page_tokens;   /* tokens per KV page; 0 = 64 (CHEETAH_CUDA_KV_PAGE) */
+    uint32_t kv_pool_tokens;   /* KV pool size in tokens; 0 = default */
+    int32_t kv_dtype;          /* CHEETAH_CUDA_KV_* */
+} CheetahCudaConfig;
+
+typedef struct CheetahCudaModel CheetahCudaModel;
+typedef struct CheetahCudaSeq CheetahCudaSeq;
+typedef struct CheetahCudaSnapshot CheetahCudaSnapshot;
+
+typedef struct CheetahCudaModelInfo {
+    uint64_t weight_bytes;    /* bytes of weights resident in HBM */
+    uint64_t kv_pool_bytes;   /* bytes of the KV page pool */
+    uint32_t kv_pages_total;
+    uint32_t kv_pages_free;
+    int32_t device;
+    int32_t quant;            /* 0 bf16, 1 q8, 2 q4 */
+} CheetahCudaModelInfo;
+
+/* Thread-local description of the last failure on this thread
+ * (mirrors `check_native_result`, `src/native.rs:1860-1870`). */
+CHEETAH_CUDA_API const char *cheetah_cuda_last_error(void);
+CHEETAH_CUDA_API int cheetah_cuda_abi_version(void);
+CHEETAH_CUDA_API int cheetah_cuda_device_count(int *count);
+
+/* Open a prepared model directory (`cheetah init` layout: cheetah_units.json
+ * + .cheetah/weights/*.safetensors, read as `store.rs:74-157` does) and make
+ * every unit HBM-resident on `device`. `quant` is "bf16", "q8" or "q4"
+ * (selected like `CHEETAH_QUANT_Q8/Q4`, `precision.rs:348`). Replaces
+ * `qwen2_native_loader` (`qwen2.rs:654`) + `OpsToolbox::open` (`ops.rs:1051`). */
+CHEETAH_CUDA_API int cheetah_cuda_model_open(const char *prepared_dir, const CheetahCudaConfig *config,
+                            const char *quant, int device, CheetahCudaModel **out);
+CHEETAH_CUDA_API int cheetah_cuda_model_free(CheetahCudaModel *model);
+CHEETAH_CUDA_API int cheetah_cuda_model_info(const CheetahCudaModel *model, CheetahCudaModelInfo *info);
+
+/* A sequence: an empty KV cache that shares the model's weights — the
+ * `ModelForwardClone` contract (`registry.rs:95-117`, pinned by
+ * `decoder.rs:1761`). One thread uses a sequence at a time. */
+CHEETAH_CUDA_API int cheetah_cuda_seq_new(CheetahCudaModel *model, CheetahCudaSeq **out);
+CHEETAH_CUDA_API int cheetah_cuda_seq_free(CheetahCudaSeq *seq);
+/* `ModelForward::clear_cache` (`registry.rs:63`, `ops.rs:1610`). */
+CHEETAH_CUDA_API int cheetah_cuda_seq_clear(CheetahCudaSeq *seq);
+CHEETAH_CUDA_API int cheetah_cuda_seq_positions(const CheetahCudaSeq *seq, size_t *positions);
+
+/* `ModelForward::forward` (`registry.rs:60`, `qwen2.rs:600-606`): run
+ * `tokens[0..n)` at absolute positions `offset..offset+n` and write the final
+ * position's `vocab_size` f32 logits to `logits_out` (host memory). `offset`
+ * must equal the sequence's cached position count. Errors: empty input, a
+ * token id >= vocab (`ops.rs:1065-1078`), capacity exceeded. */
+CHEETAH_CUDA_API int cheetah_cuda_forward(CheetahCudaSeq *seq, const uint32_t *tokens, size_t n, size_t offset,
+                         float *logits_out);
+/* As above; `logits_out` may be NULL (no logits copy) and `argmax_out`
+ * (nullable) receives the greedy token chosen as the engine does
+ * (`engine.rs:2247-2253`: max by total order, last maximum wins). */
+CHEETAH_CUDA_API int cheetah_cuda_forward_ex(CheetahCudaSeq *seq, const uint32_t *tokens, size_t n,
+                            size_t offset, float *logits_out, uint32_t *argmax_out);
+
+/* Greedy decode kept on the device: step i consumes the greedy token of step
+ * i-1 (step 0 consumes `first_token`) at position `offset + i`; tokens_out[i]
+ * receives step i's greedy token. No host round trip between steps — the
+ * device-resident form of the engine's greedy loop (`engine.rs:1920-1958`).
+ * With tokens_out == NULL the steps are only enqueued on the sequence stream
+ * (see cheetah_cuda_seq_stream) and the call returns without waiting. */
+CHEETAH_CUDA_API int cheetah_cuda_generate_greedy(CheetahCudaSeq *seq, uint32_t first_token, size_t offset,
+                                                  size_t steps, uint32_t *tokens_out);
+/* The sequence's CUDA stream (cudaStream_t) for event timing / synchronisation. */
+CHEETAH_CUDA_API int cheetah_cuda_seq_stream(const CheetahCudaSeq *seq, void **stream);
+
+/* `ModelForward::kv_snapshot` / `restore_kv_prefix` (`registry.rs:68-79`,
+ * `ops.rs:1575-1607`): a device-resident copy of the sequence's KV pages. */
+CHEETAH_CUDA_API int cheetah_cuda_seq_snapshot(const CheetahCudaSeq *seq, CheetahCudaSnapshot **out);
+CHEETAH_CUDA_API int cheetah_cuda_snapshot_positions(const CheetahCudaSnapshot *snapshot, size_t *positions);
+CHEETAH_CUDA_API int cheetah_cuda_seq_restore_prefix(CheetahCudaSeq *seq, const CheetahCudaSnapshot *snapshot,
+                                    size_t positions);
+CHEETAH_CUDA_API int cheetah_cuda_snapshot_free(CheetahCudaSnapshot *snapshot);
+/* Test/diagnostic view of one layer's cache as f32 [positions][kv_heads*head_dim]
+ * (host buffers of positions*kv_dim floats each). */
+CHEETAH_CUDA_API int cheetah_cuda_seq_export_kv(const CheetahCudaSeq *seq, size_t layer, float *k_out,
+                               float *v_out);
+
+/* ---- Op entries: caller-owned device buffers, caller stream ---- */
+
+/* y[b] = W . x[b] for b < batch. W: bf16 row-major [rows, cols] (cols % 8 == 0,
+ * 16-byte aligned), x: f32 [batch, cols], y: f32 [batch, rows].
+ * Replaces `ops::gemv` (`ops.rs:246`) / `bf16::gemv` (`precision/bf16.rs:54`). */
+CHEETAH_CUDA_API int cheetah_cuda_op_gemv_bf16(const void *weight, size_t rows, size_t cols, const float *x,
+                              size_t batch, float *y, void *stream);
+
+/* Paged GQA decode attention for `batch` sequences, one query position each
+ * (the newest), over a paged KV pool. Replaces `OpsToolbox::attention` /
+ * `attention_head` (`ops.rs:1357-1467`) for one position of every head. */
+typedef struct CheetahCudaDecodeAttention {
+    const float *q;            /* [batch][q_heads][head_dim], RoPE applied */
+    const void *k_pool;        /* [num_pages][kv_heads][page_tokens][head_dim] */
+    const void *v_pool;        /* same layout as k_pool */
+    int32_t kv_dtype;          /* CHEETAH_CUDA_KV_* */
+    const int32_t *page_table; /* [batch][max_pages_per_seq] page ids */
+    uint32_t max_pages_per_seq;
+    const int32_t *seq_lens;   /* [batch] cached positions incl. the query's */
+    uint32_t max_seq_len;      /* host upper bound on seq_lens (work split) */
+    uint32_t num_pages;        /* pages in the pool (bounds check) */
+    uint32_t page_tokens;
+    uint32_t batch;
+    uint32_t q_heads;
+    uint32_t kv_heads;
+    uint32_t head_dim;         /* 64 or 128 */
+    uint32_t sliding_window;   /* 0 = full */
+    float *out;                /* [batch][q_heads][head_dim] */
+} CheetahCudaDecodeAttention;
+CHEETAH_CUDA_API int cheetah_cuda_op_decode_attention(const CheetahCudaDecodeAttention *args, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif
