@@ -9,11 +9,14 @@
 //
 // Grid (splits, kv_heads, batch): each CTA walks a contiguous span of
 // positions for one KV head and serves all `group` query heads that share
-// it, so every K/V byte is read once. Lane-per-position scores (K row read
-// with 128-bit loads, q broadcast from shared memory), lane-per-dimension
-// value mix. The last CTA of each (sequence, kv head) to finish merges the
+// it, so every K/V byte is read once. Lane-per-position scores (the whole K
+// row requested with 128-bit loads before use, q broadcast from shared
+// memory), lane-per-dimension value mix (16 V rows in flight). The active
+// split count follows the live length (>= 128 positions per CTA); CTAs past
+// it exit. The last CTA of each (sequence, kv head) to finish merges the
 // split partials (threadfence + atomic ticket, no spin-wait) and resets the
-// ticket for the next launch.
+// ticket for the next launch. This CUDA-core kernel serves the f32 cache;
+// the bf16 cache takes the tensor-core kernel in attention_mma.cuh.
 #pragma once
 
 #include "common.cuh"
@@ -46,6 +49,8 @@ struct AttnParams {
 constexpr int kAttnThreads = 128;
 constexpr int kAttnWarps = kAttnThreads / kWarp;
 constexpr int kMaxGroup = 8;
+constexpr int kMinChunk = kAttnWarps * kWarp;  // positions per CTA at least
+constexpr int kMaxSplits = 256;
 
 template <int HD, bool KV_F32>
 __device__ __forceinline__ void load_k_chunk(const void *pool, long long row, int c, float *out8) {
@@ -87,14 +92,120 @@ __device__ __forceinline__ void load_v_lane(const void *pool, long long row, int
     }
 }
 
+// Active split count for a visible span: at least kMinChunk positions per
+// CTA (one 32-position tile per warp), at most `splits`. Every CTA of a
+// (sequence, kv head) derives the same value from the same length.
+__device__ __forceinline__ void split_range(int span, int splits, int split, int &active, int &chunk) {
+    chunk = (span + splits - 1) / splits;
+    chunk = (chunk + kWarp - 1) / kWarp * kWarp;
+    chunk = max(chunk, kMinChunk);
+    active = span > 0 ? (span + chunk - 1) / chunk : 1;
+}
+
+// Merge this CTA's partial (m, l, o) into the per-split scratch, then the
+// last CTA to arrive merges all active splits into `out`.
+template <int HD>
+__device__ __forceinline__ void merge_splits(const AttnParams &p, int b, int kvh, int split, int active,
+                                             int group, float (*m_s)[kMaxGroup], float (*l_s)[kMaxGroup],
+                                             float (*o_s)[kMaxGroup][HD], float (*w_s)[kMaxGroup],
+                                             float *big_l, int *is_last) {
+    const int warp = threadIdx.x / kWarp;
+    const int lane = threadIdx.x % kWarp;
+    const long long base = ((long long)b * p.kv_heads + kvh) * p.splits;
+    const long long part = base + split;
+    for (int i = threadIdx.x; i < group * HD; i += kAttnThreads) {
+        const int g = i / HD, d = i % HD;
+        float m = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kAttnWarps; ++w) m = fmaxf(m, m_s[w][g]);
+        float l = 0.0f, o = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kAttnWarps; ++w) {
+            const float f = (m == -INFINITY) ? 0.0f : expf(m_s[w][g] - m);
+            l += l_s[w][g] * f;
+            o += o_s[w][g][d] * f;
+        }
+        if (active == 1) {
+            p.out[((long long)b * p.q_heads + kvh * group + g) * HD + d] = l > 0.0f ? o / l : 0.0f;
+        } else {
+            p.part_o[(part * kMaxGroup + g) * HD + d] = o;
+            if (d == 0) {
+                p.part_ml[(part * kMaxGroup + g) * 2 + 0] = m;
+                p.part_ml[(part * kMaxGroup + g) * 2 + 1] = l;
+            }
+        }
+    }
+    if (active == 1) return;
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        unsigned int *ticket = p.tickets + (long long)b * p.kv_heads + kvh;
+        const unsigned int prev = atomicAdd(ticket, 1u);
+        *is_last = (prev == (unsigned)active - 1);
+        if (*is_last) *ticket = 0u;
+    }
+    __syncthreads();
+    if (!*is_last) return;
+    __threadfence();
+    // Per-head global max and split weights (warp g handles heads g, g+4).
+    for (int g = warp; g < group; g += kAttnWarps) {
+        float m = -INFINITY;
+        for (int s2 = lane; s2 < active; s2 += kWarp) m = fmaxf(m, __ldcg(&p.part_ml[((base + s2) * kMaxGroup + g) * 2]));
+        m = warp_max(m);
+        float l = 0.0f;
+        for (int s2 = lane; s2 < active; s2 += kWarp) {
+            const float ms = __ldcg(&p.part_ml[((base + s2) * kMaxGroup + g) * 2]);
+            const float w = (m == -INFINITY) ? 0.0f : expf(ms - m);
+            w_s[s2][g] = w;
+            l += w * __ldcg(&p.part_ml[((base + s2) * kMaxGroup + g) * 2 + 1]);
+        }
+        l = warp_sum(l);
+        if (lane == 0) big_l[g] = l;
+    }
+    __syncthreads();
+    // Weighted sum of the split outputs, four dimensions per thread.
+    for (int i = threadIdx.x; i < group * (HD / 4); i += kAttnThreads) {
+        const int g = i / (HD / 4), d4 = i % (HD / 4);
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        const float4 *src = reinterpret_cast<const float4 *>(p.part_o + ((base * kMaxGroup) + g) * HD) + d4;
+        const long long stride4 = (long long)kMaxGroup * HD / 4;
+        int s2 = 0;
+        for (; s2 + 8 <= active; s2 += 8) {
+            float4 v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) v[u] = __ldcg(src + (s2 + u) * stride4);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const float w = w_s[s2 + u][g];
+                acc.x = fmaf(w, v[u].x, acc.x); acc.y = fmaf(w, v[u].y, acc.y);
+                acc.z = fmaf(w, v[u].z, acc.z); acc.w = fmaf(w, v[u].w, acc.w);
+            }
+        }
+        for (; s2 < active; ++s2) {
+            const float4 v = __ldcg(src + s2 * stride4);
+            const float w = w_s[s2][g];
+            acc.x = fmaf(w, v.x, acc.x); acc.y = fmaf(w, v.y, acc.y);
+            acc.z = fmaf(w, v.z, acc.z); acc.w = fmaf(w, v.w, acc.w);
+        }
+        const float l = big_l[g];
+        const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+        float4 r = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+        if (!(l > 0.0f)) r = make_float4(0.f, 0.f, 0.f, 0.f);
+        reinterpret_cast<float4 *>(p.out + ((long long)b * p.q_heads + kvh * group + g) * HD)[d4] = r;
+    }
+}
+
 template <int HD, bool KV_F32>
 __global__ void __launch_bounds__(kAttnThreads) decode_attention_kernel(const AttnParams p) {
     constexpr int DPL = HD / kWarp;
+    constexpr int CHUNKS = HD / 8;  // 8-element chunks per row
     __shared__ __align__(16) float q_s[kMaxGroup][HD];
     __shared__ __align__(16) float p_s[kAttnWarps][kWarp][kMaxGroup];
     __shared__ float m_s[kAttnWarps][kMaxGroup];
     __shared__ float l_s[kAttnWarps][kMaxGroup];
     __shared__ __align__(16) float o_s[kAttnWarps][kMaxGroup][HD];
+    __shared__ float w_s[kMaxSplits][kMaxGroup];
+    __shared__ float big_l[kMaxGroup];
     __shared__ int is_last;
 
     const int split = blockIdx.x;
@@ -112,8 +223,9 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attention_kernel(const At
     if (p.window > 0) ws = L > p.window ? L - p.window : 0;
     if (ws > L - 1) ws = L > 0 ? L - 1 : 0;
     const int span = L - ws;
-    int chunk = (span + p.splits - 1) / p.splits;
-    chunk = (chunk + kWarp - 1) / kWarp * kWarp;
+    int active, chunk;
+    split_range(span, p.splits, split, active, chunk);
+    if (split >= active) return;
     const int begin = ws + split * chunk;
     const int end = min(L, begin + chunk);
 
@@ -145,25 +257,30 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attention_kernel(const At
                 row = ((long long)page * p.kv_heads + kvh) * p.page_tokens + (pos % p.page_tokens);
             }
         }
+        // Scores: the whole K row is requested before any arithmetic.
         float s[kMaxGroup];
 #pragma unroll
         for (int g = 0; g < kMaxGroup; ++g) s[g] = 0.0f;
         if (valid) {
-#pragma unroll 2
-            for (int c = 0; c < HD / 8; ++c) {
-                float k8[8];
-                load_k_chunk<HD, KV_F32>(p.k_pool, row, c, k8);
 #pragma unroll
-                for (int g = 0; g < kMaxGroup; ++g) {
-                    if (g < group) {
-                        const float4 qa = *reinterpret_cast<const float4 *>(&q_s[g][c * 8]);
-                        const float4 qb = *reinterpret_cast<const float4 *>(&q_s[g][c * 8 + 4]);
-                        float acc = s[g];
-                        acc = fmaf(k8[0], qa.x, acc); acc = fmaf(k8[1], qa.y, acc);
-                        acc = fmaf(k8[2], qa.z, acc); acc = fmaf(k8[3], qa.w, acc);
-                        acc = fmaf(k8[4], qb.x, acc); acc = fmaf(k8[5], qb.y, acc);
-                        acc = fmaf(k8[6], qb.z, acc); acc = fmaf(k8[7], qb.w, acc);
-                        s[g] = acc;
+            for (int c0 = 0; c0 < CHUNKS; c0 += 8) {
+                float k8[8][8];
+#pragma unroll
+                for (int c = 0; c < 8; ++c) load_k_chunk<HD, KV_F32>(p.k_pool, row, c0 + c, k8[c]);
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+#pragma unroll
+                    for (int g = 0; g < kMaxGroup; ++g) {
+                        if (g < group) {
+                            const float4 qa = *reinterpret_cast<const float4 *>(&q_s[g][(c0 + c) * 8]);
+                            const float4 qb = *reinterpret_cast<const float4 *>(&q_s[g][(c0 + c) * 8 + 4]);
+                            float acc = s[g];
+                            acc = fmaf(k8[c][0], qa.x, acc); acc = fmaf(k8[c][1], qa.y, acc);
+                            acc = fmaf(k8[c][2], qa.z, acc); acc = fmaf(k8[c][3], qa.w, acc);
+                            acc = fmaf(k8[c][4], qb.x, acc); acc = fmaf(k8[c][5], qb.y, acc);
+                            acc = fmaf(k8[c][6], qb.z, acc); acc = fmaf(k8[c][7], qb.w, acc);
+                            s[g] = acc;
+                        }
                     }
                 }
             }
@@ -183,26 +300,40 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attention_kernel(const At
             }
         }
         __syncwarp();
+        // Value mix: 16 V rows requested at a time, then the FMAs.
         const int count = min(kWarp, end - t0);
-        for (int j = 0; j < count; ++j) {
-            const long long vrow = __shfl_sync(0xFFFFFFFFu, row, j);
-            float v[DPL];
-            load_v_lane<HD, KV_F32>(p.v_pool, vrow, lane, v);
-            const float4 pa = *reinterpret_cast<const float4 *>(&p_s[warp][j][0]);
-            const float4 pb = *reinterpret_cast<const float4 *>(&p_s[warp][j][4]);
-            const float pj[kMaxGroup] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
 #pragma unroll
-            for (int g = 0; g < kMaxGroup; ++g) {
-                if (g < group) {
+        for (int j0 = 0; j0 < kWarp; j0 += 16) {
+            if (j0 < count) {
+                float v[16][DPL];
 #pragma unroll
-                    for (int e = 0; e < DPL; ++e) o_run[g][e] = fmaf(pj[g], v[e], o_run[g][e]);
+                for (int j = 0; j < 16; ++j) {
+                    const long long vrow = __shfl_sync(0xFFFFFFFFu, row, j0 + j);
+                    if (j0 + j < count) {
+                        load_v_lane<HD, KV_F32>(p.v_pool, vrow, lane, v[j]);
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < DPL; ++e) v[j][e] = 0.0f;
+                    }
+                }
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const float4 pa = *reinterpret_cast<const float4 *>(&p_s[warp][j0 + j][0]);
+                    const float4 pb = *reinterpret_cast<const float4 *>(&p_s[warp][j0 + j][4]);
+                    const float pj[kMaxGroup] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
+#pragma unroll
+                    for (int g = 0; g < kMaxGroup; ++g) {
+                        if (g < group) {
+#pragma unroll
+                            for (int e = 0; e < DPL; ++e) o_run[g][e] = fmaf(pj[g], v[j][e], o_run[g][e]);
+                        }
+                    }
                 }
             }
         }
         __syncwarp();
     }
 
-    // Merge the warps of this CTA.
     if (lane == 0) {
 #pragma unroll
         for (int g = 0; g < kMaxGroup; ++g) {
@@ -216,53 +347,7 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attention_kernel(const At
         for (int e = 0; e < DPL; ++e) o_s[warp][g][lane * DPL + e] = o_run[g][e];
     }
     __syncthreads();
-
-    const long long part = ((long long)b * p.kv_heads + kvh) * p.splits + split;
-    for (int i = threadIdx.x; i < group * HD; i += kAttnThreads) {
-        const int g = i / HD, d = i % HD;
-        float m = -INFINITY;
-#pragma unroll
-        for (int w = 0; w < kAttnWarps; ++w) m = fmaxf(m, m_s[w][g]);
-        float l = 0.0f, o = 0.0f;
-#pragma unroll
-        for (int w = 0; w < kAttnWarps; ++w) {
-            const float f = (m == -INFINITY) ? 0.0f : expf(m_s[w][g] - m);
-            l += l_s[w][g] * f;
-            o += o_s[w][g][d] * f;
-        }
-        p.part_o[(part * kMaxGroup + g) * HD + d] = o;
-        if (d == 0) {
-            p.part_ml[(part * kMaxGroup + g) * 2 + 0] = m;
-            p.part_ml[(part * kMaxGroup + g) * 2 + 1] = l;
-        }
-    }
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        unsigned int *ticket = p.tickets + (long long)b * p.kv_heads + kvh;
-        const unsigned int prev = atomicAdd(ticket, 1u);
-        is_last = (prev == (unsigned)p.splits - 1);
-        if (is_last) *ticket = 0u;
-    }
-    __syncthreads();
-    if (!is_last) return;
-    __threadfence();
-
-    // Last CTA: merge all splits of this (sequence, kv head).
-    const long long base = ((long long)b * p.kv_heads + kvh) * p.splits;
-    for (int i = threadIdx.x; i < group * HD; i += kAttnThreads) {
-        const int g = i / HD, d = i % HD;
-        float m = -INFINITY;
-        for (int s2 = 0; s2 < p.splits; ++s2) m = fmaxf(m, __ldcg(&p.part_ml[((base + s2) * kMaxGroup + g) * 2]));
-        float l = 0.0f, o = 0.0f;
-        for (int s2 = 0; s2 < p.splits; ++s2) {
-            const float ms = __ldcg(&p.part_ml[((base + s2) * kMaxGroup + g) * 2]);
-            const float f = (m == -INFINITY) ? 0.0f : expf(ms - m);
-            l += __ldcg(&p.part_ml[((base + s2) * kMaxGroup + g) * 2 + 1]) * f;
-            o += __ldcg(&p.part_o[((base + s2) * kMaxGroup + g) * HD + d]) * f;
-        }
-        p.out[((long long)b * p.q_heads + kvh * group + g) * HD + d] = l > 0.0f ? o / l : 0.0f;
-    }
+    merge_splits<HD>(p, b, kvh, split, active, group, m_s, l_s, o_s, w_s, big_l, &is_last);
 }
 
 }  // namespace cheetah

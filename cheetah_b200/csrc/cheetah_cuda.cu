@@ -8,6 +8,8 @@
 // for the decode step (embed -> 24 x [qkv, attention, o_proj, gate/up, down]
 // -> lm_head), launched with programmatic dependent launch so each kernel's
 // weight stream starts while its predecessor drains.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 #include <math.h>
 #include <string.h>
@@ -15,12 +17,14 @@
 #include <algorithm>
 #include <atomic>
 #include <cstdlib>
+#include <map>
 #include <mutex>
 #include <string>
 #include <vector>
 
 #include "cheetah_cuda.h"
 #include "attention.cuh"
+#include "attention_mma.cuh"
 #include "common.cuh"
 #include "gemv.cuh"
 #include "kernels_misc.cuh"
@@ -120,7 +124,69 @@ int launch_attention(const AttnParams &p, int head_dim, bool kv_f32, cudaStream_
 int attention_splits(int batch, int kv_heads, int max_len, int sms) {
     const int target = std::max(1, (2 * sms) / std::max(1, batch * kv_heads));
     const int by_len = std::max(1, (max_len + kWarp - 1) / kWarp);
-    return std::max(1, std::min(std::min(target, by_len), 512));
+    return std::max(1, std::min(std::min(target, by_len), kMaxSplits));
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *ptr = nullptr;
+        cudaDriverEntryPointQueryResult status;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &status) == cudaSuccess &&
+            status == cudaDriverEntryPointSuccess) {
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+        }
+    });
+    return fn;
+}
+
+// 2D map over a bf16 KV pool viewed as [rows][head_dim]: 64-column boxes of
+// `tile_rows` rows, 128-byte swizzle (the layout the MMA kernel's ldmatrix
+// addressing undoes).
+int make_kv_tensor_map(CUtensorMap *map, const void *base, unsigned long long rows, int head_dim) {
+    auto encode = tensor_map_encoder();
+    CH_REQUIRE(encode != nullptr, "CUDA backend: cuTensorMapEncodeTiled is unavailable");
+    CH_REQUIRE(((uintptr_t)base & 15) == 0, "CUDA backend: KV pool must be 16-byte aligned");
+    const int tile_rows = kTileBytes / (head_dim * 2);
+    cuuint64_t dims[2] = {(cuuint64_t)head_dim, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)head_dim * 2};
+    cuuint32_t box[2] = {64u, (cuuint32_t)tile_rows};
+    cuuint32_t estr[2] = {1u, 1u};
+    CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box,
+                        estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    CH_REQUIRE(r == CUDA_SUCCESS, "CUDA backend: cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+    return 0;
+}
+
+bool mma_attention_eligible(int head_dim, int page_tokens) {
+    if (!env_flag("CHEETAH_CUDA_MMA_ATTENTION", true)) return false;
+    if (head_dim != 64 && head_dim != 128) return false;
+    return page_tokens % (kTileBytes / (head_dim * 2)) == 0;
+}
+
+int launch_attention_mma(const CUtensorMap &k_map, const CUtensorMap &v_map, const MmaAttnParams &mp,
+                         int head_dim, cudaStream_t stream, bool pdl) {
+    const size_t smem = mma_attention_smem();
+    dim3 grid(mp.a.splits, mp.a.kv_heads, mp.a.batch);
+    if (head_dim == 64) {
+        CH_CUDA_TRY(cudaFuncSetAttribute(decode_attention_mma_kernel<64>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        CH_CUDA_TRY(launch_ex(decode_attention_mma_kernel<64>, grid, dim3(kMmaThreads), smem, stream, pdl,
+                              k_map, v_map, mp));
+    } else {
+        CH_CUDA_TRY(cudaFuncSetAttribute(decode_attention_mma_kernel<128>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        CH_CUDA_TRY(launch_ex(decode_attention_mma_kernel<128>, grid, dim3(kMmaThreads), smem, stream, pdl,
+                              k_map, v_map, mp));
+    }
+    return 0;
+}
+
+int mma_attention_splits(int batch, int kv_heads, int sms) {
+    return std::max(1, std::min(kMaxSplits, sms / std::max(1, batch * kv_heads)));
 }
 
 struct LayerWeights {
@@ -159,6 +225,9 @@ struct Model {
     int num_pages = 0;
     int page_tokens = 64;
     int kv_f32 = 0;
+    bool use_mma_attention = false;
+    CUtensorMap k_map{};
+    CUtensorMap v_map{};
     std::mutex pool_mutex;
     std::vector<int> free_pages;
     std::atomic<int> refs{1};
@@ -215,6 +284,8 @@ struct Seq {
     unsigned int *tickets = nullptr;
     int *d_error = nullptr;
     int splits = 1;
+    int mma_splits = 1;
+    int scratch_splits = 1;
     int32_t *token_log = nullptr;
     cudaGraphExec_t graph = nullptr;
     cudaGraphExec_t chain_graph = nullptr;
@@ -324,7 +395,16 @@ int enqueue_decode_step(Seq &s, bool chain) {
         at.part_ml = s.part_ml;
         at.tickets = s.tickets;
         at.error = s.d_error;
-        if (launch_attention(at, c.head_dim, m.kv_f32 != 0, st, pdl) != 0) return -1;
+        if (m.use_mma_attention) {
+            MmaAttnParams mp = {};
+            mp.a = at;
+            mp.a.splits = s.mma_splits;
+            mp.layer_row_offset = (long long)layer * m.num_pages * c.kv_heads * m.page_tokens;
+            mp.page_tokens = m.page_tokens;
+            if (launch_attention_mma(m.k_map, m.v_map, mp, c.head_dim, st, pdl) != 0) return -1;
+        } else if (launch_attention(at, c.head_dim, m.kv_f32 != 0, st, pdl) != 0) {
+            return -1;
+        }
 
         GemvParams o = {};
         o.w0 = w.wo;
@@ -671,6 +751,15 @@ int open_model(const char *prepared_dir, const CheetahCudaConfig *config, const 
     }
     cudaMemset(m->k_pool, 0, pool_bytes);
     cudaMemset(m->v_pool, 0, pool_bytes);
+    if (!m->kv_f32 && mma_attention_eligible((int)c.head_dim, m->page_tokens)) {
+        const unsigned long long rows = (unsigned long long)c.num_layers * m->num_pages * c.kv_heads * m->page_tokens;
+        if (make_kv_tensor_map(&m->k_map, m->k_pool, rows, (int)c.head_dim) != 0 ||
+            make_kv_tensor_map(&m->v_map, m->v_pool, rows, (int)c.head_dim) != 0) {
+            delete m;
+            return -1;
+        }
+        m->use_mma_attention = true;
+    }
     m->free_pages.reserve(m->num_pages);
     for (int i = m->num_pages - 1; i >= 0; --i) m->free_pages.push_back(i);
     err = cudaDeviceSynchronize();
@@ -688,6 +777,8 @@ int new_seq(Model *m, Seq **out) {
     s->m = m;
     s->max_pages = (int)((c.max_positions + m->page_tokens - 1) / m->page_tokens);
     s->splits = attention_splits(1, c.kv_heads, c.max_positions, m->sms);
+    s->mma_splits = mma_attention_splits(1, c.kv_heads, m->sms);
+    s->scratch_splits = std::max(s->splits, s->mma_splits);
     const size_t QD = (size_t)c.q_heads * c.head_dim;
     bool ok = cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking) == cudaSuccess &&
               cudaMalloc(&s->page_table, s->max_pages * sizeof(int32_t)) == cudaSuccess &&
@@ -698,8 +789,8 @@ int new_seq(Model *m, Seq **out) {
               cudaMalloc(&s->logits, (size_t)c.vocab_size * 4) == cudaSuccess &&
               cudaMalloc(&s->argmax, 8) == cudaSuccess &&
               cudaMalloc(&s->d_step, sizeof(StepState)) == cudaSuccess &&
-              cudaMalloc(&s->part_o, (size_t)c.kv_heads * s->splits * kMaxGroup * c.head_dim * 4) == cudaSuccess &&
-              cudaMalloc(&s->part_ml, (size_t)c.kv_heads * s->splits * kMaxGroup * 2 * 4) == cudaSuccess &&
+              cudaMalloc(&s->part_o, (size_t)c.kv_heads * s->scratch_splits * kMaxGroup * c.head_dim * 4) == cudaSuccess &&
+              cudaMalloc(&s->part_ml, (size_t)c.kv_heads * s->scratch_splits * kMaxGroup * 2 * 4) == cudaSuccess &&
               cudaMalloc(&s->tickets, c.kv_heads * 4) == cudaSuccess &&
               cudaMalloc(&s->d_error, 4) == cudaSuccess &&
               cudaMalloc(&s->token_log, (size_t)c.max_positions * 4) == cudaSuccess &&
@@ -1060,6 +1151,46 @@ int cheetah_cuda_op_gemv_bf16(const void *weight, size_t rows, size_t cols, cons
     return 0;
 }
 
+// Split-merge scratch for the op entry, cached per (device, stream) and grown
+// on demand; calls on one stream are ordered, so they may share it. Merge
+// tickets live in their own buffer, zeroed when (re)allocated: every launch
+// returns the tickets it used to zero, so any later layout finds zeros.
+struct OpScratch {
+    uint8_t *partials = nullptr;
+    size_t partial_bytes = 0;
+    unsigned int *tickets = nullptr;
+    size_t ticket_count = 0;
+};
+static std::mutex g_op_scratch_mutex;
+static std::map<std::pair<int, cudaStream_t>, OpScratch> g_op_scratch;
+
+static int op_scratch(int device, cudaStream_t stream, size_t partial_bytes, size_t tickets,
+                      uint8_t **partials_out, unsigned int **tickets_out) {
+    std::lock_guard<std::mutex> lock(g_op_scratch_mutex);
+    OpScratch &s = g_op_scratch[{device, stream}];
+    if (s.partial_bytes < partial_bytes || s.ticket_count < tickets) {
+        CH_CUDA_TRY(cudaStreamSynchronize(stream));
+    }
+    if (s.partial_bytes < partial_bytes) {
+        cudaFree(s.partials);
+        s.partials = nullptr;
+        s.partial_bytes = 0;
+        CH_CUDA_TRY(cudaMalloc(&s.partials, partial_bytes));
+        s.partial_bytes = partial_bytes;
+    }
+    if (s.ticket_count < tickets) {
+        cudaFree(s.tickets);
+        s.tickets = nullptr;
+        s.ticket_count = 0;
+        CH_CUDA_TRY(cudaMalloc(&s.tickets, tickets * sizeof(unsigned int)));
+        CH_CUDA_TRY(cudaMemsetAsync(s.tickets, 0, tickets * sizeof(unsigned int), stream));
+        s.ticket_count = tickets;
+    }
+    *partials_out = s.partials;
+    *tickets_out = s.tickets;
+    return 0;
+}
+
 int cheetah_cuda_op_decode_attention(const CheetahCudaDecodeAttention *a, void *stream) {
     CH_REQUIRE(a != nullptr && a->q && a->k_pool && a->v_pool && a->page_table && a->seq_lens && a->out,
                "cheetah_cuda_op_decode_attention: null argument");
@@ -1069,10 +1200,14 @@ int cheetah_cuda_op_decode_attention(const CheetahCudaDecodeAttention *a, void *
     CH_REQUIRE(a->page_tokens > 0 && a->batch > 0 && a->num_pages > 0, "cheetah_cuda_op_decode_attention: empty shape");
     CH_REQUIRE(a->kv_dtype == CHEETAH_CUDA_KV_BF16 || a->kv_dtype == CHEETAH_CUDA_KV_F32,
                "cheetah_cuda_op_decode_attention: unknown kv_dtype");
+    CH_REQUIRE(((uintptr_t)a->q & 15) == 0 && ((uintptr_t)a->out & 15) == 0,
+               "cheetah_cuda_op_decode_attention: q and out must be 16-byte aligned");
     int device = 0;
     CH_CUDA_TRY(cudaGetDevice(&device));
     const int sms = cheetah::sm_count(device);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const bool mma = a->kv_dtype == CHEETAH_CUDA_KV_BF16 &&
+                     cheetah::mma_attention_eligible((int)a->head_dim, (int)a->page_tokens);
     cheetah::AttnParams p = {};
     p.q = a->q;
     p.k_pool = a->k_pool;
@@ -1086,27 +1221,35 @@ int cheetah_cuda_op_decode_attention(const CheetahCudaDecodeAttention *a, void *
     p.q_heads = (int)a->q_heads;
     p.kv_heads = (int)a->kv_heads;
     p.window = (int)a->sliding_window;
-    p.splits = cheetah::attention_splits((int)a->batch, (int)a->kv_heads, (int)std::max<uint32_t>(1, a->max_seq_len), sms);
+    p.splits = mma ? cheetah::mma_attention_splits((int)a->batch, (int)a->kv_heads, sms)
+                   : cheetah::attention_splits((int)a->batch, (int)a->kv_heads,
+                                               (int)std::max<uint32_t>(1, a->max_seq_len), sms);
     p.scale = 1.0f / sqrtf((float)a->head_dim);
     p.out = a->out;
     const size_t parts = (size_t)a->batch * a->kv_heads * p.splits;
-    const size_t o_bytes = parts * cheetah::kMaxGroup * a->head_dim * 4;
-    const size_t ml_bytes = parts * cheetah::kMaxGroup * 2 * 4;
-    const size_t t_bytes = (size_t)a->batch * a->kv_heads * 4;
+    const size_t o_bytes = (parts * cheetah::kMaxGroup * a->head_dim * 4 + 255) & ~size_t(255);
+    const size_t ml_bytes = (parts * cheetah::kMaxGroup * 2 * 4 + 255) & ~size_t(255);
     uint8_t *scratch = nullptr;
-    CH_CUDA_TRY(cudaMallocAsync((void **)&scratch, o_bytes + ml_bytes + t_bytes + 512, st));
-    p.part_o = reinterpret_cast<float *>(scratch);
-    p.part_ml = reinterpret_cast<float *>(scratch + ((o_bytes + 255) & ~size_t(255)));
-    p.tickets = reinterpret_cast<unsigned int *>(scratch + ((o_bytes + 255) & ~size_t(255)) + ((ml_bytes + 255) & ~size_t(255)));
-    p.error = nullptr;
-    cudaError_t err = cudaMemsetAsync(p.tickets, 0, t_bytes, st);
-    int rc = 0;
-    if (err == cudaSuccess) {
-        rc = cheetah::launch_attention(p, (int)a->head_dim, a->kv_dtype == CHEETAH_CUDA_KV_F32, st, false);
+    unsigned int *tickets = nullptr;
+    if (op_scratch(device, st, o_bytes + ml_bytes, (size_t)a->batch * a->kv_heads, &scratch, &tickets) != 0) {
+        return -1;
     }
-    cudaFreeAsync(scratch, st);
-    CH_CUDA_TRY(err);
-    return rc;
+    p.part_o = reinterpret_cast<float *>(scratch);
+    p.part_ml = reinterpret_cast<float *>(scratch + o_bytes);
+    p.tickets = tickets;
+    p.error = nullptr;
+    if (!mma) return cheetah::launch_attention(p, (int)a->head_dim, a->kv_dtype == CHEETAH_CUDA_KV_F32, st, false);
+    CUtensorMap k_map, v_map;
+    const unsigned long long rows = (unsigned long long)a->num_pages * a->kv_heads * a->page_tokens;
+    if (cheetah::make_kv_tensor_map(&k_map, a->k_pool, rows, (int)a->head_dim) != 0 ||
+        cheetah::make_kv_tensor_map(&v_map, a->v_pool, rows, (int)a->head_dim) != 0) {
+        return -1;
+    }
+    cheetah::MmaAttnParams mp = {};
+    mp.a = p;
+    mp.layer_row_offset = 0;
+    mp.page_tokens = (int)a->page_tokens;
+    return cheetah::launch_attention_mma(k_map, v_map, mp, (int)a->head_dim, st, false);
 }
 
 }  // extern "C"

@@ -85,11 +85,18 @@ def make_paged_kv(B, L_list, kv_heads, D, page_tokens, kv_dtype, seed, extra_pag
     return kt, vt, torch.from_numpy(table).cuda(), dense
 
 
+# Tolerances: the CUDA-core kernel (f32 cache, or bf16 cache with the MMA
+# path switched off) computes in f32 — 1e-4; the tensor-core kernel rounds q
+# and the softmax weights to bf16 for the MMAs — the 1e-2 max-abs contract.
 @pytest.mark.parametrize("q_heads,kv_heads,D", [(14, 2, 64), (28, 4, 128)])
-@pytest.mark.parametrize("kv_dtype", ["bf16", "f32"])
+@pytest.mark.parametrize("kernel", ["mma", "cuda-core-bf16", "cuda-core-f32"])
 @pytest.mark.parametrize("L_list", [[1], [17], [64], [1000, 3], [4097, 65, 640]])
-def test_decode_attention_matches_oracle(q_heads, kv_heads, D, kv_dtype, L_list):
+def test_decode_attention_matches_oracle(q_heads, kv_heads, D, kernel, L_list, monkeypatch):
     from cheetah_b200 import runtime as R
+    kv_dtype = "f32" if kernel == "cuda-core-f32" else "bf16"
+    if kernel == "cuda-core-bf16":
+        monkeypatch.setenv("CHEETAH_CUDA_MMA_ATTENTION", "0")
+    tol = 1e-2 if kernel == "mma" else 1e-4
     B = len(L_list)
     kt, vt, table, dense = make_paged_kv(B, L_list, kv_heads, D, 64, kv_dtype, seed=sum(L_list) + D)
     rng = np.random.default_rng(11)
@@ -99,20 +106,21 @@ def test_decode_attention_matches_oracle(q_heads, kv_heads, D, kv_dtype, L_list)
     for b in range(B):
         ref = O.attention(dense[b][0], dense[b][1], q[b].reshape(-1), q_heads, kv_heads, D)
         err = np.abs(out[b].reshape(-1) - ref).max()
-        assert err < 1e-4, f"b={b} max err {err}"  # contract: 1e-2 max-abs
+        assert err < tol, f"b={b} max err {err}"
 
 
-def test_decode_attention_sliding_window():
+@pytest.mark.parametrize("kv_dtype", ["f32", "bf16"])
+def test_decode_attention_sliding_window(kv_dtype):
     from cheetah_b200 import runtime as R
     L, window = 700, 100
-    kt, vt, table, dense = make_paged_kv(1, [L], 2, 64, 64, "f32", seed=3)
+    kt, vt, table, dense = make_paged_kv(1, [L], 2, 64, 64, kv_dtype, seed=3)
     q = np.random.default_rng(4).standard_normal((1, 14, 64), dtype=np.float32)
     lens = torch.tensor([L], dtype=torch.int32, device="cuda")
     out = R.decode_attention(torch.from_numpy(q).cuda(), kt, vt, table, lens, L,
                              sliding_window=window).cpu().numpy()
     ref = O.attention(dense[0][0], dense[0][1], q[0].reshape(-1), 14, 2, 64, position=L - 1,
                       sliding_window=window)
-    assert np.abs(out[0].reshape(-1) - ref).max() < 1e-4
+    assert np.abs(out[0].reshape(-1) - ref).max() < (1e-4 if kv_dtype == "f32" else 1e-2)
 
 
 def test_decode_attention_full_size_sampled():
@@ -125,7 +133,7 @@ def test_decode_attention_full_size_sampled():
     out = R.decode_attention(torch.from_numpy(q).cuda(), kt, vt, table, lens, L).cpu().numpy()
     for b in (0, B - 1):
         ref = O.attention(dense[b][0], dense[b][1], q[b].reshape(-1), 14, 2, 64)
-        assert np.abs(out[b].reshape(-1) - ref).max() < 1e-4
+        assert np.abs(out[b].reshape(-1) - ref).max() < 1e-2
     # Linearity property over the whole batch: a repeated call is identical.
     again = R.decode_attention(torch.from_numpy(q).cuda(), kt, vt, table, lens, L).cpu().numpy()
     np.testing.assert_array_equal(out, again)
