@@ -28,8 +28,12 @@ enum GemvEpilogue : int {
 };
 
 struct GemvParams {
-    const uint16_t *w0;      // bf16 [rows, cols]
+    const uint16_t *w0;      // bf16 [rows, cols], or q8/q4 codes (reference layout rows)
     const uint16_t *w1;      // up_proj for kEpiSwiglu
+    long long row_stride;    // bytes between weight rows (q8/q4); 0 = cols * 2 (bf16)
+    const float *scale0;     // q8/q4 per-row scales of w0 (nullptr for bf16)
+    const float *scale1;     // q8/q4 per-row scales of w1
+    int wt;                  // WeightFormat of w0/w1
     int rows;                // output rows (for kEpiSwiglu: intermediate size)
     int cols;                // multiple of 8
     int batch;               // input vectors (NB template bound)
@@ -54,6 +58,7 @@ struct GemvParams {
     int kv_f32;              // 1: f32 cache, 0: bf16
     // kEpiLogits
     unsigned long long *argmax;  // [batch] packed (order key << 32 | index), nullable
+    int *error;                  // nullable: set when a bounded wait gives up
 };
 
 template <int NB>
@@ -123,6 +128,65 @@ __device__ __forceinline__ void store_kv(const GemvParams &p, int b, int kv_head
     }
 }
 
+// Epilogue for one output row pair of batch row b once the dot products
+// are known. row_b < 0: single row. kEpiQkv: (row_a, row_b) are the logical
+// rope partners (i, i + head_dim/2) of one head.
+template <int EPI>
+__device__ __forceinline__ void epilogue_rows(const GemvParams &p, int b, int row_a, int row_b, float acc_a,
+                                              float acc_b, unsigned long long &best) {
+    float *y = p.y + (long long)b * p.y_stride;
+    if (EPI == kEpiStore || EPI == kEpiResidual) {
+        float va = acc_a;
+        if (p.bias) va = __fadd_rn(va, p.bias[row_a]);
+        if (EPI == kEpiResidual) va = __fadd_rn(y[row_a], va);
+        y[row_a] = va;
+        if (row_b >= 0) {
+            float vb = acc_b;
+            if (p.bias) vb = __fadd_rn(vb, p.bias[row_b]);
+            if (EPI == kEpiResidual) vb = __fadd_rn(y[row_b], vb);
+            y[row_b] = vb;
+        }
+    } else if (EPI == kEpiSwiglu) {
+        y[row_a] = silu_mul(acc_a, acc_b);
+    } else if (EPI == kEpiLogits) {
+        y[row_a] = acc_a;
+        unsigned long long key = ((unsigned long long)total_order_key(acc_a) << 32) | (unsigned)row_a;
+        if (row_b >= 0) {
+            y[row_b] = acc_b;
+            unsigned long long kb = ((unsigned long long)total_order_key(acc_b) << 32) | (unsigned)row_b;
+            key = kb > key ? kb : key;
+        }
+        best = key > best ? key : best;
+    } else {  // kEpiQkv
+        const int hd = p.head_dim;
+        const int half = hd >> 1;
+        const int head = row_a / hd;
+        const int i = row_a - head * hd;
+        float va = __fadd_rn(acc_a, p.bias ? p.bias[row_a] : 0.0f);
+        float vb = __fadd_rn(acc_b, p.bias ? p.bias[row_b] : 0.0f);
+        if (head < p.q_heads + p.kv_heads) {
+            // ops.rs:693-715: a' = a*cos - b*sin, b' = b*cos + a*sin
+            const int pos = p.positions[b];
+            const float c = p.rope_cos[(long long)pos * half + i];
+            const float s = p.rope_sin[(long long)pos * half + i];
+            const float ra = __fsub_rn(__fmul_rn(va, c), __fmul_rn(vb, s));
+            const float rb = __fadd_rn(__fmul_rn(vb, c), __fmul_rn(va, s));
+            va = ra;
+            vb = rb;
+        }
+        if (head < p.q_heads) {
+            y[row_a] = va;
+            y[row_b] = vb;
+        } else if (head < p.q_heads + p.kv_heads) {
+            store_kv<1>(p, b, head - p.q_heads, i, va, true);
+            store_kv<1>(p, b, head - p.q_heads, i + half, vb, true);
+        } else {
+            store_kv<1>(p, b, head - p.q_heads - p.kv_heads, i, va, false);
+            store_kv<1>(p, b, head - p.q_heads - p.kv_heads, i + half, vb, false);
+        }
+    }
+}
+
 // Epilogue for one row group once the full dot products are known.
 template <int NB, int EPI>
 __device__ __forceinline__ void gemv_epilogue(const GemvParams &p, int group, const float *acc_a,
@@ -132,59 +196,95 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams &p, int group, co
 #pragma unroll
     for (int b = 0; b < NB; ++b) {
         if (b >= p.batch) break;
-        float *y = p.y + (long long)b * p.y_stride;
-        if (EPI == kEpiStore || EPI == kEpiResidual) {
-            float va = acc_a[b];
-            if (p.bias) va = __fadd_rn(va, p.bias[row_a]);
-            if (EPI == kEpiResidual) va = __fadd_rn(y[row_a], va);
-            y[row_a] = va;
-            if (row_b >= 0) {
-                float vb = acc_b[b];
-                if (p.bias) vb = __fadd_rn(vb, p.bias[row_b]);
-                if (EPI == kEpiResidual) vb = __fadd_rn(y[row_b], vb);
-                y[row_b] = vb;
-            }
-        } else if (EPI == kEpiSwiglu) {
-            y[row_a] = silu_mul(acc_a[b], acc_b[b]);
-        } else if (EPI == kEpiLogits) {
-            y[row_a] = acc_a[b];
-            unsigned long long key =
-                ((unsigned long long)total_order_key(acc_a[b]) << 32) | (unsigned)row_a;
-            if (row_b >= 0) {
-                y[row_b] = acc_b[b];
-                unsigned long long kb =
-                    ((unsigned long long)total_order_key(acc_b[b]) << 32) | (unsigned)row_b;
-                key = kb > key ? kb : key;
-            }
-            best[b] = key > best[b] ? key : best[b];
-        } else {  // kEpiQkv
-            const int hd = p.head_dim;
-            const int half = hd >> 1;
-            const int head = row_a / hd;
-            const int i = row_a - head * hd;
-            float va = __fadd_rn(acc_a[b], p.bias ? p.bias[row_a] : 0.0f);
-            float vb = __fadd_rn(acc_b[b], p.bias ? p.bias[row_b] : 0.0f);
-            if (head < p.q_heads + p.kv_heads) {
-                // ops.rs:693-715: a' = a*cos - b*sin, b' = b*cos + a*sin
-                const int pos = p.positions[b];
-                const float c = p.rope_cos[(long long)pos * half + i];
-                const float s = p.rope_sin[(long long)pos * half + i];
-                const float ra = __fsub_rn(__fmul_rn(va, c), __fmul_rn(vb, s));
-                const float rb = __fadd_rn(__fmul_rn(vb, c), __fmul_rn(va, s));
-                va = ra;
-                vb = rb;
-            }
-            if (head < p.q_heads) {
-                y[row_a] = va;
-                y[row_b] = vb;
-            } else if (head < p.q_heads + p.kv_heads) {
-                store_kv<NB>(p, b, head - p.q_heads, i, va, true);
-                store_kv<NB>(p, b, head - p.q_heads, i + half, vb, true);
-            } else {
-                store_kv<NB>(p, b, head - p.q_heads - p.kv_heads, i, va, false);
-                store_kv<NB>(p, b, head - p.q_heads - p.kv_heads, i + half, vb, false);
-            }
-        }
+        epilogue_rows<EPI>(p, b, row_a, EPI == kEpiSwiglu ? row_a : row_b, acc_a[b], acc_b[b], best[b]);
+    }
+}
+
+// Weight formats of the register-streaming GEMV. bf16: 128-bit vectors of 8
+// weights. q8 / q4 (`precision/q8.rs`, `precision/q4.rs` row layouts): 32-bit
+// words of 4 int8 / 8 int4 codes, unpacked in registers; the per-row scale
+// is applied once to the finished dot product.
+enum WeightFormat : int { kWBf16 = 0, kWQ8 = 1, kWQ4 = 2 };
+
+template <int WT>
+struct WeightTraits;
+
+template <>
+struct WeightTraits<kWBf16> {
+    using Vec = uint4;
+    static constexpr int kElems = 8;
+    static constexpr int kUnroll = 4;
+    static __device__ __forceinline__ Vec load(const Vec *p) { return ldg_stream(p); }
+    static __device__ __forceinline__ Vec zero() { return make_uint4(0, 0, 0, 0); }
+    static __device__ __forceinline__ void fma(float &acc, Vec w, const float *x) { fma8(acc, w, x); }
+};
+
+__device__ __forceinline__ uint32_t ldg_stream_u32(const uint32_t *ptr) {
+    uint32_t v;
+    asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(v) : "l"(ptr));
+    return v;
+}
+
+// int8 code -> exact float: (code + 128) in the low mantissa bits of 2^23.
+__device__ __forceinline__ float q8_code(uint32_t biased, int byte) {
+    return __uint_as_float(__byte_perm(biased, 0x4B000000u, 0x7440u + byte)) - 8388736.0f;
+}
+
+template <>
+struct WeightTraits<kWQ8> {
+    using Vec = uint32_t;
+    static constexpr int kElems = 4;
+    static constexpr int kUnroll = 8;
+    static __device__ __forceinline__ Vec load(const Vec *p) { return ldg_stream_u32(p); }
+    static __device__ __forceinline__ Vec zero() { return 0u; }
+    static __device__ __forceinline__ void fma(float &acc, Vec w, const float *x) {
+        const uint32_t b = w ^ 0x80808080u;
+        const float4 xv = *reinterpret_cast<const float4 *>(x);
+        acc = fmaf(q8_code(b, 0), xv.x, acc);
+        acc = fmaf(q8_code(b, 1), xv.y, acc);
+        acc = fmaf(q8_code(b, 2), xv.z, acc);
+        acc = fmaf(q8_code(b, 3), xv.w, acc);
+    }
+};
+
+// int4 code (low nibble = even column, `q4.rs:59-66`) -> exact float.
+__device__ __forceinline__ float q4_code(uint32_t biased, int nibble) {
+    return __uint_as_float(0x4B000000u | ((biased >> (4 * nibble)) & 0xFu)) - 8388616.0f;
+}
+
+template <>
+struct WeightTraits<kWQ4> {
+    using Vec = uint32_t;
+    static constexpr int kElems = 8;
+    static constexpr int kUnroll = 8;
+    static __device__ __forceinline__ Vec load(const Vec *p) { return ldg_stream_u32(p); }
+    static __device__ __forceinline__ Vec zero() { return 0u; }
+    static __device__ __forceinline__ void fma(float &acc, Vec w, const float *x) {
+        const uint32_t b = w ^ 0x88888888u;
+        const float4 x0 = *reinterpret_cast<const float4 *>(x);
+        const float4 x1 = *reinterpret_cast<const float4 *>(x + 4);
+        acc = fmaf(q4_code(b, 0), x0.x, acc);
+        acc = fmaf(q4_code(b, 1), x0.y, acc);
+        acc = fmaf(q4_code(b, 2), x0.z, acc);
+        acc = fmaf(q4_code(b, 3), x0.w, acc);
+        acc = fmaf(q4_code(b, 4), x1.x, acc);
+        acc = fmaf(q4_code(b, 5), x1.y, acc);
+        acc = fmaf(q4_code(b, 6), x1.z, acc);
+        acc = fmaf(q4_code(b, 7), x1.w, acc);
+    }
+};
+
+// Quantised rows: dot = scale[row] * sum(code * x).
+template <int NB, int EPI>
+__device__ __forceinline__ void apply_row_scales(const GemvParams &p, int group, float *acc_a, float *acc_b) {
+    int row_a, row_b;
+    group_rows<EPI>(p, group, row_a, row_b);
+    const float sa = p.scale0[row_a];
+    const float sb = EPI == kEpiSwiglu ? p.scale1[row_a] : (row_b >= 0 ? p.scale0[row_b] : 0.0f);
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+        acc_a[b] *= sa;
+        acc_b[b] *= sb;
     }
 }
 
@@ -193,8 +293,11 @@ constexpr int kGemvWarps = kGemvThreads / kWarp;
 constexpr int kGemvUnroll = 4;
 
 // Dynamic shared memory: x [NB][cols] f32, partials [warps][2][NB], argmax [warps][NB].
-template <int NB, int EPI, int KSPLIT>
+template <int NB, int EPI, int KSPLIT, int WT = kWBf16>
 __global__ void __launch_bounds__(kGemvThreads) gemv_bf16_kernel(const GemvParams p) {
+    using W = WeightTraits<WT>;
+    using Vec = typename W::Vec;
+    constexpr int kU = W::kUnroll;
     extern __shared__ __align__(16) float smem[];
     float *xs = smem;
     float *partial = smem + (size_t)NB * p.cols;
@@ -206,7 +309,8 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_bf16_kernel(const GemvParam
     constexpr int kGroupsPerCta = kGemvWarps / KSPLIT;
     const int group_in_cta = warp / KSPLIT;
     const int kslice = warp % KSPLIT;
-    const int nvec = p.cols >> 3;
+    const int nvec = p.cols / W::kElems;
+    const long long row_stride = p.row_stride ? p.row_stride : (long long)p.cols * 2;
     const int slice_len = (nvec + KSPLIT - 1) / KSPLIT;
     const int v_begin = kslice * slice_len;
     const int v_end = min(nvec, v_begin + slice_len);
@@ -220,22 +324,23 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_bf16_kernel(const GemvParam
     int group = blockIdx.x * kGroupsPerCta + group_in_cta;
 
     // Stage the first weight vectors before waiting on the previous kernel.
-    uint4 wa[kGemvUnroll], wb[kGemvUnroll];
+    Vec wa[kU], wb[kU];
     auto load_batch = [&](int g, int base) {
         int ra, rb;
         group_rows<EPI>(p, g, ra, rb);
-        const uint4 *pa = reinterpret_cast<const uint4 *>(p.w0) + (long long)ra * nvec;
+        const Vec *pa = reinterpret_cast<const Vec *>(reinterpret_cast<const uint8_t *>(p.w0) + (long long)ra * row_stride);
         const uint16_t *wsrc_b = (EPI == kEpiSwiglu) ? p.w1 : p.w0;
-        const uint4 *pb = reinterpret_cast<const uint4 *>(wsrc_b) + (long long)(rb < 0 ? ra : rb) * nvec;
+        const Vec *pb = reinterpret_cast<const Vec *>(reinterpret_cast<const uint8_t *>(wsrc_b) +
+                                                      (long long)(rb < 0 ? ra : rb) * row_stride);
 #pragma unroll
-        for (int u = 0; u < kGemvUnroll; ++u) {
+        for (int u = 0; u < kU; ++u) {
             const int v = base + u * kWarp + lane;
             if (v < v_end && g < groups) {
-                wa[u] = ldg_stream(pa + v);
-                wb[u] = ldg_stream(pb + v);
+                wa[u] = W::load(pa + v);
+                wb[u] = W::load(pb + v);
             } else {
-                wa[u] = make_uint4(0, 0, 0, 0);
-                wb[u] = make_uint4(0, 0, 0, 0);
+                wa[u] = W::zero();
+                wb[u] = W::zero();
             }
         }
     };
@@ -276,18 +381,18 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_bf16_kernel(const GemvParam
 #pragma unroll
         for (int b = 0; b < NB; ++b) acc_a[b] = acc_b[b] = 0.0f;
         const bool active = group < groups;
-        for (int base = v_begin; base < v_end; base += kWarp * kGemvUnroll) {
+        for (int base = v_begin; base < v_end; base += kWarp * kU) {
             if (base != v_begin) load_batch(group, base);
 #pragma unroll
-            for (int u = 0; u < kGemvUnroll; ++u) {
+            for (int u = 0; u < kU; ++u) {
                 const int v = base + u * kWarp + lane;
                 if (v < v_end) {
 #pragma unroll
                     for (int b = 0; b < NB; ++b) {
                         if (b < p.batch) {
-                            const float *xv = xs + (size_t)b * p.cols + (v << 3);
-                            fma8(acc_a[b], wa[u], xv);
-                            fma8(acc_b[b], wb[u], xv);
+                            const float *xv = xs + (size_t)b * p.cols + v * W::kElems;
+                            W::fma(acc_a[b], wa[u], xv);
+                            W::fma(acc_b[b], wb[u], xv);
                         }
                     }
                 }
@@ -323,10 +428,12 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_bf16_kernel(const GemvParam
                     acc_a[b] = sa;
                     acc_b[b] = sb;
                 }
+                if (WT != kWBf16) apply_row_scales<NB, EPI>(p, group, acc_a, acc_b);
                 gemv_epilogue<NB, EPI>(p, group, acc_a, acc_b, best);
             }
             __syncthreads();
         } else if (lane == 0 && active) {
+            if (WT != kWBf16) apply_row_scales<NB, EPI>(p, group, acc_a, acc_b);
             gemv_epilogue<NB, EPI>(p, group, acc_a, acc_b, best);
         }
     }

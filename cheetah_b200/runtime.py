@@ -87,6 +87,11 @@ SIGNATURES = {
     "cheetah_cuda_seq_export_kv": (_I, [_P, _S, _P, _P]),
     "cheetah_cuda_op_gemv_bf16": (_I, [_P, _S, _S, _P, _S, _P, _P]),
     "cheetah_cuda_op_decode_attention": (_I, [C.POINTER(DecodeAttentionArgs), _P]),
+    "cheetah_cuda_quant_buffer_bytes": (_I, [C.c_char_p, _S, _S, C.POINTER(_S)]),
+    "cheetah_cuda_op_quantize_q8": (_I, [_P, _S, _S, _P, _P]),
+    "cheetah_cuda_op_quantize_q4": (_I, [_P, _S, _S, _P, _P]),
+    "cheetah_cuda_op_gemv_q8": (_I, [_P, _S, _S, _P, _S, _P, _P]),
+    "cheetah_cuda_op_gemv_q4": (_I, [_P, _S, _S, _P, _S, _P, _P]),
 }
 
 _lib: Optional[C.CDLL] = None
@@ -295,6 +300,34 @@ def gemv_bf16(weight, x, stream=None):
     y = torch.empty(xb.shape[0], rows, dtype=torch.float32, device=x.device)
     _check(lib().cheetah_cuda_op_gemv_bf16(weight.data_ptr(), rows, cols, xb.data_ptr(),
                                            xb.shape[0], y.data_ptr(), _stream_ptr(stream)))
+    return y
+
+
+def quant_buffer_bytes(fmt: str, rows: int, cols: int) -> int:
+    n = C.c_size_t(0)
+    _check(lib().cheetah_cuda_quant_buffer_bytes(fmt.encode(), rows, cols, C.byref(n)))
+    return n.value
+
+
+def quantize(weight, fmt: str, stream=None):
+    """Per-row q8/q4 quantisation (`q8.rs:91`, `q4.rs:126`) of bf16 [rows, cols]
+    on the device; returns the uint8 buffer in the reference layout."""
+    import torch
+    assert weight.dtype == torch.bfloat16 and weight.is_cuda and weight.is_contiguous()
+    rows, cols = weight.shape
+    out = torch.empty(quant_buffer_bytes(fmt, rows, cols), dtype=torch.uint8, device=weight.device)
+    fn = lib().cheetah_cuda_op_quantize_q8 if fmt == "q8" else lib().cheetah_cuda_op_quantize_q4
+    _check(fn(weight.data_ptr(), rows, cols, out.data_ptr(), _stream_ptr(stream)))
+    return out
+
+
+def gemv_quant(buffer, fmt: str, rows: int, cols: int, x, stream=None):
+    """y = W . x over a q8/q4 reference-layout buffer (`ops.rs:544`, `:586`)."""
+    import torch
+    xb = x.reshape(-1, cols).contiguous()
+    y = torch.empty(xb.shape[0], rows, dtype=torch.float32, device=x.device)
+    fn = lib().cheetah_cuda_op_gemv_q8 if fmt == "q8" else lib().cheetah_cuda_op_gemv_q4
+    _check(fn(buffer.data_ptr(), rows, cols, xb.data_ptr(), xb.shape[0], y.data_ptr(), _stream_ptr(stream)))
     return y
 
 

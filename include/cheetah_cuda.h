@@ -143,6 +143,30 @@ CHEETAH_CUDA_API int cheetah_cuda_seq_export_kv(const CheetahCudaSeq *seq, size_
 CHEETAH_CUDA_API int cheetah_cuda_op_gemv_bf16(const void *weight, size_t rows, size_t cols, const float *x,
                               size_t batch, float *y, void *stream);
 
+/* Bytes of a q8 / q4 buffer in the reference interchange layout
+ * (`precision/q8.rs:8-21`, `precision/q4.rs:9-36`): rows f32 scales, then
+ * rows x row_bytes codes (q8 row_bytes = (cols+3)/4*4; q4 row_bytes =
+ * (cols+1).div_ceil(2).div_ceil(4)*4). `format` is "q8" or "q4". */
+CHEETAH_CUDA_API int cheetah_cuda_quant_buffer_bytes(const char *format, size_t rows, size_t cols, size_t *bytes);
+
+/* Per-row quantisation of bf16 weights [rows, cols] (device) into `out`
+ * (device, the reference layout above), bit-identical to `q8::quantize`
+ * (`precision/q8.rs:91`) / `q4::quantize` (`precision/q4.rs:126`) applied to
+ * the exactly widened values. */
+CHEETAH_CUDA_API int cheetah_cuda_op_quantize_q8(const void *weight, size_t rows, size_t cols, void *out,
+                                                 void *stream);
+CHEETAH_CUDA_API int cheetah_cuda_op_quantize_q4(const void *weight, size_t rows, size_t cols, void *out,
+                                                 void *stream);
+
+/* y[b] = W . x[b] over a q8 / q4 buffer in the reference layout (device):
+ * codes unpacked in registers, f32 accumulation, the row scale applied to the
+ * finished dot. cols % 8 == 0. Replaces `gemv_q8` / `gemv_q4` (`ops.rs:544`,
+ * `ops.rs:586`). */
+CHEETAH_CUDA_API int cheetah_cuda_op_gemv_q8(const void *buffer, size_t rows, size_t cols, const float *x,
+                                             size_t batch, float *y, void *stream);
+CHEETAH_CUDA_API int cheetah_cuda_op_gemv_q4(const void *buffer, size_t rows, size_t cols, const float *x,
+                                             size_t batch, float *y, void *stream);
+
 /* Paged GQA decode attention for `batch` sequences, one query position each
  * (the newest), over a paged KV pool. Replaces `OpsToolbox::attention` /
  * `attention_head` (`ops.rs:1357-1467`) for one position of every head. */

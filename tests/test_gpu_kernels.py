@@ -34,10 +34,12 @@ def _gemv_case(rows, cols, batch, seed):
         assert np.all(err <= 1e-6 * scale + 1e-7), f"max err {err.max()}"
 
 
+@pytest.mark.parametrize("kernel", ["bulk-prefetch", "register-stream"])
 @pytest.mark.parametrize("rows,cols", [(1152, 896), (896, 896), (4864, 896), (896, 4864),
                                        (151936, 896), (3584, 3584), (18944, 3584), (3584, 18944),
                                        (1, 8), (3, 24), (257, 40)])
-def test_gemv_bf16_matches_oracle(rows, cols):
+def test_gemv_bf16_matches_oracle(rows, cols, kernel, monkeypatch):
+    monkeypatch.setenv("CHEETAH_CUDA_TMA_GEMV", "1" if kernel == "bulk-prefetch" else "0")
     _gemv_case(rows, cols, 1, rows + cols)
 
 

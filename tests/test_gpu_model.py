@@ -171,3 +171,14 @@ def test_device_greedy_chain_equals_per_token_greedy(tiny_prepared):
     np.testing.assert_array_equal(va, vb)
     # The sequence keeps working after a chain (page table and positions).
     np.testing.assert_array_equal(a.forward([5], 73), b.forward([5], 73))
+
+
+def test_bulk_prefetch_gemv_decode_path(tiny_prepared, monkeypatch):
+    """The bulk-prefetch GEMV variant (pair-interleaved QKV rows) keeps parity."""
+    monkeypatch.setenv("CHEETAH_CUDA_TMA_GEMV", "1")
+    cfg, ref, model = _pair(tiny_prepared, "f32")
+    seq = model.new_sequence()
+    prompt = _tokens(20, cfg["vocab_size"], 12)
+    assert np.abs(seq.forward(prompt, 0) - ref.forward(prompt, 0)).max() < 1e-4
+    for i in range(5):
+        assert np.abs(seq.forward([i + 3], 20 + i) - ref.forward([i + 3], 20 + i)).max() < 1e-4
