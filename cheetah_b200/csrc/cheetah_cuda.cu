@@ -30,6 +30,8 @@
 #include "gemv_tma.cuh"
 #include "kernels_misc.cuh"
 #include "quant.cuh"
+#include "gemm_tcgen05.cuh"
+#include "prefill_attention.cuh"
 #include "store.h"
 
 namespace cheetah {
@@ -242,6 +244,24 @@ int make_kv_tensor_map(CUtensorMap *map, const void *base, unsigned long long ro
     return 0;
 }
 
+// 2D map over a bf16 row-major matrix [rows][cols]: 64-column x box_rows
+// boxes, 128-byte swizzle (the K-major UMMA operand layout).
+int make_bf16_tensor_map(CUtensorMap *map, const void *base, unsigned long long rows, unsigned long long cols,
+                         int box_rows) {
+    auto encode = tensor_map_encoder();
+    CH_REQUIRE(encode != nullptr, "CUDA backend: cuTensorMapEncodeTiled is unavailable");
+    CH_REQUIRE(((uintptr_t)base & 15) == 0 && (cols * 2) % 16 == 0, "CUDA backend: operand must be 16-byte aligned");
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+    cuuint32_t box[2] = {64u, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1u, 1u};
+    CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    CH_REQUIRE(r == CUDA_SUCCESS, "CUDA backend: cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+    return 0;
+}
+
 bool mma_attention_eligible(int head_dim, int page_tokens) {
     if (!env_flag("CHEETAH_CUDA_MMA_ATTENTION", true)) return false;
     if (head_dim != 64 && head_dim != 128) return false;
@@ -285,6 +305,8 @@ struct LayerWeights {
     const uint16_t *wup = nullptr;
     const uint16_t *wdown = nullptr;
     QuantMatrix qqkv, qo, qgate, qup, qdown;
+    // Tensor maps of the bf16 linears for the prefill GEMMs.
+    CUtensorMap map_qkv{}, map_o{}, map_gate{}, map_up{}, map_down{};
     const float *ln1 = nullptr;
     const float *ln2 = nullptr;
     const float *bqkv = nullptr;
@@ -317,6 +339,7 @@ struct Model {
     int kv_f32 = 0;
     bool use_mma_attention = false;
     bool qkv_interleaved = false;  // QKV rows stored pair-interleaved (bulk-prefetch GEMV)
+    bool gemm_prefill = false;     // bf16 weights with tensor maps: tensor-core chunked prefill
     CUtensorMap k_map{};
     CUtensorMap v_map{};
     std::mutex pool_mutex;
@@ -378,6 +401,13 @@ struct Seq {
     int mma_splits = 1;
     int scratch_splits = 1;
     int32_t *token_log = nullptr;
+    // Chunked-prefill buffers (allocated on the first prompt): token ids,
+    // f32 residual rows, bf16 normed / q / attention / SwiGLU rows.
+    int chunk_cap = 0;
+    int32_t *ptokens = nullptr;
+    float *phid = nullptr;
+    uint16_t *pxb = nullptr, *pqb = nullptr, *pab = nullptr, *pact = nullptr;
+    CUtensorMap map_xb{}, map_ab{}, map_act{};
     cudaGraphExec_t graph = nullptr;
     cudaGraphExec_t chain_graph = nullptr;
 
@@ -387,6 +417,12 @@ struct Seq {
         if (graph) cudaGraphExecDestroy(graph);
         if (chain_graph) cudaGraphExecDestroy(chain_graph);
         cudaFree(token_log);
+        cudaFree(ptokens);
+        cudaFree(phid);
+        cudaFree(pxb);
+        cudaFree(pqb);
+        cudaFree(pab);
+        cudaFree(pact);
         if (stream) cudaStreamDestroy(stream);
         cudaFree(page_table);
         cudaFree(hidden);
@@ -903,6 +939,25 @@ int open_model(const char *prepared_dir, const CheetahCudaConfig *config, const 
 
     cudaFree(staging);
 
+    // Prefill GEMM operands (bf16 models with the standard QKV row order).
+    bool weight_maps_ok = false;
+    if (wfmt == kWBf16 && !m->qkv_interleaved && env_flag("CHEETAH_CUDA_GEMM_PREFILL", true)) {
+        bool ok = true;
+        for (uint32_t layer = 0; layer < c.num_layers && ok; ++layer) {
+            LayerWeights &w = m->layers[layer];
+            ok = make_bf16_tensor_map(&w.map_qkv, w.wqkv, QD + 2 * KD, H, kGemmBM) == 0 &&
+                 make_bf16_tensor_map(&w.map_o, w.wo, H, QD, kGemmBM) == 0 &&
+                 make_bf16_tensor_map(&w.map_gate, w.wgate, I, H, kGemmBM / 2) == 0 &&
+                 make_bf16_tensor_map(&w.map_up, w.wup, I, H, kGemmBM / 2) == 0 &&
+                 make_bf16_tensor_map(&w.map_down, w.wdown, H, I, kGemmBM) == 0;
+        }
+        if (!ok) {
+            delete m;
+            return -1;
+        }
+        weight_maps_ok = true;
+    }
+
     // Rotary table.
     std::vector<float> cos_t, sin_t;
     build_rope_table((int)c.max_positions, (int)c.head_dim, c.rope_theta, cos_t, sin_t);
@@ -934,6 +989,8 @@ int open_model(const char *prepared_dir, const CheetahCudaConfig *config, const 
         }
         m->use_mma_attention = true;
     }
+    // Tensor-core chunked prefill needs the bf16 weight maps and the bf16 KV maps.
+    m->gemm_prefill = weight_maps_ok && m->use_mma_attention && (c.head_dim == 64 || c.head_dim == 128);
     m->free_pages.reserve(m->num_pages);
     for (int i = m->num_pages - 1; i >= 0; --i) m->free_pages.push_back(i);
     err = cudaDeviceSynchronize();
@@ -991,6 +1048,10 @@ int new_seq(Model *m, Seq **out) {
     return 0;
 }
 
+int prefill_chunk_rows();
+int run_prefill_chunk(Seq &s, const uint32_t *tokens, int M, size_t offset, bool last);
+int check_device_error(Seq &s);
+
 int forward(Seq *s, const uint32_t *tokens, size_t n, size_t offset, float *logits_out,
             uint32_t *argmax_out) {
     CH_REQUIRE(s != nullptr, "cheetah_cuda_forward: null sequence");
@@ -1010,9 +1071,18 @@ int forward(Seq *s, const uint32_t *tokens, size_t n, size_t offset, float *logi
                "CUDA backend: position " + std::to_string(offset + n - 1) +
                    " exceeds the sequence capacity " + std::to_string(c.max_positions) + ".");
     CH_CUDA_TRY(cudaSetDevice(s->m->device));
-    for (size_t i = 0; i < n; ++i) {
-        if (run_decode_step(*s, tokens[i], offset + i) != 0) return -1;
-        if (i + 1 < n) CH_CUDA_TRY(cudaStreamSynchronize(s->stream));  // h_step is reused
+    const bool chunked = n > 1 && s->m->gemm_prefill && std::getenv("CHEETAH_CUDA_STEPWISE_PREFILL") == nullptr;
+    if (chunked) {
+        const size_t chunk = (size_t)prefill_chunk_rows();
+        for (size_t start = 0; start < n; start += chunk) {
+            const size_t rows = std::min(chunk, n - start);
+            if (run_prefill_chunk(*s, tokens + start, (int)rows, offset + start, start + rows == n) != 0) return -1;
+        }
+    } else {
+        for (size_t i = 0; i < n; ++i) {
+            if (run_decode_step(*s, tokens[i], offset + i) != 0) return -1;
+            if (i + 1 < n) CH_CUDA_TRY(cudaStreamSynchronize(s->stream));  // h_step is reused
+        }
     }
     if (logits_out) {
         CH_CUDA_TRY(cudaMemcpyAsync(s->h_logits, s->logits, (size_t)c.vocab_size * 4,
@@ -1022,8 +1092,221 @@ int forward(Seq *s, const uint32_t *tokens, size_t n, size_t offset, float *logi
         CH_CUDA_TRY(cudaMemcpyAsync(s->h_argmax, s->argmax, 8, cudaMemcpyDeviceToHost, s->stream));
     }
     CH_CUDA_TRY(cudaStreamSynchronize(s->stream));
+    if (check_device_error(*s) != 0) return -1;
     if (logits_out) memcpy(logits_out, s->h_logits, (size_t)c.vocab_size * 4);
     if (argmax_out) *argmax_out = (uint32_t)(*s->h_argmax & 0xFFFFFFFFull);
+    return 0;
+}
+
+// Allocate pages so positions [0, end) are backed; new entries are written
+// to the device page table.
+int ensure_pages_upto(Seq &s, size_t end) {
+    const size_t need = (end + s.m->page_tokens - 1) / s.m->page_tokens;
+    if (need > (size_t)s.max_pages) {
+        set_error("CUDA backend: position " + std::to_string(end - 1) + " exceeds the sequence capacity " +
+                  std::to_string(s.m->cfg.max_positions) + ".");
+        return -1;
+    }
+    const size_t first = s.pages.size();
+    while (s.pages.size() < need) {
+        const int page = s.m->alloc_page();
+        if (page < 0) {
+            set_error("CUDA backend: KV page pool exhausted (raise kv_pool_tokens).");
+            return -1;
+        }
+        s.pages.push_back(page);
+    }
+    if (need > first) {
+        std::vector<int32_t> ids(s.pages.begin() + first, s.pages.end());
+        CH_CUDA_TRY(cudaMemcpyAsync(s.page_table + first, ids.data(), ids.size() * 4, cudaMemcpyHostToDevice, s.stream));
+        CH_CUDA_TRY(cudaStreamSynchronize(s.stream));
+    }
+    return 0;
+}
+
+int prefill_chunk_rows() {
+    const char *env = std::getenv("CHEETAH_PREFILL_CHUNK");  // ops.rs:523-535 (default 256)
+    const int v = env ? std::atoi(env) : 0;
+    return v > 0 ? v : 256;
+}
+
+int ensure_prefill_buffers(Seq &s, int rows) {
+    if (rows <= s.chunk_cap) return 0;
+    Model &m = *s.m;
+    const CheetahCudaConfig &c = m.cfg;
+    const size_t H = c.hidden_size, I = c.intermediate_size, QD = (size_t)c.q_heads * c.head_dim;
+    cudaFree(s.ptokens);
+    cudaFree(s.phid);
+    cudaFree(s.pxb);
+    cudaFree(s.pqb);
+    cudaFree(s.pab);
+    cudaFree(s.pact);
+    s.chunk_cap = 0;
+    const size_t R = (size_t)rows;
+    bool ok = cudaMalloc(&s.ptokens, R * 4) == cudaSuccess && cudaMalloc(&s.phid, R * H * 4) == cudaSuccess &&
+              cudaMalloc(&s.pxb, R * H * 2) == cudaSuccess && cudaMalloc(&s.pqb, R * QD * 2) == cudaSuccess &&
+              cudaMalloc(&s.pab, R * QD * 2) == cudaSuccess && cudaMalloc(&s.pact, R * I * 2) == cudaSuccess;
+    if (!ok) {
+        set_error("CUDA backend: prefill buffer allocation failed.");
+        return -1;
+    }
+    if (make_bf16_tensor_map(&s.map_xb, s.pxb, R, H, kGemmBM) != 0 ||
+        make_bf16_tensor_map(&s.map_ab, s.pab, R, QD, kGemmBM) != 0 ||
+        make_bf16_tensor_map(&s.map_act, s.pact, R, I, kGemmBM) != 0) {
+        return -1;
+    }
+    s.chunk_cap = rows;
+    return 0;
+}
+
+template <int EPI>
+int launch_prefill_gemm(const CUtensorMap &a, const CUtensorMap &b, const CUtensorMap &b2, const PrefillGemmParams &p,
+                        cudaStream_t st, bool pdl) {
+    auto kernel = prefill_gemm_kernel<EPI, 128>;
+    const size_t smem = prefill_gemm_smem<128>();
+    CH_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    const int n_tiles = EPI == kPgSwiglu ? (p.N + 63) / 64 : (p.N + 127) / 128;
+    dim3 grid(n_tiles, (p.M + kGemmBM - 1) / kGemmBM);
+    CH_CUDA_TRY(launch_ex(kernel, grid, dim3(kGemmThreads), smem, st, pdl, a, b, b2, p));
+    return 0;
+}
+
+// One prompt chunk through every layer on the tensor cores
+// (`Qwen2Native::forward_chunk`, `qwen2.rs:208-233`): embeddings, then per
+// layer norm -> QKV GEMM (+bias, RoPE, KV append) -> causal attention ->
+// o_proj GEMM (+bias, residual) -> norm -> gate/up GEMM (SwiGLU) -> down
+// GEMM (residual). With `last`, the final row's norm + lm_head follow.
+int run_prefill_chunk(Seq &s, const uint32_t *tokens, int M, size_t offset, bool last) {
+    Model &m = *s.m;
+    const CheetahCudaConfig &c = m.cfg;
+    const int H = c.hidden_size, I = c.intermediate_size, QD = c.q_heads * c.head_dim, KD = c.kv_heads * c.head_dim;
+    const bool pdl = m.pdl;
+    cudaStream_t st = s.stream;
+    if (ensure_prefill_buffers(s, std::max(M, prefill_chunk_rows())) != 0) return -1;
+    if (ensure_pages_upto(s, offset + M) != 0) return -1;
+    std::vector<int32_t> ids(tokens, tokens + M);
+    CH_CUDA_TRY(cudaMemcpyAsync(s.ptokens, ids.data(), (size_t)M * 4, cudaMemcpyHostToDevice, st));
+    CH_CUDA_TRY(launch_ex(embed_rows_kernel, dim3(M), dim3(256), 0, st, pdl, m.embed, H, (const int32_t *)s.ptokens, M,
+                          s.phid));
+    for (uint32_t layer = 0; layer < c.num_layers; ++layer) {
+        const LayerWeights &w = m.layers[layer];
+        uint8_t *k_layer = m.k_pool + layer * m.layer_stride_bytes;
+        uint8_t *v_layer = m.v_pool + layer * m.layer_stride_bytes;
+        CH_CUDA_TRY(launch_ex(norm_rows_bf16_kernel, dim3(M), dim3(256), 0, st, pdl, (const float *)s.phid, M, H,
+                              w.ln1, c.rms_eps, s.pxb));
+        PrefillGemmParams g = {};
+        g.M = M;
+        g.N = QD + 2 * KD;
+        g.K = H;
+        g.bias = w.bqkv;
+        g.out_bf16 = s.pqb;
+        g.ld_out = QD;
+        g.q_heads = c.q_heads;
+        g.kv_heads = c.kv_heads;
+        g.head_dim = c.head_dim;
+        g.offset = (int)offset;
+        g.rope_cos = m.rope_cos;
+        g.rope_sin = m.rope_sin;
+        g.page_table = s.page_table;
+        g.max_pages = s.max_pages;
+        g.num_pages = m.num_pages;
+        g.page_tokens = m.page_tokens;
+        g.k_cache = k_layer;
+        g.v_cache = v_layer;
+        g.kv_f32 = m.kv_f32;
+        g.error = s.d_error;
+        if (launch_prefill_gemm<kPgQkv>(s.map_xb, w.map_qkv, w.map_qkv, g, st, pdl) != 0) return -1;
+
+        PrefillAttnParams ap = {};
+        ap.q = s.pqb;
+        ap.out = s.pab;
+        ap.T = M;
+        ap.offset = (int)offset;
+        ap.q_heads = c.q_heads;
+        ap.kv_heads = c.kv_heads;
+        ap.page_table = s.page_table;
+        ap.max_pages = s.max_pages;
+        ap.num_pages = m.num_pages;
+        ap.page_tokens = m.page_tokens;
+        ap.layer_row_offset = (long long)layer * m.num_pages * c.kv_heads * m.page_tokens;
+        ap.window = c.sliding_window;
+        ap.scale = 1.0f / sqrtf((float)c.head_dim);
+        ap.error = s.d_error;
+        const size_t asmem = prefill_attention_smem();
+        dim3 agrid((M + 15) / 16, c.kv_heads);
+        if (c.head_dim == 64) {
+            CH_CUDA_TRY(cudaFuncSetAttribute(prefill_attention_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)asmem));
+            CH_CUDA_TRY(launch_ex(prefill_attention_kernel<64>, agrid, dim3(kPrefillWarps * kWarp), asmem, st, pdl,
+                                  m.k_map, m.v_map, ap));
+        } else {
+            CH_CUDA_TRY(cudaFuncSetAttribute(prefill_attention_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)asmem));
+            CH_CUDA_TRY(launch_ex(prefill_attention_kernel<128>, agrid, dim3(kPrefillWarps * kWarp), asmem, st, pdl,
+                                  m.k_map, m.v_map, ap));
+        }
+
+        PrefillGemmParams o = {};
+        o.M = M;
+        o.N = H;
+        o.K = QD;
+        o.bias = w.bo;
+        o.out_f32 = s.phid;
+        o.ld_out = H;
+        o.error = s.d_error;
+        if (launch_prefill_gemm<kPgResidual>(s.map_ab, w.map_o, w.map_o, o, st, pdl) != 0) return -1;
+
+        CH_CUDA_TRY(launch_ex(norm_rows_bf16_kernel, dim3(M), dim3(256), 0, st, pdl, (const float *)s.phid, M, H,
+                              w.ln2, c.rms_eps, s.pxb));
+        PrefillGemmParams gu = {};
+        gu.M = M;
+        gu.N = I;
+        gu.K = H;
+        gu.out_bf16 = s.pact;
+        gu.ld_out = I;
+        gu.error = s.d_error;
+        if (launch_prefill_gemm<kPgSwiglu>(s.map_xb, w.map_gate, w.map_up, gu, st, pdl) != 0) return -1;
+
+        PrefillGemmParams dn = {};
+        dn.M = M;
+        dn.N = H;
+        dn.K = I;
+        dn.out_f32 = s.phid;
+        dn.ld_out = H;
+        dn.error = s.d_error;
+        if (launch_prefill_gemm<kPgResidual>(s.map_act, w.map_down, w.map_down, dn, st, pdl) != 0) return -1;
+    }
+    if (last) {
+        CH_CUDA_TRY(cudaMemsetAsync(s.argmax, 0, 8, st));
+        GemvParams lm = {};
+        lm.w0 = m.lm_head;
+        lm.rows = c.vocab_size;
+        lm.cols = H;
+        lm.batch = 1;
+        lm.x = s.phid + (size_t)(M - 1) * H;
+        lm.x_stride = H;
+        lm.norm_w = m.final_norm;
+        lm.eps = c.rms_eps;
+        lm.y = s.logits;
+        lm.y_stride = c.vocab_size;
+        lm.argmax = s.argmax;
+        if (run_gemv<kEpiLogits>(lm, st, pdl, m.sms) != 0) return -1;
+    }
+    s.positions = offset + M;
+    return 0;
+}
+
+// Device-side guards (bounded waits, page-table checks) record a code in the
+// sequence's error word; report and clear it after each synchronising call.
+int check_device_error(Seq &s) {
+    int code = 0;
+    CH_CUDA_TRY(cudaMemcpy(&code, s.d_error, 4, cudaMemcpyDeviceToHost));
+    if (code != 0) {
+        cudaMemset(s.d_error, 0, 4);
+        set_error("CUDA backend: device-side guard tripped (code " + std::to_string(code) +
+                  "): a bounded wait timed out or a KV page id was out of range.");
+        return -1;
+    }
     return 0;
 }
 

@@ -1,0 +1,314 @@
+// Chunked-prefill linear layers on the 5th-generation tensor cores.
+//
+// D[M, N] = A[M, K] . B[N, K]^T with A the chunk's bf16 activations (rows =
+// tokens) and B a layer's bf16 weights (rows = output features), both
+// K-major — the batched form of `ops::gemm` (`ops.rs:308-354`, the per-row
+// dot of `dot_row_bf16_avx2`) with the activations rounded to bf16 for the
+// tensor cores (f32 accumulation; tolerance-checked against the f32 oracle).
+//
+// One CTA per 128 x BN output tile, warp-specialised:
+//   warp 0      TMA producer: 128x64 A and BNx64 B boxes (128-byte swizzle,
+//               no multicast) into a kStages-deep shared-memory ring;
+//   warp 1      allocates BN TMEM columns; lane 0 issues tcgen05.mma
+//               (kind::f16, M=128, N=BN, K=16 per instruction, f32
+//               accumulators in TMEM) and tcgen05.commit to free each stage;
+//   warps 2-5   epilogue: tcgen05.ld of the accumulator rows (warp w reads
+//               TMEM lanes 32*(w%4)..+31 = tile rows), fused epilogue, global
+//               stores.
+// All mbarrier waits are bounded (error flag + early exit, TMEM freed).
+// Fused epilogues:
+//   kPgQkv      + bias, rotate-half RoPE (`ops.rs:693-715`, host rotary
+//               table), q rows -> bf16, K/V rows -> the paged cache
+//               (`ops.rs:1329` cache_append);
+//   kPgResidual + bias, then residual add into the f32 hidden rows
+//               (`qwen2.rs:442-463`);
+//   kPgSwiglu   B tile = 64 gate rows || 64 up rows; silu(g) * u
+//               (`ops.rs:743`) -> bf16.
+#pragma once
+
+#include <cuda.h>
+
+#include "common.cuh"
+#include "tma.cuh"
+
+namespace cheetah {
+
+enum PrefillEpilogue : int { kPgQkv = 0, kPgResidual = 1, kPgSwiglu = 2 };
+
+constexpr int kGemmBM = 128;
+constexpr int kGemmBK = 64;
+constexpr int kGemmStages = 4;
+constexpr int kGemmThreads = 192;
+
+struct PrefillGemmParams {
+    int M, N, K;              // N counts output features (kPgSwiglu: intermediate size)
+    // epilogue inputs
+    const float *bias;        // [N] or nullptr
+    float *out_f32;           // kPgResidual: hidden [M][ld_out]
+    uint16_t *out_bf16;       // kPgQkv: q [M][q_dim]; kPgSwiglu: act [M][N]
+    int ld_out;
+    // kPgQkv
+    int q_heads, kv_heads, head_dim;
+    int offset;               // absolute position of row 0
+    const float *rope_cos, *rope_sin;  // [max_positions][head_dim/2]
+    const int32_t *page_table;
+    int max_pages, num_pages, page_tokens;
+    void *k_cache, *v_cache;  // this layer's pool base
+    int kv_f32;
+    int *error;
+};
+
+__device__ __forceinline__ uint64_t umma_smem_desc(uint32_t addr) {
+    // K-major, 128-byte swizzle: 8-row atoms of 128 B (SBO = 1024 B), LBO
+    // unused (1), descriptor version 1, layout type 2 (SWIZZLE_128B).
+    uint64_t desc = 0;
+    desc |= (uint64_t)((addr >> 4) & 0x3FFF);
+    desc |= (uint64_t)1 << 16;
+    desc |= (uint64_t)(1024 >> 4) << 32;
+    desc |= (uint64_t)1 << 46;
+    desc |= (uint64_t)2 << 61;
+    return desc;
+}
+
+// Instruction descriptor: kind::f16, A = B = bf16, D = f32, both K-major.
+__host__ __device__ constexpr uint32_t umma_idesc_bf16(int m, int n) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(tmem_d), "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void store_kv_row(const PrefillGemmParams &p, int pos, int kv_head, int d, float value,
+                                             bool is_k) {
+    const int pidx = pos / p.page_tokens;
+    if (pos < 0 || pidx >= p.max_pages) return;
+    const int page = p.page_table[pidx];
+    if (page < 0 || page >= p.num_pages) return;
+    const long long index =
+        (((long long)page * p.kv_heads + kv_head) * p.page_tokens + (pos - pidx * p.page_tokens)) * p.head_dim + d;
+    void *base = is_k ? p.k_cache : p.v_cache;
+    if (p.kv_f32) static_cast<float *>(base)[index] = value;
+    else static_cast<uint16_t *>(base)[index] = f32_to_bf16_rne(value);
+}
+
+template <int EPI, int BN>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    prefill_gemm_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant__ CUtensorMap b_map,
+                        const __grid_constant__ CUtensorMap b2_map, const PrefillGemmParams p) {
+    constexpr int kABytes = kGemmBM * kGemmBK * 2;  // 16 KB
+    constexpr int kBBytes = BN * kGemmBK * 2;
+    constexpr int kStageBytes = kABytes + kBBytes;
+    constexpr uint32_t kIdesc = umma_idesc_bf16(kGemmBM, BN);
+    extern __shared__ __align__(1024) uint8_t gsmem[];
+    __shared__ __align__(8) uint64_t full_bar[kGemmStages];
+    __shared__ __align__(8) uint64_t empty_bar[kGemmStages];
+    __shared__ __align__(8) uint64_t done_bar;
+    __shared__ uint32_t tmem_base_s;
+    __shared__ int abort_s;
+
+    uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(gsmem) + 1023) & ~uintptr_t(1023));
+    const int warp = threadIdx.x / kWarp;
+    const int lane = threadIdx.x % kWarp;
+    const int n_tile = blockIdx.x;
+    const int m_tile = blockIdx.y;
+    const int k_blocks = (p.K + kGemmBK - 1) / kGemmBK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kGemmStages; ++s) {
+            mbar_init(smem_u32(&full_bar[s]), 1);
+            mbar_init(smem_u32(&empty_bar[s]), 1);
+        }
+        mbar_init(smem_u32(&done_bar), 1);
+        abort_s = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_s)),
+                     "r"((uint32_t)BN));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_base_s;
+
+    pdl_wait();
+    pdl_launch_dependents();
+
+    if (warp == 0) {
+        if (lane == 0) {
+            for (int kb = 0; kb < k_blocks; ++kb) {
+                const int s = kb % kGemmStages;
+                const uint32_t round = kb / kGemmStages;
+                if (!mbar_wait(smem_u32(&empty_bar[s]), (round & 1) ^ 1)) {
+                    abort_s = 1;
+                    break;
+                }
+                uint8_t *a_dst = base + s * kStageBytes;
+                uint8_t *b_dst = a_dst + kABytes;
+                const uint32_t bar = smem_u32(&full_bar[s]);
+                mbar_expect_tx(bar, kStageBytes);
+                tma_load_2d(smem_u32(a_dst), &a_map, kb * kGemmBK, m_tile * kGemmBM, bar);
+                if (EPI == kPgSwiglu) {
+                    tma_load_2d(smem_u32(b_dst), &b_map, kb * kGemmBK, n_tile * (BN / 2), bar);
+                    tma_load_2d(smem_u32(b_dst + kBBytes / 2), &b2_map, kb * kGemmBK, n_tile * (BN / 2), bar);
+                } else {
+                    tma_load_2d(smem_u32(b_dst), &b_map, kb * kGemmBK, n_tile * BN, bar);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            for (int kb = 0; kb < k_blocks; ++kb) {
+                const int s = kb % kGemmStages;
+                const uint32_t round = kb / kGemmStages;
+                if (!mbar_wait(smem_u32(&full_bar[s]), round & 1)) {
+                    abort_s = 1;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t a_addr = smem_u32(base + s * kStageBytes);
+                const uint32_t b_addr = a_addr + kABytes;
+#pragma unroll
+                for (int k = 0; k < kGemmBK / 16; ++k) {
+                    umma_bf16(tmem, umma_smem_desc(a_addr + k * 32), umma_smem_desc(b_addr + k * 32), kIdesc,
+                              (kb > 0 || k > 0) ? 1u : 0u);
+                }
+                umma_commit(smem_u32(&empty_bar[s]));
+            }
+            umma_commit(smem_u32(&done_bar));
+        }
+    } else {
+        // Epilogue warps 2..5: TMEM lane quadrant = warp % 4.
+        const int quad = warp % 4;
+        const int row = m_tile * kGemmBM + quad * 32 + lane;
+        const bool ok = mbar_wait(smem_u32(&done_bar), 0);
+        tc_fence_after();
+        if (!ok) {
+            if (p.error) *p.error = 4;
+        } else {
+            const uint32_t lane_addr = tmem + ((uint32_t)(quad * 32) << 16);
+            const bool live = row < p.M;
+            if (EPI == kPgResidual) {
+#pragma unroll 1
+                for (int c0 = 0; c0 < BN; c0 += 16) {
+                    float v[16];
+                    tmem_ld16(lane_addr + c0, v);
+                    const int n0 = n_tile * BN + c0;
+                    if (live) {
+                        float *dst = p.out_f32 + (long long)row * p.ld_out + n0;
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {
+                            if (n0 + i < p.N) {
+                                float val = v[i];
+                                if (p.bias) val = __fadd_rn(val, p.bias[n0 + i]);
+                                dst[i] = __fadd_rn(dst[i], val);
+                            }
+                        }
+                    }
+                }
+            } else if (EPI == kPgSwiglu) {
+#pragma unroll 1
+                for (int c0 = 0; c0 < BN / 2; c0 += 16) {
+                    float g[16], u[16];
+                    tmem_ld16(lane_addr + c0, g);
+                    tmem_ld16(lane_addr + BN / 2 + c0, u);
+                    const int n0 = n_tile * (BN / 2) + c0;
+                    if (live) {
+                        uint16_t *dst = p.out_bf16 + (long long)row * p.ld_out + n0;
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {
+                            if (n0 + i < p.N) {
+                                const float a = __fmul_rn(g[i], __fdiv_rn(u[i], __fadd_rn(1.0f, expf(-g[i]))));
+                                dst[i] = f32_to_bf16_rne(a);
+                            }
+                        }
+                    }
+                }
+            } else {  // kPgQkv: BN covers whole heads
+                const int hd = p.head_dim;
+                const int half = hd >> 1;
+                const int pos = p.offset + row;
+#pragma unroll 1
+                for (int hb = 0; hb < BN; hb += hd) {
+                    const int col0 = n_tile * BN + hb;  // first output feature of this head
+                    const int head = col0 / hd;
+#pragma unroll 1
+                    for (int j = 0; j < half; j += 16) {
+                        float a[16], b[16];
+                        tmem_ld16(lane_addr + hb + j, a);
+                        tmem_ld16(lane_addr + hb + half + j, b);
+                        if (!live || col0 >= p.N) continue;
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {
+                            const int d = j + i;
+                            float va = a[i], vb = b[i];
+                            if (p.bias) {
+                                va = __fadd_rn(va, p.bias[col0 + d]);
+                                vb = __fadd_rn(vb, p.bias[col0 + half + d]);
+                            }
+                            if (head < p.q_heads + p.kv_heads) {
+                                const float c = p.rope_cos[(long long)pos * half + d];
+                                const float s = p.rope_sin[(long long)pos * half + d];
+                                const float ra = __fsub_rn(__fmul_rn(va, c), __fmul_rn(vb, s));
+                                const float rb = __fadd_rn(__fmul_rn(vb, c), __fmul_rn(va, s));
+                                va = ra;
+                                vb = rb;
+                            }
+                            if (head < p.q_heads) {
+                                uint16_t *q = p.out_bf16 + (long long)row * p.ld_out + head * hd;
+                                q[d] = f32_to_bf16_rne(va);
+                                q[d + half] = f32_to_bf16_rne(vb);
+                            } else if (head < p.q_heads + p.kv_heads) {
+                                store_kv_row(p, pos, head - p.q_heads, d, va, true);
+                                store_kv_row(p, pos, head - p.q_heads, d + half, vb, true);
+                            } else {
+                                store_kv_row(p, pos, head - p.q_heads - p.kv_heads, d, va, false);
+                                store_kv_row(p, pos, head - p.q_heads - p.kv_heads, d + half, vb, false);
+                            }
+                        }
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (abort_s && threadIdx.x == 0 && p.error) *p.error = 5;
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)BN));
+    }
+}
+
+template <int BN>
+constexpr size_t prefill_gemm_smem() {
+    return (size_t)kGemmStages * (kGemmBM * kGemmBK * 2 + BN * kGemmBK * 2) + 1024;
+}
+
+}  // namespace cheetah

@@ -73,7 +73,9 @@ def test_kv_cache_matches_oracle(tiny_prepared):
 
 def test_continuation_snapshot_clone_and_clear_are_exact(tiny_prepared):
     # decoder.rs:1710 (continuation), :1795 (snapshot/restore), :1761 (clone),
-    # :1733 (clear) — bit-exact on the device, which is deterministic.
+    # :1733 (clear). Prompt rows take the tensor-core path and single tokens
+    # the GEMV path, so prompt-vs-decode continuation agrees to tolerance;
+    # every path is deterministic per row, so the rest is bit-exact.
     cfg, _, model = _pair(tiny_prepared, "bf16")
     toks = _tokens(90, cfg["vocab_size"], 5)
     a = model.new_sequence()
@@ -83,7 +85,7 @@ def test_continuation_snapshot_clone_and_clear_are_exact(tiny_prepared):
     b.forward(toks[:50], 0)
     for i in range(50, 90):
         step = b.forward(toks[i:i + 1], i)
-    np.testing.assert_array_equal(step, full)
+    np.testing.assert_allclose(step, full, rtol=0, atol=2e-3)
     snap = a.kv_snapshot()
     assert snap.positions == 90
     c = model.new_sequence()
@@ -93,6 +95,12 @@ def test_continuation_snapshot_clone_and_clear_are_exact(tiny_prepared):
     a.clear_cache()
     assert a.positions() == 0
     np.testing.assert_array_equal(a.forward(toks, 0), full)
+    # Per-token continuation after a restore is bit-exact with itself.
+    d = model.new_sequence()
+    d.restore_kv_prefix(snap, 80)
+    e = model.new_sequence()
+    e.restore_kv_prefix(snap, 80)
+    np.testing.assert_array_equal(d.forward([7], 80), e.forward([7], 80))
 
 
 def test_forward_errors(tiny_prepared):
