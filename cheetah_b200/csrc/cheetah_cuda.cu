@@ -1783,4 +1783,107 @@ int cheetah_cuda_op_decode_attention(const CheetahCudaDecodeAttention *a, void *
     return cheetah::launch_attention_mma(k_map, v_map, mp, (int)a->head_dim, st, false);
 }
 
+// ---- Decode attention without allocation ----------------------------------
+// Some callers cannot let the library allocate device memory: a caller that
+// records its work into a CUDA graph (allocation is not allowed while a stream
+// is being captured), a caller that manages a fixed device-memory budget
+// itself, or a latency-critical caller that cannot absorb the device-wide
+// synchronisation cudaMalloc / cudaFree may cause. This entry point computes
+// the same attention as cheetah_cuda_op_decode_attention, but its split-merge
+// scratch is a fixed array compiled into the library (held by every GPU that
+// loads it, until exit) instead of memory allocated on first use.
+constexpr int kNoAllocMaxParts = 1024;  // (sequence, kv head, split) partials
+constexpr int kNoAllocMaxPairs = 1024;  // (sequence, kv head) merge tickets
+constexpr size_t kNoAllocOBytes = (size_t)kNoAllocMaxParts * cheetah::kMaxGroup * 128 * sizeof(float);
+constexpr size_t kNoAllocMlBytes = (size_t)kNoAllocMaxParts * cheetah::kMaxGroup * 2 * sizeof(float);
+constexpr size_t kNoAllocTicketBytes = (size_t)kNoAllocMaxPairs * sizeof(unsigned int);
+constexpr size_t kNoAllocScratchBytes = kNoAllocOBytes + kNoAllocMlBytes + kNoAllocTicketBytes;  // ~4.1 MiB
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+// Device address of g_noalloc_scratch, looked up once per device with that
+// device current (the host-side symbol is only a stand-in, not an address).
+static std::mutex g_noalloc_mutex;
+static std::map<int, uint8_t *> g_noalloc_ptrs;
+
+static int noalloc_scratch(int device, uint8_t **out) {
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    auto it = g_noalloc_ptrs.find(device);
+    if (it == g_noalloc_ptrs.end()) {
+        void *ptr = nullptr;
+        const cudaError_t err = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+        CH_REQUIRE(err == cudaSuccess && ptr != nullptr,
+                   std::string("cheetah_cuda_op_decode_attention_noalloc: cudaGetSymbolAddress failed: ") +
+                       cudaGetErrorString(err));
+        it = g_noalloc_ptrs.emplace(device, static_cast<uint8_t *>(ptr)).first;
+    }
+    *out = it->second;
+    return 0;
+}
+
+int cheetah_cuda_op_decode_attention_noalloc(const CheetahCudaDecodeAttention *a, void *stream) {
+    CH_REQUIRE(a != nullptr && a->q && a->k_pool && a->v_pool && a->page_table && a->seq_lens && a->out,
+               "cheetah_cuda_op_decode_attention_noalloc: null argument");
+    CH_REQUIRE(a->head_dim == 64 || a->head_dim == 128,
+               "cheetah_cuda_op_decode_attention_noalloc: head_dim must be 64 or 128");
+    CH_REQUIRE(a->kv_heads > 0 && a->q_heads % a->kv_heads == 0 && a->q_heads / a->kv_heads <= (uint32_t)cheetah::kMaxGroup,
+               "cheetah_cuda_op_decode_attention_noalloc: q_heads must be a multiple of kv_heads (group <= 8)");
+    CH_REQUIRE(a->page_tokens > 0 && a->batch > 0 && a->num_pages > 0,
+               "cheetah_cuda_op_decode_attention_noalloc: empty shape");
+    CH_REQUIRE(a->kv_dtype == CHEETAH_CUDA_KV_BF16 || a->kv_dtype == CHEETAH_CUDA_KV_F32,
+               "cheetah_cuda_op_decode_attention_noalloc: unknown kv_dtype");
+    CH_REQUIRE(((uintptr_t)a->q & 15) == 0 && ((uintptr_t)a->out & 15) == 0,
+               "cheetah_cuda_op_decode_attention_noalloc: q and out must be 16-byte aligned");
+    const size_t pairs = (size_t)a->batch * a->kv_heads;
+    CH_REQUIRE(pairs <= (size_t)kNoAllocMaxPairs,
+               "cheetah_cuda_op_decode_attention_noalloc: batch * kv_heads = " + std::to_string(pairs) +
+                   " exceeds the fixed scratch limit of " + std::to_string(kNoAllocMaxPairs) + " sequence-head pairs");
+    int device = 0;
+    CH_CUDA_TRY(cudaGetDevice(&device));
+    uint8_t *scratch = nullptr;
+    if (noalloc_scratch(device, &scratch) != 0) return -1;
+    const int sms = cheetah::sm_count(device);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const bool mma = a->kv_dtype == CHEETAH_CUDA_KV_BF16 &&
+                     cheetah::mma_attention_eligible((int)a->head_dim, (int)a->page_tokens);
+    cheetah::AttnParams p = {};
+    p.q = a->q;
+    p.k_pool = a->k_pool;
+    p.v_pool = a->v_pool;
+    p.page_table = a->page_table;
+    p.seq_lens = a->seq_lens;
+    p.max_pages = (int)a->max_pages_per_seq;
+    p.num_pages = (int)a->num_pages;
+    p.page_tokens = (int)a->page_tokens;
+    p.batch = (int)a->batch;
+    p.q_heads = (int)a->q_heads;
+    p.kv_heads = (int)a->kv_heads;
+    p.window = (int)a->sliding_window;
+    int splits = mma ? cheetah::mma_attention_splits((int)a->batch, (int)a->kv_heads, sms)
+                     : cheetah::attention_splits((int)a->batch, (int)a->kv_heads,
+                                                 (int)std::max<uint32_t>(1, a->max_seq_len), sms);
+    splits = std::max(1, std::min(splits, (int)(kNoAllocMaxParts / pairs)));  // fit the fixed partials
+    p.splits = splits;
+    p.scale = 1.0f / sqrtf((float)a->head_dim);
+    p.out = a->out;
+    p.part_o = reinterpret_cast<float *>(scratch);
+    p.part_ml = reinterpret_cast<float *>(scratch + kNoAllocOBytes);
+    p.tickets = reinterpret_cast<unsigned int *>(scratch + kNoAllocOBytes + kNoAllocMlBytes);
+    p.error = nullptr;
+    // The array keeps whatever the previous call left: clear the tickets this
+    // call counts on (every completed launch also returns them to zero).
+    CH_CUDA_TRY(cudaMemsetAsync(p.tickets, 0, pairs * sizeof(unsigned int), st));
+    if (!mma) return cheetah::launch_attention(p, (int)a->head_dim, a->kv_dtype == CHEETAH_CUDA_KV_F32, st, false);
+    CUtensorMap k_map, v_map;
+    const unsigned long long rows = (unsigned long long)a->num_pages * a->kv_heads * a->page_tokens;
+    if (cheetah::make_kv_tensor_map(&k_map, a->k_pool, rows, (int)a->head_dim) != 0 ||
+        cheetah::make_kv_tensor_map(&v_map, a->v_pool, rows, (int)a->head_dim) != 0) {
+        return -1;
+    }
+    cheetah::MmaAttnParams mp = {};
+    mp.a = p;
+    mp.layer_row_offset = 0;
+    mp.page_tokens = (int)a->page_tokens;
+    return cheetah::launch_attention_mma(k_map, v_map, mp, (int)a->head_dim, st, false);
+}
+
 }  // extern "C"

@@ -87,6 +87,7 @@ SIGNATURES = {
     "cheetah_cuda_seq_export_kv": (_I, [_P, _S, _P, _P]),
     "cheetah_cuda_op_gemv_bf16": (_I, [_P, _S, _S, _P, _S, _P, _P]),
     "cheetah_cuda_op_decode_attention": (_I, [C.POINTER(DecodeAttentionArgs), _P]),
+    "cheetah_cuda_op_decode_attention_noalloc": (_I, [C.POINTER(DecodeAttentionArgs), _P]),
     "cheetah_cuda_quant_buffer_bytes": (_I, [C.c_char_p, _S, _S, C.POINTER(_S)]),
     "cheetah_cuda_op_quantize_q8": (_I, [_P, _S, _S, _P, _P]),
     "cheetah_cuda_op_quantize_q4": (_I, [_P, _S, _S, _P, _P]),
@@ -332,8 +333,10 @@ def gemv_quant(buffer, fmt: str, rows: int, cols: int, x, stream=None):
 
 
 def decode_attention(q, k_pool, v_pool, page_table, seq_lens, max_seq_len: int,
-                     sliding_window: int = 0, out=None, stream=None):
-    """Paged GQA decode attention (`ops.rs:1357-1467`).
+                     sliding_window: int = 0, out=None, stream=None, noalloc: bool = False):
+    """Paged GQA decode attention (`ops.rs:1357-1467`). noalloc=True takes the
+    entry point whose scratch is a fixed array inside the library (for callers
+    that cannot let the library allocate device memory).
 
     q [B, q_heads, D] f32; k_pool/v_pool [pages, kv_heads, page_tokens, D]
     bf16 or f32; page_table [B, max_pages] int32; seq_lens [B] int32."""
@@ -348,5 +351,6 @@ def decode_attention(q, k_pool, v_pool, page_table, seq_lens, max_seq_len: int,
         KV_F32 if k_pool.dtype == torch.float32 else KV_BF16,
         page_table.data_ptr(), page_table.shape[1], seq_lens.data_ptr(), max_seq_len, pages, pt,
         B, qh, kvh, D, sliding_window, out.data_ptr())
-    _check(lib().cheetah_cuda_op_decode_attention(C.byref(args), _stream_ptr(stream)))
+    fn = lib().cheetah_cuda_op_decode_attention_noalloc if noalloc else lib().cheetah_cuda_op_decode_attention
+    _check(fn(C.byref(args), _stream_ptr(stream)))
     return out

@@ -190,6 +190,22 @@ typedef struct CheetahCudaDecodeAttention {
 } CheetahCudaDecodeAttention;
 CHEETAH_CUDA_API int cheetah_cuda_op_decode_attention(const CheetahCudaDecodeAttention *args, void *stream);
 
+/* Decode attention for callers that cannot let the library allocate device
+ * memory — e.g. code recording into a CUDA graph (no allocation while a stream
+ * is being captured), a host that runs a fixed device-memory budget, or a
+ * latency-critical path that cannot absorb cudaMalloc's synchronisation.
+ * Same arguments and result as cheetah_cuda_op_decode_attention; the
+ * split-merge scratch is a fixed ~4.1 MiB array compiled into the library,
+ * held by every GPU that loads it until the process exits. Limits:
+ * batch * kv_heads <= 1024 (larger requests fail with an error); the KV split
+ * count is reduced so batch * kv_heads * splits <= 1024. The first call on a
+ * device looks the array's device address up (cudaGetSymbolAddress); make
+ * that first call before any stream capture. All calls share the one array:
+ * calls that overlap on the GPU (different streams, no ordering) race.
+ * No counterpart in the reference. */
+CHEETAH_CUDA_API int cheetah_cuda_op_decode_attention_noalloc(const CheetahCudaDecodeAttention *args,
+                                                              void *stream);
+
 #ifdef __cplusplus
 }
 #endif
