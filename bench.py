@@ -233,6 +233,89 @@ def attention_microbench(torch, R, hbm_peak, quick: bool):
     return rows
 
 
+def prefill_bench(torch, R, model_dir, cfg, reps: int = 3):
+    """Config 3: 2048-token cached prefix, then a 4096-token prompt in chunks
+    of 512 (CHEETAH_PREFILL_CHUNK=512); the prefix is restored from a device
+    snapshot before every repetition. CUDA events on the sequence stream."""
+    prefix, prompt = 2048, 4096
+    os.environ["CHEETAH_PREFILL_CHUNK"] = "512"
+    model = R.CudaModel(model_dir, max_positions=prefix + prompt + 64)
+    toks = np.random.default_rng(3).integers(0, cfg["vocab_size"], prefix + prompt).astype(np.uint32)
+    seq = model.new_sequence()
+    seq.forward(toks[:prefix], 0)
+    snap = seq.kv_snapshot()
+    stream = torch.cuda.ExternalStream(seq.stream_handle())
+    times = []
+    for r in range(reps + 1):
+        seq.restore_kv_prefix(snap, prefix)
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        seq.forward(toks[prefix:], prefix)
+        e.record(stream)
+        e.synchronize()
+        if r > 0:
+            times.append(s.elapsed_time(e) / 1e3)
+    sec = min(times)
+    L, H, I, QD, KD = cfg["num_layers"], cfg["hidden_size"], cfg["intermediate_size"], \
+        cfg["q_heads"] * cfg["head_dim"], cfg["kv_heads"] * cfg["head_dim"]
+    linear_params = L * (H * (QD + 2 * KD) + QD * H + 2 * I * H + I * H)
+    lin_flops = 2.0 * linear_params * prompt
+    attn_flops = 4.0 * cfg["head_dim"] * cfg["q_heads"] * L * sum(p + 1 for p in range(prefix, prefix + prompt))
+    lm_flops = 2.0 * cfg["vocab_size"] * H * (prompt // 512)
+    total = lin_flops + attn_flops + lm_flops
+    del seq, snap
+    model.close()
+    os.environ.pop("CHEETAH_PREFILL_CHUNK", None)
+    return {"workload": "config 3: 0.5B, 2048-token cached prefix + 4096-token prompt, chunks of 512",
+            "tok_per_s": prompt / sec, "ms": sec * 1e3, "tflops": total / sec / 1e12,
+            "flops": {"linear": lin_flops, "attention": attn_flops, "lm_head": lm_flops},
+            "timing": f"min of {reps} repetitions, CUDA events on the sequence stream"}
+
+
+def decode_7b(args):
+    """Config 4: Qwen2-7B-architecture decode (B=1) with q8 / q4 / bf16 linears:
+    1024-token prompt, then device-chained greedy steps."""
+    import torch
+    from cheetah_b200 import runtime as R
+    from cheetah_b200.prepared import PreparedModel, cached_synthetic, resolve_config
+    quant = args.workload.split("-")[-1]
+    model_dir = cached_synthetic("qwen2-7b")
+    cfg = resolve_config(PreparedModel(model_dir))
+    hbm_peak, _, peak_kind = peaks()
+    model = R.CudaModel(model_dir, quant=quant, max_positions=4096)
+    seq = model.new_sequence()
+    prompt = np.random.default_rng(1).integers(0, cfg["vocab_size"], 1024).astype(np.uint32)
+    first = int(np.argmax(seq.forward(prompt, 0)))
+    warm = seq.generate_greedy(first, 1024, args.warmup)
+    stream = torch.cuda.ExternalStream(seq.stream_handle())
+    torch.cuda.synchronize()
+    clocks = ClockSampler(0)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record(stream)
+    seq.generate_greedy(int(warm[-1]), 1024 + args.warmup, args.steps, wait=False)
+    e.record(stream)
+    e.synchronize()
+    clock_info = clocks.stop()
+    sec = s.elapsed_time(e) / 1e3
+    info = model.info()
+    ctx = 1024 + args.warmup + args.steps / 2
+    kv = cfg["num_layers"] * cfg["kv_heads"] * cfg["head_dim"] * 2 * 2 * ctx
+    step_bytes = info["weight_bytes"] + kv
+    gbs = step_bytes / (sec / args.steps) / 1e9
+    line = {"metric": METRIC, "value": args.steps / sec, "unit": "tok/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1e3 * sec / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": quant,
+            "data": "synthetic (seeded random-init bf16 weights quantised per row at load)",
+            "config": {"workload": f"qwen2-7b decode B=1 {quant} (config 4: 1024-token prompt)",
+                       "model": "Qwen2-7B architecture", "global_batch": 1, "seq_len": 1024},
+            "clocks": clock_info,
+            "step_roofline": {"bytes_per_token": step_bytes, "achieved_GBps": gbs, "peak": hbm_peak,
+                              "peak_kind": peak_kind, "frac_measured": gbs / hbm_peak, "frac_8TBps": gbs / 8000.0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def run_ours(args):
     import torch
     from cheetah_b200 import runtime as R
@@ -337,6 +420,8 @@ def run_ours(args):
         line["roofline"]["peak_kind"] = peak_kind
         if not args.no_attention:
             line["attention"] = attention_microbench(torch, R, hbm_peak, quick=args.quick_attention)
+        if not args.no_prefill:
+            line["prefill"] = prefill_bench(torch, R, model_dir, cfg)
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(model_dir, cfg, args.cpu_steps)
         print(json.dumps(line), flush=True)
@@ -358,11 +443,16 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-attention", action="store_true")
     ap.add_argument("--quick-attention", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--workload", default="decode-0.5b",
+                    choices=["decode-0.5b", "decode-7b-q8", "decode-7b-q4", "decode-7b-bf16"])
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload.startswith("decode-7b"):
+        return decode_7b(args)
     return run_ours(args)
 
 

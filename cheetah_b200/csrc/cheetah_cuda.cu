@@ -407,6 +407,7 @@ struct Seq {
     int32_t *ptokens = nullptr;
     float *phid = nullptr;
     uint16_t *pxb = nullptr, *pqb = nullptr, *pab = nullptr, *pact = nullptr;
+    float *ppart_o = nullptr, *ppart_ml = nullptr;  // prefill attention key-range splits
     CUtensorMap map_xb{}, map_ab{}, map_act{};
     cudaGraphExec_t graph = nullptr;
     cudaGraphExec_t chain_graph = nullptr;
@@ -423,6 +424,8 @@ struct Seq {
         cudaFree(pqb);
         cudaFree(pab);
         cudaFree(pact);
+        cudaFree(ppart_o);
+        cudaFree(ppart_ml);
         if (stream) cudaStreamDestroy(stream);
         cudaFree(page_table);
         cudaFree(hidden);
@@ -945,11 +948,11 @@ int open_model(const char *prepared_dir, const CheetahCudaConfig *config, const 
         bool ok = true;
         for (uint32_t layer = 0; layer < c.num_layers && ok; ++layer) {
             LayerWeights &w = m->layers[layer];
-            ok = make_bf16_tensor_map(&w.map_qkv, w.wqkv, QD + 2 * KD, H, kGemmBM) == 0 &&
-                 make_bf16_tensor_map(&w.map_o, w.wo, H, QD, kGemmBM) == 0 &&
-                 make_bf16_tensor_map(&w.map_gate, w.wgate, I, H, kGemmBM / 2) == 0 &&
-                 make_bf16_tensor_map(&w.map_up, w.wup, I, H, kGemmBM / 2) == 0 &&
-                 make_bf16_tensor_map(&w.map_down, w.wdown, H, I, kGemmBM) == 0;
+            ok = make_bf16_tensor_map(&w.map_qkv, w.wqkv, QD + 2 * KD, H, 64) == 0 &&
+                 make_bf16_tensor_map(&w.map_o, w.wo, H, QD, 64) == 0 &&
+                 make_bf16_tensor_map(&w.map_gate, w.wgate, I, H, 64) == 0 &&
+                 make_bf16_tensor_map(&w.map_up, w.wup, I, H, 64) == 0 &&
+                 make_bf16_tensor_map(&w.map_down, w.wdown, H, I, 64) == 0;
         }
         if (!ok) {
             delete m;
@@ -990,7 +993,9 @@ int open_model(const char *prepared_dir, const CheetahCudaConfig *config, const 
         m->use_mma_attention = true;
     }
     // Tensor-core chunked prefill needs the bf16 weight maps and the bf16 KV maps.
-    m->gemm_prefill = weight_maps_ok && m->use_mma_attention && (c.head_dim == 64 || c.head_dim == 128);
+    // Vectorised epilogues: residual widths in 32-column groups, SwiGLU in 16.
+    m->gemm_prefill = weight_maps_ok && m->use_mma_attention && (c.head_dim == 64 || c.head_dim == 128) &&
+                      c.hidden_size % 32 == 0 && c.intermediate_size % 16 == 0;
     m->free_pages.reserve(m->num_pages);
     for (int i = m->num_pages - 1; i >= 0; --i) m->free_pages.push_back(i);
     err = cudaDeviceSynchronize();
@@ -1141,11 +1146,15 @@ int ensure_prefill_buffers(Seq &s, int rows) {
     cudaFree(s.pqb);
     cudaFree(s.pab);
     cudaFree(s.pact);
+    cudaFree(s.ppart_o);
+    cudaFree(s.ppart_ml);
     s.chunk_cap = 0;
     const size_t R = (size_t)rows;
     bool ok = cudaMalloc(&s.ptokens, R * 4) == cudaSuccess && cudaMalloc(&s.phid, R * H * 4) == cudaSuccess &&
               cudaMalloc(&s.pxb, R * H * 2) == cudaSuccess && cudaMalloc(&s.pqb, R * QD * 2) == cudaSuccess &&
-              cudaMalloc(&s.pab, R * QD * 2) == cudaSuccess && cudaMalloc(&s.pact, R * I * 2) == cudaSuccess;
+              cudaMalloc(&s.pab, R * QD * 2) == cudaSuccess && cudaMalloc(&s.pact, R * I * 2) == cudaSuccess &&
+              cudaMalloc(&s.ppart_o, (size_t)kPrefillMaxSplits * R * QD * 4) == cudaSuccess &&
+              cudaMalloc(&s.ppart_ml, (size_t)kPrefillMaxSplits * R * c.q_heads * 2 * 4) == cudaSuccess;
     if (!ok) {
         set_error("CUDA backend: prefill buffer allocation failed.");
         return -1;
@@ -1159,16 +1168,28 @@ int ensure_prefill_buffers(Seq &s, int rows) {
     return 0;
 }
 
-template <int EPI>
-int launch_prefill_gemm(const CUtensorMap &a, const CUtensorMap &b, const CUtensorMap &b2, const PrefillGemmParams &p,
-                        cudaStream_t st, bool pdl) {
-    auto kernel = prefill_gemm_kernel<EPI, 128>;
-    const size_t smem = prefill_gemm_smem<128>();
+template <int EPI, int BN>
+int launch_prefill_gemm_bn(const CUtensorMap &a, const CUtensorMap &b, const CUtensorMap &b2,
+                           const PrefillGemmParams &p, cudaStream_t st, bool pdl) {
+    auto kernel = prefill_gemm_kernel<EPI, BN>;
+    const size_t smem = prefill_gemm_smem<BN>();
     CH_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    const int n_tiles = EPI == kPgSwiglu ? (p.N + 63) / 64 : (p.N + 127) / 128;
+    const int n_tiles = EPI == kPgSwiglu ? (p.N + BN / 2 - 1) / (BN / 2) : (p.N + BN - 1) / BN;
     dim3 grid(n_tiles, (p.M + kGemmBM - 1) / kGemmBM);
     CH_CUDA_TRY(launch_ex(kernel, grid, dim3(kGemmThreads), smem, st, pdl, a, b, b2, p));
     return 0;
+}
+
+// Tile width: 64-column tiles double the CTA count of the narrow GEMMs
+// (QKV, o_proj, down at chunk sizes of a few hundred rows).
+template <int EPI>
+int launch_prefill_gemm(const CUtensorMap &a, const CUtensorMap &b, const CUtensorMap &b2, const PrefillGemmParams &p,
+                        cudaStream_t st, bool pdl, int sms) {
+    const int m_tiles = (p.M + kGemmBM - 1) / kGemmBM;
+    const bool narrow = EPI != kPgSwiglu && (EPI != kPgQkv || p.head_dim == 64) &&
+                        ((p.N + 127) / 128) * m_tiles < sms;
+    if (narrow) return launch_prefill_gemm_bn<EPI, 64>(a, b, b2, p, st, pdl);
+    return launch_prefill_gemm_bn<EPI, 128>(a, b, b2, p, st, pdl);
 }
 
 // One prompt chunk through every layer on the tensor cores
@@ -1215,7 +1236,7 @@ int run_prefill_chunk(Seq &s, const uint32_t *tokens, int M, size_t offset, bool
         g.v_cache = v_layer;
         g.kv_f32 = m.kv_f32;
         g.error = s.d_error;
-        if (launch_prefill_gemm<kPgQkv>(s.map_xb, w.map_qkv, w.map_qkv, g, st, pdl) != 0) return -1;
+        if (launch_prefill_gemm<kPgQkv>(s.map_xb, w.map_qkv, w.map_qkv, g, st, pdl, m.sms) != 0) return -1;
 
         PrefillAttnParams ap = {};
         ap.q = s.pqb;
@@ -1233,17 +1254,30 @@ int run_prefill_chunk(Seq &s, const uint32_t *tokens, int M, size_t offset, bool
         ap.scale = 1.0f / sqrtf((float)c.head_dim);
         ap.error = s.d_error;
         const size_t asmem = prefill_attention_smem();
-        dim3 agrid((M + 15) / 16, c.kv_heads);
+        // Key-range splits: about two CTAs per SM (each CTA covers >= 4 key tiles).
+        const int blocks = ((M + 15) / 16) * (int)c.kv_heads;
+        const int key_tiles = (int)((offset + M + 63) / 64);
+        ap.splits = std::max(1, std::min(std::min(kPrefillMaxSplits, (2 * m.sms + blocks - 1) / blocks),
+                                         std::max(1, key_tiles / 4)));
+        ap.part_o = s.ppart_o;
+        ap.part_ml = s.ppart_ml;
+        dim3 agrid((M + 15) / 16, c.kv_heads, ap.splits);
         if (c.head_dim == 64) {
             CH_CUDA_TRY(cudaFuncSetAttribute(prefill_attention_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)asmem));
             CH_CUDA_TRY(launch_ex(prefill_attention_kernel<64>, agrid, dim3(kPrefillWarps * kWarp), asmem, st, pdl,
                                   m.k_map, m.v_map, ap));
+            if (ap.splits > 1) {
+                CH_CUDA_TRY(launch_ex(prefill_merge_kernel<64>, dim3(2 * m.sms), dim3(256), 0, st, pdl, ap));
+            }
         } else {
             CH_CUDA_TRY(cudaFuncSetAttribute(prefill_attention_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)asmem));
             CH_CUDA_TRY(launch_ex(prefill_attention_kernel<128>, agrid, dim3(kPrefillWarps * kWarp), asmem, st, pdl,
                                   m.k_map, m.v_map, ap));
+            if (ap.splits > 1) {
+                CH_CUDA_TRY(launch_ex(prefill_merge_kernel<128>, dim3(2 * m.sms), dim3(256), 0, st, pdl, ap));
+            }
         }
 
         PrefillGemmParams o = {};
@@ -1254,7 +1288,7 @@ int run_prefill_chunk(Seq &s, const uint32_t *tokens, int M, size_t offset, bool
         o.out_f32 = s.phid;
         o.ld_out = H;
         o.error = s.d_error;
-        if (launch_prefill_gemm<kPgResidual>(s.map_ab, w.map_o, w.map_o, o, st, pdl) != 0) return -1;
+        if (launch_prefill_gemm<kPgResidual>(s.map_ab, w.map_o, w.map_o, o, st, pdl, m.sms) != 0) return -1;
 
         CH_CUDA_TRY(launch_ex(norm_rows_bf16_kernel, dim3(M), dim3(256), 0, st, pdl, (const float *)s.phid, M, H,
                               w.ln2, c.rms_eps, s.pxb));
@@ -1265,7 +1299,7 @@ int run_prefill_chunk(Seq &s, const uint32_t *tokens, int M, size_t offset, bool
         gu.out_bf16 = s.pact;
         gu.ld_out = I;
         gu.error = s.d_error;
-        if (launch_prefill_gemm<kPgSwiglu>(s.map_xb, w.map_gate, w.map_up, gu, st, pdl) != 0) return -1;
+        if (launch_prefill_gemm<kPgSwiglu>(s.map_xb, w.map_gate, w.map_up, gu, st, pdl, m.sms) != 0) return -1;
 
         PrefillGemmParams dn = {};
         dn.M = M;
@@ -1274,7 +1308,7 @@ int run_prefill_chunk(Seq &s, const uint32_t *tokens, int M, size_t offset, bool
         dn.out_f32 = s.phid;
         dn.ld_out = H;
         dn.error = s.d_error;
-        if (launch_prefill_gemm<kPgResidual>(s.map_act, w.map_down, w.map_down, dn, st, pdl) != 0) return -1;
+        if (launch_prefill_gemm<kPgResidual>(s.map_act, w.map_down, w.map_down, dn, st, pdl, m.sms) != 0) return -1;
     }
     if (last) {
         CH_CUDA_TRY(cudaMemsetAsync(s.argmax, 0, 8, st));

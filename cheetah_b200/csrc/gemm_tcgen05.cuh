@@ -100,21 +100,39 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// 16 consecutive values as bf16 (two 16-byte stores; dst 16-byte aligned).
+__device__ __forceinline__ void store_bf16x16(uint16_t *dst, const float (&v)[16]) {
+    uint32_t w[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) w[i] = (uint32_t)f32_to_bf16_rne(v[2 * i]) | ((uint32_t)f32_to_bf16_rne(v[2 * i + 1]) << 16);
+    uint4 *d = reinterpret_cast<uint4 *>(dst);
+    d[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    d[1] = make_uint4(w[4], w[5], w[6], w[7]);
+}
+
+__device__ __forceinline__ void store_f32x16(float *dst, const float (&v)[16]) {
+    float4 *d = reinterpret_cast<float4 *>(dst);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) d[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+}
+
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-__device__ __forceinline__ void store_kv_row(const PrefillGemmParams &p, int pos, int kv_head, int d, float value,
-                                             bool is_k) {
-    const int pidx = pos / p.page_tokens;
-    if (pos < 0 || pidx >= p.max_pages) return;
-    const int page = p.page_table[pidx];
-    if (page < 0 || page >= p.num_pages) return;
-    const long long index =
-        (((long long)page * p.kv_heads + kv_head) * p.page_tokens + (pos - pidx * p.page_tokens)) * p.head_dim + d;
-    void *base = is_k ? p.k_cache : p.v_cache;
-    if (p.kv_f32) static_cast<float *>(base)[index] = value;
-    else static_cast<uint16_t *>(base)[index] = f32_to_bf16_rne(value);
-}
 
 template <int EPI, int BN>
 __global__ void __launch_bounds__(kGemmThreads, 1)
@@ -178,7 +196,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     tma_load_2d(smem_u32(b_dst), &b_map, kb * kGemmBK, n_tile * (BN / 2), bar);
                     tma_load_2d(smem_u32(b_dst + kBBytes / 2), &b2_map, kb * kGemmBK, n_tile * (BN / 2), bar);
                 } else {
-                    tma_load_2d(smem_u32(b_dst), &b_map, kb * kGemmBK, n_tile * BN, bar);
+                    // Weight maps use 64-row boxes; a BN-row tile is BN/64 boxes.
+#pragma unroll
+                    for (int r = 0; r < BN / 64; ++r) {
+                        tma_load_2d(smem_u32(b_dst + r * 64 * 128), &b_map, kb * kGemmBK, n_tile * BN + r * 64, bar);
+                    }
                 }
             }
         }
@@ -204,31 +226,46 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             umma_commit(smem_u32(&done_bar));
         }
     } else {
-        // Epilogue warps 2..5: TMEM lane quadrant = warp % 4.
+        // Epilogue warps 2..5: TMEM lane quadrant = warp % 4; thread = tile row.
         const int quad = warp % 4;
         const int row = m_tile * kGemmBM + quad * 32 + lane;
+        const bool live = row < p.M;
         const bool ok = mbar_wait(smem_u32(&done_bar), 0);
         tc_fence_after();
         if (!ok) {
             if (p.error) *p.error = 4;
         } else {
             const uint32_t lane_addr = tmem + ((uint32_t)(quad * 32) << 16);
-            const bool live = row < p.M;
             if (EPI == kPgResidual) {
+                // hidden[row][n] += acc (+ bias): 32 columns per step, float4 traffic.
 #pragma unroll 1
-                for (int c0 = 0; c0 < BN; c0 += 16) {
-                    float v[16];
-                    tmem_ld16(lane_addr + c0, v);
+                for (int c0 = 0; c0 < BN; c0 += 32) {
+                    float v[32];
+                    tmem_ld32(lane_addr + c0, v);
                     const int n0 = n_tile * BN + c0;
-                    if (live) {
-                        float *dst = p.out_f32 + (long long)row * p.ld_out + n0;
+                    if (live && n0 < p.N) {
+                        float4 *d4 = reinterpret_cast<float4 *>(p.out_f32 + (long long)row * p.ld_out + n0);
+                        float4 r[8];
 #pragma unroll
-                        for (int i = 0; i < 16; ++i) {
-                            if (n0 + i < p.N) {
-                                float val = v[i];
-                                if (p.bias) val = __fadd_rn(val, p.bias[n0 + i]);
-                                dst[i] = __fadd_rn(dst[i], val);
+                        for (int i = 0; i < 8; ++i) r[i] = d4[i];
+                        if (p.bias) {
+                            const float4 *b4 = reinterpret_cast<const float4 *>(p.bias + n0);
+#pragma unroll
+                            for (int i = 0; i < 8; ++i) {
+                                const float4 b = b4[i];
+                                v[4 * i] = __fadd_rn(v[4 * i], b.x);
+                                v[4 * i + 1] = __fadd_rn(v[4 * i + 1], b.y);
+                                v[4 * i + 2] = __fadd_rn(v[4 * i + 2], b.z);
+                                v[4 * i + 3] = __fadd_rn(v[4 * i + 3], b.w);
                             }
+                        }
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            r[i].x = __fadd_rn(r[i].x, v[4 * i]);
+                            r[i].y = __fadd_rn(r[i].y, v[4 * i + 1]);
+                            r[i].z = __fadd_rn(r[i].z, v[4 * i + 2]);
+                            r[i].w = __fadd_rn(r[i].w, v[4 * i + 3]);
+                            d4[i] = r[i];
                         }
                     }
                 }
@@ -239,21 +276,36 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     tmem_ld16(lane_addr + c0, g);
                     tmem_ld16(lane_addr + BN / 2 + c0, u);
                     const int n0 = n_tile * (BN / 2) + c0;
-                    if (live) {
-                        uint16_t *dst = p.out_bf16 + (long long)row * p.ld_out + n0;
+                    if (live && n0 < p.N) {
+                        uint32_t packed[8];
 #pragma unroll
-                        for (int i = 0; i < 16; ++i) {
-                            if (n0 + i < p.N) {
-                                const float a = __fmul_rn(g[i], __fdiv_rn(u[i], __fadd_rn(1.0f, expf(-g[i]))));
-                                dst[i] = f32_to_bf16_rne(a);
-                            }
+                        for (int i = 0; i < 8; ++i) {
+                            const float a0 = __fmul_rn(g[2 * i], __fdiv_rn(u[2 * i], __fadd_rn(1.0f, expf(-g[2 * i]))));
+                            const float a1 =
+                                __fmul_rn(g[2 * i + 1], __fdiv_rn(u[2 * i + 1], __fadd_rn(1.0f, expf(-g[2 * i + 1]))));
+                            packed[i] = (uint32_t)f32_to_bf16_rne(a0) | ((uint32_t)f32_to_bf16_rne(a1) << 16);
                         }
+                        uint4 *dst = reinterpret_cast<uint4 *>(p.out_bf16 + (long long)row * p.ld_out + n0);
+                        dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+                        dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
                     }
                 }
             } else {  // kPgQkv: BN covers whole heads
                 const int hd = p.head_dim;
                 const int half = hd >> 1;
                 const int pos = p.offset + row;
+                // The row's KV slot, resolved once.
+                long long slot_base = -1;  // element index of (page, kv head 0, slot, d 0)
+                if (live) {
+                    const int pidx = pos / p.page_tokens;
+                    const int page = pidx < p.max_pages ? p.page_table[pidx] : -1;
+                    if (page >= 0 && page < p.num_pages) {
+                        slot_base = ((long long)page * p.kv_heads * p.page_tokens + (pos - pidx * p.page_tokens)) * hd;
+                    } else if (p.error) {
+                        *p.error = 9;
+                    }
+                }
+                const long long head_stride = (long long)p.page_tokens * hd;  // elements between kv heads of a page
 #pragma unroll 1
                 for (int hb = 0; hb < BN; hb += hd) {
                     const int col0 = n_tile * BN + hb;  // first output feature of this head
@@ -264,32 +316,52 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                         tmem_ld16(lane_addr + hb + j, a);
                         tmem_ld16(lane_addr + hb + half + j, b);
                         if (!live || col0 >= p.N) continue;
+                        if (p.bias) {
+                            const float4 *ba = reinterpret_cast<const float4 *>(p.bias + col0 + j);
+                            const float4 *bb = reinterpret_cast<const float4 *>(p.bias + col0 + half + j);
 #pragma unroll
-                        for (int i = 0; i < 16; ++i) {
-                            const int d = j + i;
-                            float va = a[i], vb = b[i];
-                            if (p.bias) {
-                                va = __fadd_rn(va, p.bias[col0 + d]);
-                                vb = __fadd_rn(vb, p.bias[col0 + half + d]);
+                            for (int i = 0; i < 4; ++i) {
+                                const float4 x = ba[i], y = bb[i];
+                                a[4 * i] = __fadd_rn(a[4 * i], x.x); a[4 * i + 1] = __fadd_rn(a[4 * i + 1], x.y);
+                                a[4 * i + 2] = __fadd_rn(a[4 * i + 2], x.z); a[4 * i + 3] = __fadd_rn(a[4 * i + 3], x.w);
+                                b[4 * i] = __fadd_rn(b[4 * i], y.x); b[4 * i + 1] = __fadd_rn(b[4 * i + 1], y.y);
+                                b[4 * i + 2] = __fadd_rn(b[4 * i + 2], y.z); b[4 * i + 3] = __fadd_rn(b[4 * i + 3], y.w);
                             }
-                            if (head < p.q_heads + p.kv_heads) {
-                                const float c = p.rope_cos[(long long)pos * half + d];
-                                const float s = p.rope_sin[(long long)pos * half + d];
-                                const float ra = __fsub_rn(__fmul_rn(va, c), __fmul_rn(vb, s));
-                                const float rb = __fadd_rn(__fmul_rn(vb, c), __fmul_rn(va, s));
-                                va = ra;
-                                vb = rb;
+                        }
+                        if (head < p.q_heads + p.kv_heads) {
+                            // ops.rs:693-715: a' = a*cos - b*sin, b' = b*cos + a*sin
+                            const float4 *c4 = reinterpret_cast<const float4 *>(p.rope_cos + (long long)pos * half + j);
+                            const float4 *s4 = reinterpret_cast<const float4 *>(p.rope_sin + (long long)pos * half + j);
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) {
+                                const float4 cv = c4[i], sv = s4[i];
+                                const float cc[4] = {cv.x, cv.y, cv.z, cv.w};
+                                const float ss[4] = {sv.x, sv.y, sv.z, sv.w};
+#pragma unroll
+                                for (int e = 0; e < 4; ++e) {
+                                    const float va = a[4 * i + e], vb = b[4 * i + e];
+                                    a[4 * i + e] = __fsub_rn(__fmul_rn(va, cc[e]), __fmul_rn(vb, ss[e]));
+                                    b[4 * i + e] = __fadd_rn(__fmul_rn(vb, cc[e]), __fmul_rn(va, ss[e]));
+                                }
                             }
-                            if (head < p.q_heads) {
-                                uint16_t *q = p.out_bf16 + (long long)row * p.ld_out + head * hd;
-                                q[d] = f32_to_bf16_rne(va);
-                                q[d + half] = f32_to_bf16_rne(vb);
-                            } else if (head < p.q_heads + p.kv_heads) {
-                                store_kv_row(p, pos, head - p.q_heads, d, va, true);
-                                store_kv_row(p, pos, head - p.q_heads, d + half, vb, true);
+                        }
+                        if (head < p.q_heads) {
+                            uint16_t *q = p.out_bf16 + (long long)row * p.ld_out + head * hd;
+                            store_bf16x16(q + j, a);
+                            store_bf16x16(q + half + j, b);
+                        } else if (slot_base >= 0) {
+                            const bool is_k = head < p.q_heads + p.kv_heads;
+                            const int kvh = is_k ? head - p.q_heads : head - p.q_heads - p.kv_heads;
+                            void *cache = is_k ? p.k_cache : p.v_cache;
+                            const long long e0 = slot_base + kvh * head_stride;
+                            if (p.kv_f32) {
+                                float *dst = static_cast<float *>(cache) + e0;
+                                store_f32x16(dst + j, a);
+                                store_f32x16(dst + half + j, b);
                             } else {
-                                store_kv_row(p, pos, head - p.q_heads - p.kv_heads, d, va, false);
-                                store_kv_row(p, pos, head - p.q_heads - p.kv_heads, d + half, vb, false);
+                                uint16_t *dst = static_cast<uint16_t *>(cache) + e0;
+                                store_bf16x16(dst + j, a);
+                                store_bf16x16(dst + half + j, b);
                             }
                         }
                     }

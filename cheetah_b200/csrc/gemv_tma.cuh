@@ -166,7 +166,7 @@ __global__ void __launch_bounds__(kTmaGemvThreads, 2)
         __syncthreads();  // slot consumed, partials visible
         if (threadIdx.x == 0 && k + slots < n) issue(k + slots);
         if (EPI == kEpiQkv) {
-            if (threadIdx.x < RT / 2) {
+            if (RT >= 2 && (int)threadIdx.x < RT / 2) {
                 const int j = threadIdx.x;
                 float da = 0.0f, db = 0.0f;
 #pragma unroll

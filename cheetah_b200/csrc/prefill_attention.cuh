@@ -10,7 +10,9 @@
 // on mbarriers, bounded waits) and used by every query head of the group.
 // S = Q K^T and O += P V with mma.m16n8k16 (bf16 -> f32), causal and window
 // masks applied per (token, key) on the score fragments. A CTA barrier after
-// each tile frees its stage for the next TMA load.
+// each tile frees its stage for the next TMA load. The key range of a token
+// block splits over blockIdx.z so the grid covers every SM; the splits are
+// merged by prefill_merge_kernel.
 #pragma once
 
 #include "attention_mma.cuh"
@@ -19,6 +21,7 @@ namespace cheetah {
 
 constexpr int kPrefillStages = 3;
 constexpr int kPrefillWarps = 8;
+constexpr int kPrefillMaxSplits = 8;
 
 struct PrefillAttnParams {
     const uint16_t *q;        // bf16 [T][q_heads * head_dim], RoPE applied
@@ -32,10 +35,16 @@ struct PrefillAttnParams {
     int window;
     float scale;
     int *error;
+    // Key-range split: blockIdx.z of `splits` takes a contiguous share of the
+    // key tiles; with splits > 1 the CTA writes unnormalised partials
+    // (O, and m in log2 units, l) that prefill_merge_kernel combines.
+    int splits;
+    float *part_o;            // [splits][T][q_heads][head_dim]
+    float *part_ml;           // [splits][T][q_heads][2]
 };
 
 template <int HD>
-__global__ void __launch_bounds__(kPrefillWarps * kWarp, 1)
+__global__ void __launch_bounds__(kPrefillWarps * kWarp, HD == 64 ? 2 : 1)
     prefill_attention_kernel(const __grid_constant__ CUtensorMap k_map, const __grid_constant__ CUtensorMap v_map,
                              const PrefillAttnParams p) {
     using TL = MmaTile<HD>;
@@ -59,9 +68,13 @@ __global__ void __launch_bounds__(kPrefillWarps * kWarp, 1)
     const int pos_last = p.offset + t_last;
     int ws = 0;
     if (p.window > 0) ws = max(0, pos_first + 1 - p.window);
-    const int tile_lo = ws / TILE;
-    const int tile_hi = pos_last / TILE + 1;
-    const int n_tiles = tile_hi - tile_lo;
+    const int all_lo = ws / TILE;
+    const int all_hi = pos_last / TILE + 1;
+    const int per_split = (all_hi - all_lo + p.splits - 1) / p.splits;
+    const int split = blockIdx.z;
+    const int tile_lo = all_lo + split * per_split;
+    const int tile_hi = min(all_hi, tile_lo + per_split);
+    const int n_tiles = max(0, tile_hi - tile_lo);
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kPrefillStages; ++s) mbar_init(smem_u32(&full_bar[s]), 1);
@@ -217,6 +230,21 @@ __global__ void __launch_bounds__(kPrefillWarps * kWarp, 1)
         return;
     }
     if (!active) return;
+    if (p.splits > 1) {
+        const bool r0 = t0 + g <= t_last, r1 = t0 + g + 8 <= t_last;
+        const long long base0 = (((long long)split * p.T + t0 + g) * p.q_heads + head);
+        const long long base1 = (((long long)split * p.T + t0 + g + 8) * p.q_heads + head);
+#pragma unroll
+        for (int j = 0; j < HD / 8; ++j) {
+            if (r0) *reinterpret_cast<float2 *>(p.part_o + base0 * HD + j * 8 + 2 * c) = make_float2(o[j][0], o[j][1]);
+            if (r1) *reinterpret_cast<float2 *>(p.part_o + base1 * HD + j * 8 + 2 * c) = make_float2(o[j][2], o[j][3]);
+        }
+        if (c == 0) {
+            if (r0) *reinterpret_cast<float2 *>(p.part_ml + base0 * 2) = make_float2(m0, l0);
+            if (r1) *reinterpret_cast<float2 *>(p.part_ml + base1 * 2) = make_float2(m1, l1);
+        }
+        return;
+    }
     const float inv0 = l0 > 0.0f ? 1.0f / l0 : 0.0f;
     const float inv1 = l1 > 0.0f ? 1.0f / l1 : 0.0f;
     const bool r0 = t0 + g <= t_last, r1 = t0 + g + 8 <= t_last;
@@ -226,6 +254,37 @@ __global__ void __launch_bounds__(kPrefillWarps * kWarp, 1)
     for (int j = 0; j < HD / 8; ++j) {
         if (r0) *reinterpret_cast<uint32_t *>(out0 + j * 8 + 2 * c) = pack_bf16(o[j][0] * inv0, o[j][1] * inv0);
         if (r1) *reinterpret_cast<uint32_t *>(out1 + j * 8 + 2 * c) = pack_bf16(o[j][2] * inv1, o[j][3] * inv1);
+    }
+}
+
+// Combine the key-range splits of prefill_attention_kernel: per (token, head)
+// O = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s, written as bf16.
+template <int HD>
+__global__ void prefill_merge_kernel(const PrefillAttnParams p) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const long long rows = (long long)p.T * p.q_heads;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < rows * (HD / 4);
+         i += (long long)gridDim.x * blockDim.x) {
+        const long long rh = i / (HD / 4);
+        const int d4 = (int)(i % (HD / 4));
+        float m = -INFINITY;
+        for (int s = 0; s < p.splits; ++s) m = fmaxf(m, p.part_ml[((long long)s * rows + rh) * 2]);
+        float l = 0.0f;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int s = 0; s < p.splits; ++s) {
+            const float ms = p.part_ml[((long long)s * rows + rh) * 2];
+            const float w = m == -INFINITY ? 0.0f : exp2f(ms - m);
+            l += w * p.part_ml[((long long)s * rows + rh) * 2 + 1];
+            const float4 v = reinterpret_cast<const float4 *>(p.part_o + ((long long)s * rows + rh) * HD)[d4];
+            acc.x = fmaf(w, v.x, acc.x); acc.y = fmaf(w, v.y, acc.y);
+            acc.z = fmaf(w, v.z, acc.z); acc.w = fmaf(w, v.w, acc.w);
+        }
+        const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+        uint16_t *out = p.out + rh * HD + d4 * 4;
+        const uint32_t lo = (uint32_t)f32_to_bf16_rne(acc.x * inv) | ((uint32_t)f32_to_bf16_rne(acc.y * inv) << 16);
+        const uint32_t hi = (uint32_t)f32_to_bf16_rne(acc.z * inv) | ((uint32_t)f32_to_bf16_rne(acc.w * inv) << 16);
+        *reinterpret_cast<uint2 *>(out) = make_uint2(lo, hi);
     }
 }
 
