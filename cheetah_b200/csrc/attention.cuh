@@ -44,7 +44,13 @@ struct AttnParams {
     float *part_ml;            // [batch][kv_heads][splits][kMaxGroup][2]
     unsigned int *tickets;     // [batch][kv_heads], zero between launches
     int *error;                // nullable: set to 1 on an out-of-range page id
+    uint16_t *out_bf16;        // nullable: write the result as bf16 here instead of `out`
 };
+
+__device__ __forceinline__ void store_attn_out(const AttnParams &p, long long index, float value) {
+    if (p.out_bf16) p.out_bf16[index] = f32_to_bf16_rne(value);
+    else p.out[index] = value;
+}
 
 constexpr int kAttnThreads = 128;
 constexpr int kAttnWarps = kAttnThreads / kWarp;
@@ -126,7 +132,7 @@ __device__ __forceinline__ void merge_splits(const AttnParams &p, int b, int kvh
             o += o_s[w][g][d] * f;
         }
         if (active == 1) {
-            p.out[((long long)b * p.q_heads + kvh * group + g) * HD + d] = l > 0.0f ? o / l : 0.0f;
+            store_attn_out(p, ((long long)b * p.q_heads + kvh * group + g) * HD + d, l > 0.0f ? o / l : 0.0f);
         } else {
             p.part_o[(part * kMaxGroup + g) * HD + d] = o;
             if (d == 0) {
@@ -191,7 +197,15 @@ __device__ __forceinline__ void merge_splits(const AttnParams &p, int b, int kvh
         const float inv = l > 0.0f ? 1.0f / l : 0.0f;
         float4 r = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
         if (!(l > 0.0f)) r = make_float4(0.f, 0.f, 0.f, 0.f);
-        reinterpret_cast<float4 *>(p.out + ((long long)b * p.q_heads + kvh * group + g) * HD)[d4] = r;
+        const long long o0 = ((long long)b * p.q_heads + kvh * group + g) * HD + d4 * 4;
+        if (p.out_bf16) {
+            store_attn_out(p, o0, r.x);
+            store_attn_out(p, o0 + 1, r.y);
+            store_attn_out(p, o0 + 2, r.z);
+            store_attn_out(p, o0 + 3, r.w);
+        } else {
+            reinterpret_cast<float4 *>(p.out + o0)[0] = r;
+        }
     }
 }
 

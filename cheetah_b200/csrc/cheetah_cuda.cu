@@ -340,11 +340,51 @@ struct Model {
     bool use_mma_attention = false;
     bool qkv_interleaved = false;  // QKV rows stored pair-interleaved (bulk-prefetch GEMV)
     bool gemm_prefill = false;     // bf16 weights with tensor maps: tensor-core chunked prefill
+    CUtensorMap map_lm_head{};
+    // Batched decode workspace (one batch at a time per model).
+    std::mutex batch_mutex;
+    int batch_cap = 0;
+    int batch_table_cap = 0;
+    cudaStream_t batch_stream = nullptr;
+    int32_t *b_meta = nullptr;        // tokens[cap] | pos[cap] | lens[cap] | table[cap][table_cap]
+    int32_t *h_meta = nullptr;        // pinned staging of b_meta
+    float *b_hid = nullptr, *b_q = nullptr, *b_logits = nullptr;
+    uint16_t *b_xb = nullptr, *b_ab = nullptr, *b_act = nullptr;
+    unsigned long long *b_argmax = nullptr, *h_argmax = nullptr;
+    float *b_part_o = nullptr, *b_part_ml = nullptr;
+    unsigned int *b_tickets = nullptr;
+    int *b_error = nullptr;
+    CUtensorMap map_bxb{}, map_bab{}, map_bact{};
     CUtensorMap k_map{};
     CUtensorMap v_map{};
     std::mutex pool_mutex;
     std::vector<int> free_pages;
     std::atomic<int> refs{1};
+
+    void free_batch() {
+        cudaFree(b_meta);
+        cudaFreeHost(h_meta);
+        cudaFree(b_hid);
+        cudaFree(b_q);
+        cudaFree(b_logits);
+        cudaFree(b_xb);
+        cudaFree(b_ab);
+        cudaFree(b_act);
+        cudaFree(b_argmax);
+        cudaFreeHost(h_argmax);
+        cudaFree(b_part_o);
+        cudaFree(b_part_ml);
+        cudaFree(b_tickets);
+        cudaFree(b_error);
+        b_meta = h_meta = nullptr;
+        b_hid = b_q = b_logits = nullptr;
+        b_xb = b_ab = b_act = nullptr;
+        b_argmax = h_argmax = nullptr;
+        b_part_o = b_part_ml = nullptr;
+        b_tickets = nullptr;
+        b_error = nullptr;
+        batch_cap = batch_table_cap = 0;
+    }
 
     void *take(size_t bytes) {
         size_t offset = (arena_used + 255) & ~size_t(255);
@@ -369,6 +409,8 @@ struct Model {
 
     ~Model() {
         cudaSetDevice(device);
+        free_batch();
+        if (batch_stream) cudaStreamDestroy(batch_stream);
         cudaFree(arena);
         cudaFree(rope_cos);
         cudaFree(rope_sin);
@@ -958,6 +1000,11 @@ int open_model(const char *prepared_dir, const CheetahCudaConfig *config, const 
             delete m;
             return -1;
         }
+        ok = ok && make_bf16_tensor_map(&m->map_lm_head, m->lm_head, V, H, 64) == 0;
+        if (!ok) {
+            delete m;
+            return -1;
+        }
         weight_maps_ok = true;
     }
 
@@ -1344,6 +1391,206 @@ int check_device_error(Seq &s) {
     return 0;
 }
 
+// Batched decode workspace for up to `cap` sequences and page tables of
+// `table_cap` entries.
+int ensure_batch_workspace(Model &m, int cap, int table_cap) {
+    if (cap <= m.batch_cap && table_cap <= m.batch_table_cap) return 0;
+    CH_CUDA_TRY(cudaSetDevice(m.device));
+    if (m.batch_stream) CH_CUDA_TRY(cudaStreamSynchronize(m.batch_stream));
+    cap = std::max(cap, m.batch_cap);
+    table_cap = std::max(table_cap, m.batch_table_cap);
+    m.free_batch();
+    const CheetahCudaConfig &c = m.cfg;
+    const size_t R = (size_t)std::max(cap, 1), H = c.hidden_size, I = c.intermediate_size;
+    const size_t QD = (size_t)c.q_heads * c.head_dim, V = c.vocab_size;
+    const size_t meta = R * 3 + R * (size_t)table_cap;
+    // Split partials for any batch <= cap: batch * kv_heads * splits <= max(SMs, batch * kv_heads).
+    const size_t parts = std::max((size_t)m.sms, R * c.kv_heads) + 8;
+    if (!m.batch_stream) CH_CUDA_TRY(cudaStreamCreateWithFlags(&m.batch_stream, cudaStreamNonBlocking));
+    bool ok = cudaMalloc(&m.b_meta, meta * 4) == cudaSuccess && cudaMallocHost(&m.h_meta, meta * 4) == cudaSuccess &&
+              cudaMalloc(&m.b_hid, R * H * 4) == cudaSuccess && cudaMalloc(&m.b_q, R * QD * 4) == cudaSuccess &&
+              cudaMalloc(&m.b_logits, R * V * 4) == cudaSuccess && cudaMalloc(&m.b_xb, R * H * 2) == cudaSuccess &&
+              cudaMalloc(&m.b_ab, R * QD * 2) == cudaSuccess && cudaMalloc(&m.b_act, R * I * 2) == cudaSuccess &&
+              cudaMalloc(&m.b_argmax, R * 8) == cudaSuccess && cudaMallocHost(&m.h_argmax, R * 8) == cudaSuccess &&
+              cudaMalloc(&m.b_part_o, parts * kMaxGroup * c.head_dim * 4) == cudaSuccess &&
+              cudaMalloc(&m.b_part_ml, parts * kMaxGroup * 2 * 4) == cudaSuccess &&
+              cudaMalloc(&m.b_tickets, R * c.kv_heads * 4) == cudaSuccess && cudaMalloc(&m.b_error, 4) == cudaSuccess;
+    if (!ok) {
+        m.free_batch();
+        set_error("CUDA backend: batch workspace allocation failed.");
+        return -1;
+    }
+    cudaMemset(m.b_tickets, 0, R * c.kv_heads * 4);
+    cudaMemset(m.b_error, 0, 4);
+    if (make_bf16_tensor_map(&m.map_bxb, m.b_xb, R, H, kGemmBM) != 0 ||
+        make_bf16_tensor_map(&m.map_bab, m.b_ab, R, QD, kGemmBM) != 0 ||
+        make_bf16_tensor_map(&m.map_bact, m.b_act, R, I, kGemmBM) != 0) {
+        m.free_batch();
+        return -1;
+    }
+    m.batch_cap = cap;
+    m.batch_table_cap = table_cap;
+    return 0;
+}
+
+// One decode token for each of B sequences (`ModelForward::forward` with a
+// single token, B times), batched into GEMMs on the tensor cores: the weight
+// stream is shared by the batch; attention reads each sequence's own pages.
+int forward_batch(Model *mp, Seq *const *seqs, const uint32_t *tokens, const size_t *offsets, size_t B,
+                  float *logits_out, uint32_t *argmax_out) {
+    CH_REQUIRE(mp != nullptr && seqs != nullptr && tokens != nullptr && offsets != nullptr,
+               "cheetah_cuda_forward_batch: null argument");
+    Model &m = *mp;
+    const CheetahCudaConfig &c = m.cfg;
+    CH_REQUIRE(B > 0 && B <= 128, "cheetah_cuda_forward_batch: batch must be 1..128");
+    CH_REQUIRE(m.gemm_prefill, "cheetah_cuda_forward_batch: needs bf16 weights and a bf16 KV cache");
+    std::lock_guard<std::mutex> lock(m.batch_mutex);
+    CH_CUDA_TRY(cudaSetDevice(m.device));
+    // Validate, allocate pages, and sync each sequence's own stream.
+    size_t max_pages_used = 1;
+    for (size_t b = 0; b < B; ++b) {
+        Seq *s = seqs[b];
+        CH_REQUIRE(s != nullptr && s->m == mp, "cheetah_cuda_forward_batch: sequence of another model");
+        for (size_t b2 = 0; b2 < b; ++b2) CH_REQUIRE(seqs[b2] != s, "cheetah_cuda_forward_batch: sequence repeated");
+        CH_REQUIRE(tokens[b] < c.vocab_size, "Native backend: token id " + std::to_string(tokens[b]) +
+                                                 " exceeds the vocabulary size " + std::to_string(c.vocab_size) + ".");
+        CH_REQUIRE(offsets[b] == s->positions, "CUDA backend: offset " + std::to_string(offsets[b]) +
+                                                   " does not match the " + std::to_string(s->positions) +
+                                                   " cached positions.");
+        CH_CUDA_TRY(cudaStreamSynchronize(s->stream));
+        if (ensure_pages_upto(*s, offsets[b] + 1) != 0) return -1;
+        max_pages_used = std::max(max_pages_used, s->pages.size());
+    }
+    const int table_stride = (int)((max_pages_used + 15) / 16 * 16);
+    if (ensure_batch_workspace(m, (int)std::max<size_t>(B, 8), table_stride) != 0) return -1;
+    const int cap = m.batch_cap;
+    const int H = c.hidden_size, I = c.intermediate_size, QD = c.q_heads * c.head_dim, KD = c.kv_heads * c.head_dim;
+    // Metadata: tokens | positions | lengths | page tables (stride table_stride).
+    int32_t *h_tok = m.h_meta, *h_pos = m.h_meta + cap, *h_len = m.h_meta + 2 * cap, *h_tab = m.h_meta + 3 * cap;
+    for (size_t b = 0; b < B; ++b) {
+        h_tok[b] = (int32_t)tokens[b];
+        h_pos[b] = (int32_t)offsets[b];
+        h_len[b] = (int32_t)offsets[b] + 1;
+        const Seq *s = seqs[b];
+        for (int i = 0; i < table_stride; ++i) h_tab[b * table_stride + i] = i < (int)s->pages.size() ? s->pages[i] : -1;
+    }
+    cudaStream_t st = m.batch_stream;
+    const bool pdl = m.pdl;
+    CH_CUDA_TRY(cudaMemcpyAsync(m.b_meta, m.h_meta, (size_t)(3 * cap + B * table_stride) * 4, cudaMemcpyHostToDevice, st));
+    const int32_t *d_tok = m.b_meta, *d_pos = m.b_meta + cap, *d_len = m.b_meta + 2 * cap;
+    const int32_t *d_tab = m.b_meta + 3 * cap;
+    const int M = (int)B;
+    CH_CUDA_TRY(cudaMemsetAsync(m.b_argmax, 0, (size_t)B * 8, st));
+    CH_CUDA_TRY(launch_ex(embed_rows_kernel, dim3(M), dim3(256), 0, st, pdl, m.embed, H, d_tok, M, m.b_hid));
+    const int splits = mma_attention_splits(M, c.kv_heads, m.sms);
+    for (uint32_t layer = 0; layer < c.num_layers; ++layer) {
+        const LayerWeights &w = m.layers[layer];
+        CH_CUDA_TRY(launch_ex(norm_rows_bf16_kernel, dim3(M), dim3(256), 0, st, pdl, (const float *)m.b_hid, M, H,
+                              w.ln1, c.rms_eps, m.b_xb));
+        PrefillGemmParams g = {};
+        g.M = M;
+        g.N = QD + 2 * KD;
+        g.K = H;
+        g.bias = w.bqkv;
+        g.out_q_f32 = m.b_q;
+        g.ld_out = QD;
+        g.q_heads = c.q_heads;
+        g.kv_heads = c.kv_heads;
+        g.head_dim = c.head_dim;
+        g.rope_cos = m.rope_cos;
+        g.rope_sin = m.rope_sin;
+        g.page_table = d_tab;
+        g.row_pos = d_pos;
+        g.table_stride = table_stride;
+        g.max_pages = table_stride;
+        g.num_pages = m.num_pages;
+        g.page_tokens = m.page_tokens;
+        g.k_cache = m.k_pool + layer * m.layer_stride_bytes;
+        g.v_cache = m.v_pool + layer * m.layer_stride_bytes;
+        g.kv_f32 = m.kv_f32;
+        g.error = m.b_error;
+        if (launch_prefill_gemm<kPgQkv>(m.map_bxb, w.map_qkv, w.map_qkv, g, st, pdl, m.sms) != 0) return -1;
+
+        MmaAttnParams ap = {};
+        ap.a.q = m.b_q;
+        ap.a.page_table = d_tab;
+        ap.a.seq_lens = d_len;
+        ap.a.max_pages = table_stride;
+        ap.a.num_pages = m.num_pages;
+        ap.a.page_tokens = m.page_tokens;
+        ap.a.batch = M;
+        ap.a.q_heads = c.q_heads;
+        ap.a.kv_heads = c.kv_heads;
+        ap.a.window = c.sliding_window;
+        ap.a.splits = splits;
+        ap.a.scale = 1.0f / sqrtf((float)c.head_dim);
+        ap.a.out_bf16 = m.b_ab;
+        ap.a.part_o = m.b_part_o;
+        ap.a.part_ml = m.b_part_ml;
+        ap.a.tickets = m.b_tickets;
+        ap.a.error = m.b_error;
+        ap.layer_row_offset = (long long)layer * m.num_pages * c.kv_heads * m.page_tokens;
+        ap.page_tokens = m.page_tokens;
+        if (launch_attention_mma(m.k_map, m.v_map, ap, c.head_dim, st, pdl) != 0) return -1;
+
+        PrefillGemmParams o = {};
+        o.M = M;
+        o.N = H;
+        o.K = QD;
+        o.bias = w.bo;
+        o.out_f32 = m.b_hid;
+        o.ld_out = H;
+        o.error = m.b_error;
+        if (launch_prefill_gemm<kPgResidual>(m.map_bab, w.map_o, w.map_o, o, st, pdl, m.sms) != 0) return -1;
+        CH_CUDA_TRY(launch_ex(norm_rows_bf16_kernel, dim3(M), dim3(256), 0, st, pdl, (const float *)m.b_hid, M, H,
+                              w.ln2, c.rms_eps, m.b_xb));
+        PrefillGemmParams gu = {};
+        gu.M = M;
+        gu.N = I;
+        gu.K = H;
+        gu.out_bf16 = m.b_act;
+        gu.ld_out = I;
+        gu.error = m.b_error;
+        if (launch_prefill_gemm<kPgSwiglu>(m.map_bxb, w.map_gate, w.map_up, gu, st, pdl, m.sms) != 0) return -1;
+        PrefillGemmParams dn = {};
+        dn.M = M;
+        dn.N = H;
+        dn.K = I;
+        dn.out_f32 = m.b_hid;
+        dn.ld_out = H;
+        dn.error = m.b_error;
+        if (launch_prefill_gemm<kPgResidual>(m.map_bact, w.map_down, w.map_down, dn, st, pdl, m.sms) != 0) return -1;
+    }
+    CH_CUDA_TRY(launch_ex(norm_rows_bf16_kernel, dim3(M), dim3(256), 0, st, pdl, (const float *)m.b_hid, M, H,
+                          m.final_norm, c.rms_eps, m.b_xb));
+    PrefillGemmParams lm = {};
+    lm.M = M;
+    lm.N = c.vocab_size;
+    lm.K = H;
+    lm.out_f32 = logits_out ? m.b_logits : nullptr;
+    lm.ld_out = c.vocab_size;
+    lm.argmax = m.b_argmax;
+    lm.error = m.b_error;
+    if (launch_prefill_gemm_bn<kPgLogits, 128>(m.map_bxb, m.map_lm_head, m.map_lm_head, lm, st, pdl) != 0) return -1;
+    if (logits_out) {
+        CH_CUDA_TRY(cudaMemcpyAsync(logits_out, m.b_logits, (size_t)B * c.vocab_size * 4, cudaMemcpyDeviceToHost, st));
+    }
+    CH_CUDA_TRY(cudaMemcpyAsync(m.h_argmax, m.b_argmax, (size_t)B * 8, cudaMemcpyDeviceToHost, st));
+    CH_CUDA_TRY(cudaStreamSynchronize(st));
+    int code = 0;
+    CH_CUDA_TRY(cudaMemcpy(&code, m.b_error, 4, cudaMemcpyDeviceToHost));
+    if (code != 0) {
+        cudaMemset(m.b_error, 0, 4);
+        set_error("CUDA backend: device-side guard tripped in a batched step (code " + std::to_string(code) + ").");
+        return -1;
+    }
+    for (size_t b = 0; b < B; ++b) {
+        seqs[b]->positions = offsets[b] + 1;
+        if (argmax_out) argmax_out[b] = (uint32_t)(m.h_argmax[b] & 0xFFFFFFFFull);
+    }
+    return 0;
+}
+
 // Greedy decode entirely on the device: step i consumes the argmax of step
 // i-1 (step 0 consumes `first_token`) at position offset+i. Pages for the
 // whole run are allocated up front; nothing returns to the host between steps.
@@ -1488,6 +1735,12 @@ int cheetah_cuda_forward(CheetahCudaSeq *seq, const uint32_t *tokens, size_t n, 
 int cheetah_cuda_forward_ex(CheetahCudaSeq *seq, const uint32_t *tokens, size_t n, size_t offset,
                             float *logits_out, uint32_t *argmax_out) {
     return cheetah::forward(reinterpret_cast<Seq *>(seq), tokens, n, offset, logits_out, argmax_out);
+}
+
+int cheetah_cuda_forward_batch(CheetahCudaModel *model, CheetahCudaSeq *const *seqs, const uint32_t *tokens,
+                               const size_t *offsets, size_t batch, float *logits_out, uint32_t *argmax_out) {
+    return cheetah::forward_batch(reinterpret_cast<Model *>(model), reinterpret_cast<Seq *const *>(seqs), tokens,
+                                  offsets, batch, logits_out, argmax_out);
 }
 
 int cheetah_cuda_generate_greedy(CheetahCudaSeq *seq, uint32_t first_token, size_t offset, size_t steps,

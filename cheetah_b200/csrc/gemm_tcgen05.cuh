@@ -33,7 +33,7 @@
 
 namespace cheetah {
 
-enum PrefillEpilogue : int { kPgQkv = 0, kPgResidual = 1, kPgSwiglu = 2 };
+enum PrefillEpilogue : int { kPgQkv = 0, kPgResidual = 1, kPgSwiglu = 2, kPgLogits = 3 };
 
 constexpr int kGemmBM = 128;
 constexpr int kGemmBK = 64;
@@ -56,6 +56,13 @@ struct PrefillGemmParams {
     void *k_cache, *v_cache;  // this layer's pool base
     int kv_f32;
     int *error;
+    // Batched decode: row r is sequence r at position row_pos[r] with its page
+    // table at page_table + r * table_stride; q rows go out as f32.
+    const int32_t *row_pos;   // nullptr: position = offset + row (prefill)
+    int table_stride;
+    float *out_q_f32;         // kPgQkv: q [M][q_dim] f32 instead of bf16
+    // kPgLogits: logits [M][ld_out] f32 + per-row packed argmax
+    unsigned long long *argmax;
 };
 
 __device__ __forceinline__ uint64_t umma_smem_desc(uint32_t addr) {
@@ -290,15 +297,38 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                         dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
                     }
                 }
+            } else if (EPI == kPgLogits) {
+                // Logits rows + greedy argmax per row (`engine.rs:2247-2253`).
+                unsigned long long best = 0ull;
+#pragma unroll 1
+                for (int c0 = 0; c0 < BN; c0 += 32) {
+                    float v[32];
+                    tmem_ld32(lane_addr + c0, v);
+                    const int n0 = n_tile * BN + c0;
+                    if (live && n0 < p.N) {
+                        float *dst = p.out_f32 ? p.out_f32 + (long long)row * p.ld_out + n0 : nullptr;
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) {
+                            if (n0 + i < p.N) {
+                                if (dst) dst[i] = v[i];
+                                const unsigned long long key =
+                                    ((unsigned long long)total_order_key(v[i]) << 32) | (unsigned)(n0 + i);
+                                best = key > best ? key : best;
+                            }
+                        }
+                    }
+                }
+                if (live && best != 0ull) atomicMax(p.argmax + row, best);
             } else {  // kPgQkv: BN covers whole heads
                 const int hd = p.head_dim;
                 const int half = hd >> 1;
-                const int pos = p.offset + row;
+                const int pos = p.row_pos ? (live ? p.row_pos[row] : 0) : p.offset + row;
+                const int32_t *table = p.page_table + (p.row_pos ? (long long)row * p.table_stride : 0);
                 // The row's KV slot, resolved once.
                 long long slot_base = -1;  // element index of (page, kv head 0, slot, d 0)
                 if (live) {
                     const int pidx = pos / p.page_tokens;
-                    const int page = pidx < p.max_pages ? p.page_table[pidx] : -1;
+                    const int page = pidx < p.max_pages ? table[pidx] : -1;
                     if (page >= 0 && page < p.num_pages) {
                         slot_base = ((long long)page * p.kv_heads * p.page_tokens + (pos - pidx * p.page_tokens)) * hd;
                     } else if (p.error) {
@@ -346,9 +376,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                             }
                         }
                         if (head < p.q_heads) {
-                            uint16_t *q = p.out_bf16 + (long long)row * p.ld_out + head * hd;
-                            store_bf16x16(q + j, a);
-                            store_bf16x16(q + half + j, b);
+                            if (p.out_q_f32) {
+                                float *q = p.out_q_f32 + (long long)row * p.ld_out + head * hd;
+                                store_f32x16(q + j, a);
+                                store_f32x16(q + half + j, b);
+                            } else {
+                                uint16_t *q = p.out_bf16 + (long long)row * p.ld_out + head * hd;
+                                store_bf16x16(q + j, a);
+                                store_bf16x16(q + half + j, b);
+                            }
                         } else if (slot_base >= 0) {
                             const bool is_k = head < p.q_heads + p.kv_heads;
                             const int kvh = is_k ? head - p.q_heads : head - p.q_heads - p.kv_heads;

@@ -78,6 +78,7 @@ SIGNATURES = {
     "cheetah_cuda_seq_positions": (_I, [_P, C.POINTER(_S)]),
     "cheetah_cuda_forward": (_I, [_P, _P, _S, _S, _P]),
     "cheetah_cuda_forward_ex": (_I, [_P, _P, _S, _S, _P, _P]),
+    "cheetah_cuda_forward_batch": (_I, [_P, _P, _P, _P, _S, _P, _P]),
     "cheetah_cuda_generate_greedy": (_I, [_P, C.c_uint32, _S, _S, _P]),
     "cheetah_cuda_seq_stream": (_I, [_P, C.POINTER(_P)]),
     "cheetah_cuda_seq_snapshot": (_I, [_P, C.POINTER(_P)]),
@@ -175,6 +176,19 @@ class CudaModel:
 
     def new_sequence(self) -> "CudaQwen2":
         return CudaQwen2(self)
+
+    def forward_batch(self, seqs, tokens, offsets, want_logits: bool = False):
+        """One decode token for each sequence (`cheetah_cuda_forward_batch`).
+        Returns the greedy ids (and the [B, vocab] logits when asked)."""
+        B = len(seqs)
+        handles = (C.c_void_p * B)(*[s._h.value for s in seqs])
+        t = np.ascontiguousarray(np.asarray(tokens, dtype=np.uint32))
+        o = np.ascontiguousarray(np.asarray(offsets, dtype=np.uint64))
+        am = np.zeros(B, dtype=np.uint32)
+        logits = np.empty((B, self.cfg["vocab_size"]), dtype=np.float32) if want_logits else None
+        _check(lib().cheetah_cuda_forward_batch(self._h, handles, _ptr(t), _ptr(o), B,
+                                                _ptr(logits) if want_logits else None, _ptr(am)))
+        return (am, logits) if want_logits else am
 
 
 class CudaSnapshot:

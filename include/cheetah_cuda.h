@@ -112,6 +112,18 @@ CHEETAH_CUDA_API int cheetah_cuda_forward(CheetahCudaSeq *seq, const uint32_t *t
 CHEETAH_CUDA_API int cheetah_cuda_forward_ex(CheetahCudaSeq *seq, const uint32_t *tokens, size_t n,
                             size_t offset, float *logits_out, uint32_t *argmax_out);
 
+/* One decode token for each of `batch` (1..128) sequences of `model`: seqs[b]
+ * consumes tokens[b] at position offsets[b] (= its cached position count).
+ * The batch shares one pass over the weights (tensor-core GEMMs); attention
+ * reads each sequence's own pages. logits_out (nullable, host) receives
+ * batch x vocab f32; argmax_out (nullable, host) each row's greedy token
+ * (`engine.rs:2247-2253`). The batched form of `ModelForward::forward`
+ * (`registry.rs:60`) for concurrent sequences (serve: `engine.rs:1874`,
+ * `serve/queue.rs:48-67`). Needs bf16 weights and a bf16 KV cache. */
+CHEETAH_CUDA_API int cheetah_cuda_forward_batch(CheetahCudaModel *model, CheetahCudaSeq *const *seqs,
+                                                const uint32_t *tokens, const size_t *offsets, size_t batch,
+                                                float *logits_out, uint32_t *argmax_out);
+
 /* Greedy decode kept on the device: step i consumes the greedy token of step
  * i-1 (step 0 consumes `first_token`) at position `offset + i`; tokens_out[i]
  * receives step i's greedy token. No host round trip between steps — the

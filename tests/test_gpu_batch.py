@@ -1,0 +1,72 @@
+"""Batched decode (`cheetah_cuda_forward_batch`): one token for each of B
+sequences in one pass over the weights, against the oracle run sequence by
+sequence (`ModelForward::forward`, `qwen2.rs:600-606`)."""
+
+import numpy as np
+import pytest
+
+import oracle as O
+from cheetah_b200.prepared import PreparedModel, resolve_config
+
+pytestmark = pytest.mark.gpu
+torch = pytest.importorskip("torch")
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+
+
+@pytest.mark.parametrize("fixture", ["tiny_prepared", "tiny7b_prepared"])
+def test_batched_decode_matches_per_sequence_oracle(fixture, request):
+    from cheetah_b200 import runtime as R
+    root = request.getfixturevalue(fixture)
+    pm = PreparedModel(root)
+    cfg = resolve_config(pm)
+    model = R.CudaModel(root, max_positions=2048)
+    lengths = [5, 70, 1, 130, 64]
+    rng = np.random.default_rng(21)
+    prompts = [rng.integers(0, cfg["vocab_size"], n).astype(np.uint32) for n in lengths]
+    seqs, refs, toks = [], [], []
+    for prompt in prompts:
+        seq = model.new_sequence()
+        ref = O.OracleModel(pm, cfg)
+        want = ref.forward(prompt, 0)
+        got = seq.forward(prompt, 0)
+        assert np.abs(got - want).max() < 2e-3
+        seqs.append(seq)
+        refs.append(ref)
+        toks.append(int(np.argmax(want)))
+    offsets = list(lengths)
+    for step in range(6):
+        am, logits = model.forward_batch(seqs, toks, offsets, want_logits=True)
+        for b, ref in enumerate(refs):
+            want = ref.forward([toks[b]], offsets[b])
+            assert np.abs(logits[b] - want).max() < 2e-3, (step, b)
+            mx = logits[b].max()
+            assert am[b] == int(np.nonzero(logits[b] == mx)[0][-1])
+            toks[b] = int(np.argmax(want))
+            offsets[b] += 1
+    assert [s.positions() for s in seqs] == offsets
+    # The sequences keep working one at a time afterwards.
+    want = refs[0].forward([toks[0]], offsets[0])
+    assert np.abs(seqs[0].forward([toks[0]], offsets[0]) - want).max() < 2e-3
+
+
+def test_batched_decode_argmax_only_and_errors(tiny_prepared):
+    from cheetah_b200 import runtime as R
+    model = R.CudaModel(tiny_prepared, max_positions=512)
+    a, b = model.new_sequence(), model.new_sequence()
+    a.forward([1, 2, 3], 0)
+    b.forward([4], 0)
+    am = model.forward_batch([a, b], [5, 6], [3, 1])
+    assert am.shape == (2,) and a.positions() == 4 and b.positions() == 2
+    with pytest.raises(R.CheetahCudaError, match="does not match"):
+        model.forward_batch([a, b], [5, 6], [3, 1])
+    with pytest.raises(R.CheetahCudaError, match="repeated"):
+        model.forward_batch([a, a], [5, 6], [4, 4])
+    other = R.CudaModel(tiny_prepared, max_positions=512)
+    c = other.new_sequence()
+    with pytest.raises(R.CheetahCudaError, match="another model"):
+        model.forward_batch([a, c], [5, 6], [4, 0])
