@@ -316,6 +316,107 @@ def decode_7b(args):
     return 0
 
 
+def serve_bench(args):
+    """Config 5: 64 concurrent sequences, prompts ~U[128, 8192], outputs
+    ~U[32, 512] (seed 2); half share a 1024-token prefix (prefilled once,
+    restored from a device snapshot like the engine's prefix cache). The 64
+    sequences are sharded across the ranks (strong scaling); each rank
+    prefills its share, then decodes it with batched steps
+    (cheetah_cuda_forward_batch) until every sequence has its output length.
+    value = generated tokens of all ranks / max-over-ranks decode time."""
+    import torch
+    from cheetah_b200 import runtime as R
+    from cheetah_b200.prepared import PreparedModel, cached_synthetic, resolve_config
+
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300))
+    name = "qwen2-0.5b" if args.workload == "serve-0.5b" else "qwen2-7b"
+    model_dir = cached_synthetic(name)
+    cfg = resolve_config(PreparedModel(model_dir))
+    rng = np.random.default_rng(2)
+    n_seq = 64
+    prompt_len = rng.integers(128, 8193, n_seq)
+    out_len = rng.integers(32, 513, n_seq)
+    shared = rng.permutation(n_seq)[: n_seq // 2]
+    prefix = rng.integers(0, cfg["vocab_size"], 1024).astype(np.uint32)
+    mine = [i for i in range(n_seq) if i % world == rank]
+    pool = int(sum(prompt_len[i] + out_len[i] + 64 for i in mine)) + 4096
+    model = R.CudaModel(model_dir, max_positions=8192 + 512 + 128, kv_pool_tokens=pool, device=local)
+    prompts = {}
+    for i in range(n_seq):
+        body = rng.integers(0, cfg["vocab_size"], int(prompt_len[i])).astype(np.uint32)
+        if i in shared and prompt_len[i] > 1024:
+            body[:1024] = prefix
+        prompts[i] = body
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    snap = None
+    if any(i in shared and prompt_len[i] > 1024 for i in mine):
+        pre = model.new_sequence()
+        pre.forward(prefix, 0)
+        snap = pre.kv_snapshot()
+    seqs, toks, offs, left = [], [], [], []
+    for i in mine:
+        seq = model.new_sequence()
+        start = 0
+        if snap is not None and i in shared and prompt_len[i] > 1024:
+            seq.restore_kv_prefix(snap, 1024)
+            start = 1024
+        logits = seq.forward(prompts[i][start:], start)
+        seqs.append(seq)
+        toks.append(int(np.argmax(logits)))
+        offs.append(int(prompt_len[i]))
+        left.append(int(out_len[i]) - 1)
+    torch.cuda.synchronize()
+    prefill_s = time.perf_counter() - t0
+    prefill_tokens = int(sum(prompt_len[i] for i in mine))
+    if world > 1:
+        torch.distributed.barrier()
+    generated, steps, batch_sizes = len(mine), 0, []
+    t1 = time.perf_counter()
+    active = [j for j in range(len(seqs)) if left[j] > 0]
+    while active:
+        am = model.forward_batch([seqs[j] for j in active], [toks[j] for j in active], [offs[j] for j in active])
+        batch_sizes.append(len(active))
+        for k, j in enumerate(active):
+            toks[j] = int(am[k])
+            offs[j] += 1
+            left[j] -= 1
+            generated += 1
+        active = [j for j in active if left[j] > 0]
+        steps += 1
+    decode_s = time.perf_counter() - t1
+    totals = torch.tensor([decode_s, prefill_s], device="cuda", dtype=torch.float64)
+    counts = torch.tensor([generated, prefill_tokens], device="cuda", dtype=torch.float64)
+    if world > 1:
+        torch.distributed.all_reduce(totals, op=torch.distributed.ReduceOp.MAX)
+        torch.distributed.all_reduce(counts, op=torch.distributed.ReduceOp.SUM)
+    decode_s, prefill_s = float(totals[0]), float(totals[1])
+    generated, prefill_tokens = int(counts[0]), int(counts[1])
+    if rank == 0:
+        line = {"metric": METRIC, "value": generated / decode_s, "unit": "tok/s", "n_gpus": world,
+                "steps": steps, "warmup": 0, "ms_per_step": 1e3 * decode_s / max(steps, 1),
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic (seeded random-init bf16 weights; seeded prompt/output lengths and ids)",
+                "config": {"workload": f"config 5: {name} batched serving, 64 sequences sharded over {world} GPU(s)",
+                           "model": name, "global_batch": n_seq, "parallelism": f"sequence-sharded x{world}"},
+                "decode": {"tokens": generated, "seconds": decode_s,
+                           "timing": "host wall clock around the batched decode loop (each step returns argmax)",
+                           "mean_batch": float(np.mean(batch_sizes)) if batch_sizes else 0.0},
+                "prefill": {"tokens": prefill_tokens, "seconds": prefill_s, "tok_per_s": prefill_tokens / prefill_s}}
+        print(json.dumps(line), flush=True)
+    del seqs
+    model.close()
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+    return 0
+
+
 def run_ours(args):
     import torch
     from cheetah_b200 import runtime as R
@@ -445,7 +546,8 @@ def main():
     ap.add_argument("--quick-attention", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--workload", default="decode-0.5b",
-                    choices=["decode-0.5b", "decode-7b-q8", "decode-7b-q4", "decode-7b-bf16"])
+                    choices=["decode-0.5b", "decode-7b-q8", "decode-7b-q4", "decode-7b-bf16",
+                             "serve-0.5b", "serve-7b"])
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -453,6 +555,8 @@ def main():
         return run_reference(args)
     if args.workload.startswith("decode-7b"):
         return decode_7b(args)
+    if args.workload.startswith("serve"):
+        return serve_bench(args)
     return run_ours(args)
 
 

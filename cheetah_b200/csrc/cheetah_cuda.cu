@@ -355,6 +355,7 @@ struct Model {
     unsigned int *b_tickets = nullptr;
     int *b_error = nullptr;
     CUtensorMap map_bxb{}, map_bab{}, map_bact{};
+    std::map<uint64_t, cudaGraphExec_t> batch_graphs;  // (rows, table stride, logits) -> captured step
     CUtensorMap k_map{};
     CUtensorMap v_map{};
     std::mutex pool_mutex;
@@ -362,6 +363,8 @@ struct Model {
     std::atomic<int> refs{1};
 
     void free_batch() {
+        for (auto &kv : batch_graphs) cudaGraphExecDestroy(kv.second);
+        batch_graphs.clear();
         cudaFree(b_meta);
         cudaFreeHost(h_meta);
         cudaFree(b_hid);
@@ -1433,54 +1436,18 @@ int ensure_batch_workspace(Model &m, int cap, int table_cap) {
     return 0;
 }
 
-// One decode token for each of B sequences (`ModelForward::forward` with a
-// single token, B times), batched into GEMMs on the tensor cores: the weight
-// stream is shared by the batch; attention reads each sequence's own pages.
-int forward_batch(Model *mp, Seq *const *seqs, const uint32_t *tokens, const size_t *offsets, size_t B,
-                  float *logits_out, uint32_t *argmax_out) {
-    CH_REQUIRE(mp != nullptr && seqs != nullptr && tokens != nullptr && offsets != nullptr,
-               "cheetah_cuda_forward_batch: null argument");
-    Model &m = *mp;
-    const CheetahCudaConfig &c = m.cfg;
-    CH_REQUIRE(B > 0 && B <= 128, "cheetah_cuda_forward_batch: batch must be 1..128");
-    CH_REQUIRE(m.gemm_prefill, "cheetah_cuda_forward_batch: needs bf16 weights and a bf16 KV cache");
-    std::lock_guard<std::mutex> lock(m.batch_mutex);
-    CH_CUDA_TRY(cudaSetDevice(m.device));
-    // Validate, allocate pages, and sync each sequence's own stream.
-    size_t max_pages_used = 1;
-    for (size_t b = 0; b < B; ++b) {
-        Seq *s = seqs[b];
-        CH_REQUIRE(s != nullptr && s->m == mp, "cheetah_cuda_forward_batch: sequence of another model");
-        for (size_t b2 = 0; b2 < b; ++b2) CH_REQUIRE(seqs[b2] != s, "cheetah_cuda_forward_batch: sequence repeated");
-        CH_REQUIRE(tokens[b] < c.vocab_size, "Native backend: token id " + std::to_string(tokens[b]) +
-                                                 " exceeds the vocabulary size " + std::to_string(c.vocab_size) + ".");
-        CH_REQUIRE(offsets[b] == s->positions, "CUDA backend: offset " + std::to_string(offsets[b]) +
-                                                   " does not match the " + std::to_string(s->positions) +
-                                                   " cached positions.");
-        CH_CUDA_TRY(cudaStreamSynchronize(s->stream));
-        if (ensure_pages_upto(*s, offsets[b] + 1) != 0) return -1;
-        max_pages_used = std::max(max_pages_used, s->pages.size());
-    }
-    const int table_stride = (int)((max_pages_used + 15) / 16 * 16);
-    if (ensure_batch_workspace(m, (int)std::max<size_t>(B, 8), table_stride) != 0) return -1;
-    const int cap = m.batch_cap;
-    const int H = c.hidden_size, I = c.intermediate_size, QD = c.q_heads * c.head_dim, KD = c.kv_heads * c.head_dim;
-    // Metadata: tokens | positions | lengths | page tables (stride table_stride).
-    int32_t *h_tok = m.h_meta, *h_pos = m.h_meta + cap, *h_len = m.h_meta + 2 * cap, *h_tab = m.h_meta + 3 * cap;
-    for (size_t b = 0; b < B; ++b) {
-        h_tok[b] = (int32_t)tokens[b];
-        h_pos[b] = (int32_t)offsets[b];
-        h_len[b] = (int32_t)offsets[b] + 1;
-        const Seq *s = seqs[b];
-        for (int i = 0; i < table_stride; ++i) h_tab[b * table_stride + i] = i < (int)s->pages.size() ? s->pages[i] : -1;
-    }
+// Enqueue one padded batched decode step (M rows) on the model's batch
+// stream: metadata upload, embeddings, every layer, final norm, lm_head + argmax.
+int enqueue_batch_step(Model &m, int M, int table_stride, bool want_logits) {
     cudaStream_t st = m.batch_stream;
     const bool pdl = m.pdl;
-    CH_CUDA_TRY(cudaMemcpyAsync(m.b_meta, m.h_meta, (size_t)(3 * cap + B * table_stride) * 4, cudaMemcpyHostToDevice, st));
+    const int cap = m.batch_cap;
+    const CheetahCudaConfig &c = m.cfg;
+    const int H = c.hidden_size, I = c.intermediate_size, QD = c.q_heads * c.head_dim, KD = c.kv_heads * c.head_dim;
+    CH_CUDA_TRY(cudaMemcpyAsync(m.b_meta, m.h_meta, (size_t)(3 * cap + M * table_stride) * 4, cudaMemcpyHostToDevice, st));
     const int32_t *d_tok = m.b_meta, *d_pos = m.b_meta + cap, *d_len = m.b_meta + 2 * cap;
     const int32_t *d_tab = m.b_meta + 3 * cap;
-    const int M = (int)B;
-    CH_CUDA_TRY(cudaMemsetAsync(m.b_argmax, 0, (size_t)B * 8, st));
+    CH_CUDA_TRY(cudaMemsetAsync(m.b_argmax, 0, (size_t)M * 8, st));
     CH_CUDA_TRY(launch_ex(embed_rows_kernel, dim3(M), dim3(256), 0, st, pdl, m.embed, H, d_tok, M, m.b_hid));
     const int splits = mma_attention_splits(M, c.kv_heads, m.sms);
     for (uint32_t layer = 0; layer < c.num_layers; ++layer) {
@@ -1567,11 +1534,86 @@ int forward_batch(Model *mp, Seq *const *seqs, const uint32_t *tokens, const siz
     lm.M = M;
     lm.N = c.vocab_size;
     lm.K = H;
-    lm.out_f32 = logits_out ? m.b_logits : nullptr;
+    lm.out_f32 = want_logits ? m.b_logits : nullptr;
     lm.ld_out = c.vocab_size;
     lm.argmax = m.b_argmax;
     lm.error = m.b_error;
     if (launch_prefill_gemm_bn<kPgLogits, 128>(m.map_bxb, m.map_lm_head, m.map_lm_head, lm, st, pdl) != 0) return -1;
+    return 0;
+}
+
+// One decode token for each of B sequences (`ModelForward::forward` with a
+// single token, B times), batched into GEMMs on the tensor cores: the weight
+// stream is shared by the batch; attention reads each sequence's own pages.
+// The step is replayed from a CUDA graph cached per (padded rows, page-table
+// stride, logits wanted).
+int forward_batch(Model *mp, Seq *const *seqs, const uint32_t *tokens, const size_t *offsets, size_t B,
+                  float *logits_out, uint32_t *argmax_out) {
+    CH_REQUIRE(mp != nullptr && seqs != nullptr && tokens != nullptr && offsets != nullptr,
+               "cheetah_cuda_forward_batch: null argument");
+    Model &m = *mp;
+    const CheetahCudaConfig &c = m.cfg;
+    CH_REQUIRE(B > 0 && B <= 128, "cheetah_cuda_forward_batch: batch must be 1..128");
+    CH_REQUIRE(m.gemm_prefill, "cheetah_cuda_forward_batch: needs bf16 weights and a bf16 KV cache");
+    std::lock_guard<std::mutex> lock(m.batch_mutex);
+    CH_CUDA_TRY(cudaSetDevice(m.device));
+    // Validate, allocate pages, and sync each sequence's own stream.
+    size_t max_pages_used = 1;
+    for (size_t b = 0; b < B; ++b) {
+        Seq *s = seqs[b];
+        CH_REQUIRE(s != nullptr && s->m == mp, "cheetah_cuda_forward_batch: sequence of another model");
+        for (size_t b2 = 0; b2 < b; ++b2) CH_REQUIRE(seqs[b2] != s, "cheetah_cuda_forward_batch: sequence repeated");
+        CH_REQUIRE(tokens[b] < c.vocab_size, "Native backend: token id " + std::to_string(tokens[b]) +
+                                                 " exceeds the vocabulary size " + std::to_string(c.vocab_size) + ".");
+        CH_REQUIRE(offsets[b] == s->positions, "CUDA backend: offset " + std::to_string(offsets[b]) +
+                                                   " does not match the " + std::to_string(s->positions) +
+                                                   " cached positions.");
+        CH_CUDA_TRY(cudaStreamSynchronize(s->stream));
+        if (ensure_pages_upto(*s, offsets[b] + 1) != 0) return -1;
+        max_pages_used = std::max(max_pages_used, s->pages.size());
+    }
+    const int table_stride = (int)((max_pages_used + 15) / 16 * 16);
+    // Rows are padded to a multiple of 8 with copies of row 0 (they recompute
+    // and rewrite row 0's K/V bit for bit), so a handful of captured graphs
+    // serve every batch size.
+    const int M = (int)((B + 7) / 8 * 8);
+    if (ensure_batch_workspace(m, std::max(M, 8), table_stride) != 0) return -1;
+    // Metadata: tokens | positions | lengths | page tables (stride table_stride).
+    const int cap = m.batch_cap;
+    int32_t *h_tok = m.h_meta, *h_pos = m.h_meta + cap, *h_len = m.h_meta + 2 * cap, *h_tab = m.h_meta + 3 * cap;
+    for (int r = 0; r < M; ++r) {
+        const size_t b = r < (int)B ? (size_t)r : 0;
+        h_tok[r] = (int32_t)tokens[b];
+        h_pos[r] = (int32_t)offsets[b];
+        h_len[r] = (int32_t)offsets[b] + 1;
+        const Seq *s = seqs[b];
+        for (int i = 0; i < table_stride; ++i) h_tab[r * table_stride + i] = i < (int)s->pages.size() ? s->pages[i] : -1;
+    }
+    const bool want_logits = logits_out != nullptr;
+    const uint64_t key = ((uint64_t)M << 40) | ((uint64_t)table_stride << 8) | (want_logits ? 1u : 0u);
+    auto it = m.batch_graphs.find(key);
+    if (it == m.batch_graphs.end() && env_flag("CHEETAH_CUDA_GRAPH", true)) {
+        cudaGraph_t graph = nullptr;
+        CH_CUDA_TRY(cudaStreamBeginCapture(m.batch_stream, cudaStreamCaptureModeThreadLocal));
+        const int rc = enqueue_batch_step(m, M, table_stride, want_logits);
+        const cudaError_t end_err = cudaStreamEndCapture(m.batch_stream, &graph);
+        if (rc != 0 || end_err != cudaSuccess) {
+            if (graph) cudaGraphDestroy(graph);
+            if (rc == 0) set_error(std::string("batch graph capture failed: ") + cudaGetErrorString(end_err));
+            return -1;
+        }
+        cudaGraphExec_t exec = nullptr;
+        const cudaError_t inst = cudaGraphInstantiate(&exec, graph, 0);
+        cudaGraphDestroy(graph);
+        CH_REQUIRE(inst == cudaSuccess, std::string("batch graph instantiate failed: ") + cudaGetErrorString(inst));
+        it = m.batch_graphs.emplace(key, exec).first;
+    }
+    cudaStream_t st = m.batch_stream;
+    if (it != m.batch_graphs.end()) {
+        CH_CUDA_TRY(cudaGraphLaunch(it->second, st));
+    } else if (enqueue_batch_step(m, M, table_stride, want_logits) != 0) {
+        return -1;
+    }
     if (logits_out) {
         CH_CUDA_TRY(cudaMemcpyAsync(logits_out, m.b_logits, (size_t)B * c.vocab_size * 4, cudaMemcpyDeviceToHost, st));
     }
