@@ -57,6 +57,23 @@ def dist_env():
     return world, rank, local
 
 
+def synthetic_model(name):
+    """The seeded synthetic model, written once per box: local rank 0 writes
+    it, the other ranks wait for its completion marker (no collective, so a
+    slow write cannot time out a process group)."""
+    from cheetah_b200.prepared import cached_synthetic, cached_synthetic_path
+    _, _, local = dist_env()
+    if local == 0:
+        return cached_synthetic(name)
+    target = cached_synthetic_path(name)
+    deadline = time.time() + 1800
+    while not (target / ".complete").exists():
+        if time.time() > deadline:
+            raise RuntimeError(f"timed out waiting for {target}")
+        time.sleep(1.0)
+    return target
+
+
 class ClockSampler:
     """nvidia-smi clocks/throttle reasons sampled during the timed region."""
 
@@ -131,7 +148,7 @@ def run_reference(args):
     if rank != 0:
         return 0
     from cheetah_b200.prepared import PreparedModel, cached_synthetic, resolve_config
-    model_dir = cached_synthetic("qwen2-0.5b")
+    model_dir = synthetic_model("qwen2-0.5b")
     cfg = resolve_config(PreparedModel(model_dir))
     per_step = []
     import oracle as O
@@ -280,7 +297,7 @@ def decode_7b(args):
     from cheetah_b200 import runtime as R
     from cheetah_b200.prepared import PreparedModel, cached_synthetic, resolve_config
     quant = args.workload.split("-")[-1]
-    model_dir = cached_synthetic("qwen2-7b")
+    model_dir = synthetic_model("qwen2-7b")
     cfg = resolve_config(PreparedModel(model_dir))
     hbm_peak, _, peak_kind = peaks()
     model = R.CudaModel(model_dir, quant=quant, max_positions=4096)
@@ -335,7 +352,7 @@ def serve_bench(args):
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=300))
     name = "qwen2-0.5b" if args.workload == "serve-0.5b" else "qwen2-7b"
-    model_dir = cached_synthetic(name)
+    model_dir = synthetic_model(name)
     cfg = resolve_config(PreparedModel(model_dir))
     rng = np.random.default_rng(2)
     n_seq = 64
@@ -432,7 +449,7 @@ def run_ours(args):
         torch.cuda.set_device(local)
     hbm_peak, _, peak_kind = peaks()
 
-    model_dir = cached_synthetic("qwen2-0.5b")
+    model_dir = synthetic_model("qwen2-0.5b")
     cfg = resolve_config(PreparedModel(model_dir))
     total_positions = PROMPT_LEN + args.warmup + args.steps + 8
     model = R.CudaModel(model_dir, device=local, max_positions=max(4096, total_positions + 64))
@@ -519,9 +536,11 @@ def run_ours(args):
     if rank == 0:
         line["roofline"] = gemv_roofline(torch, R, hbm_peak)
         line["roofline"]["peak_kind"] = peak_kind
-        if not args.no_attention:
+        # The op microbench and prefill figures are single-GPU measurements;
+        # a multi-rank run reports the scaled decode line only.
+        if not args.no_attention and world == 1:
             line["attention"] = attention_microbench(torch, R, hbm_peak, quick=args.quick_attention)
-        if not args.no_prefill:
+        if not args.no_prefill and world == 1:
             line["prefill"] = prefill_bench(torch, R, model_dir, cfg)
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(model_dir, cfg, args.cpu_steps)

@@ -26,6 +26,7 @@
 #include "attention.cuh"
 #include "attention_mma.cuh"
 #include "common.cuh"
+#include "decode_megakernel.cuh"
 #include "gemv.cuh"
 #include "gemv_tma.cuh"
 #include "kernels_misc.cuh"
@@ -48,6 +49,13 @@ bool env_flag(const char *name, bool fallback) {
     const char *v = std::getenv(name);
     if (v == nullptr || v[0] == '\0') return fallback;
     return !(v[0] == '0' || v[0] == 'n' || v[0] == 'N' || v[0] == 'f' || v[0] == 'F');
+}
+
+int env_int(const char *name, int fallback) {
+    const char *v = std::getenv(name);
+    if (v == nullptr || v[0] == '\0') return fallback;
+    const int x = std::atoi(v);
+    return x > 0 ? x : fallback;
 }
 
 int sm_count(int device) {
@@ -311,6 +319,12 @@ struct LayerWeights {
     const float *ln2 = nullptr;
     const float *bqkv = nullptr;
     const float *bo = nullptr;
+    // Persistent decode kernel copies: QKV rows as all first rows of the
+    // rotate-half pairs, then all partner rows (a tile of pairs is two
+    // contiguous bulk copies); W_o as head-major [q_heads][hidden][head_dim]
+    // blocks.
+    const uint16_t *mk_qkv = nullptr;
+    const uint16_t *mk_wo = nullptr;
 };
 
 }  // namespace
@@ -341,6 +355,14 @@ struct Model {
     bool qkv_interleaved = false;  // QKV rows stored pair-interleaved (bulk-prefetch GEMV)
     bool gemm_prefill = false;     // bf16 weights with tensor maps: tensor-core chunked prefill
     CUtensorMap map_lm_head{};
+    // Persistent B=1 decode kernel (bf16 weights, bf16 KV): ring slots,
+    // attention key chunks per head, dynamic shared memory, layer table.
+    bool mk_enabled = false;
+    int mk_slots = 0;
+    int mk_att_splits = 1;
+    size_t mk_smem = 0;
+    size_t mk_copy_bytes = 0;  // arena bytes of the decode-kernel weight copies
+    MkLayer *mk_layers = nullptr;
     // Batched decode workspace (one batch at a time per model).
     std::mutex batch_mutex;
     int batch_cap = 0;
@@ -419,6 +441,7 @@ struct Model {
         cudaFree(rope_sin);
         cudaFree(k_pool);
         cudaFree(v_pool);
+        cudaFree(mk_layers);
     }
 };
 
@@ -456,6 +479,10 @@ struct Seq {
     CUtensorMap map_xb{}, map_ab{}, map_act{};
     cudaGraphExec_t graph = nullptr;
     cudaGraphExec_t chain_graph = nullptr;
+    // Persistent decode kernel scratch (allocated on first use).
+    float *mk_opart = nullptr, *mk_att_part = nullptr, *mk_hnew = nullptr;
+    unsigned *mk_ctrl = nullptr;
+    unsigned long long *mk_argmax = nullptr;
 
     ~Seq() {
         cudaSetDevice(m->device);
@@ -471,6 +498,11 @@ struct Seq {
         cudaFree(pact);
         cudaFree(ppart_o);
         cudaFree(ppart_ml);
+        cudaFree(mk_opart);
+        cudaFree(mk_att_part);
+        cudaFree(mk_hnew);
+        cudaFree(mk_ctrl);
+        cudaFree(mk_argmax);
         if (stream) cudaStreamDestroy(stream);
         cudaFree(page_table);
         cudaFree(hidden);
@@ -505,8 +537,104 @@ struct Snapshot {
 namespace {
 
 // Enqueue one decode step (B = 1) on the sequence stream.
+// The persistent decode kernel instance for a model shape: head dim, and
+// per-thread hidden-width slices in registers when hidden <= 1024.
+using MkKernel = void (*)(MkParams);
+MkKernel mk_kernel_for(const CheetahCudaConfig &c) {
+    const bool small = c.hidden_size <= 1024;
+    if (c.head_dim == 64) return small ? decode_megakernel<64, true> : decode_megakernel<64, false>;
+    return small ? decode_megakernel<128, true> : decode_megakernel<128, false>;
+}
+
+int ensure_mk_buffers(Seq &s) {
+    if (s.mk_ctrl != nullptr) return 0;
+    const Model &m = *s.m;
+    const CheetahCudaConfig &c = m.cfg;
+    const size_t parts = (size_t)c.q_heads * m.mk_att_splits * (2 + c.head_dim);
+    bool ok = cudaMalloc(&s.mk_opart, (size_t)c.q_heads * c.hidden_size * 4) == cudaSuccess &&
+              cudaMalloc(&s.mk_att_part, parts * 4) == cudaSuccess &&
+              cudaMalloc(&s.mk_hnew, (size_t)c.hidden_size * 4) == cudaSuccess &&
+              cudaMalloc(&s.mk_ctrl, kMkCtrlWords * 4) == cudaSuccess &&
+              cudaMalloc(&s.mk_argmax, 2 * 8) == cudaSuccess;
+    if (!ok) {
+        set_error("CUDA backend: decode kernel scratch allocation failed.");
+        return -1;
+    }
+    CH_CUDA_TRY(cudaMemset(s.mk_ctrl, 0, kMkCtrlWords * 4));
+    CH_CUDA_TRY(cudaMemset(s.mk_argmax, 0, 2 * 8));
+    CH_CUDA_TRY(cudaMemset(s.mk_att_part, 0, parts * 4));
+    CH_CUDA_TRY(cudaMemset(s.mk_opart, 0, (size_t)c.q_heads * c.hidden_size * 4));
+    return 0;
+}
+
+// One cooperative launch of the persistent decode kernel for `steps` greedy
+// steps starting from s.d_step (token, position, optional page install).
+int launch_megakernel(Seq &s, int steps, float *logits, int32_t *token_log) {
+    Model &m = *s.m;
+    const CheetahCudaConfig &c = m.cfg;
+    MkParams p = {};
+    p.layers = m.mk_layers;
+    p.num_layers = (int)c.num_layers;
+    p.H = (int)c.hidden_size;
+    p.I = (int)c.intermediate_size;
+    p.q_heads = (int)c.q_heads;
+    p.kv_heads = (int)c.kv_heads;
+    p.hd = (int)c.head_dim;
+    p.vocab = (int)c.vocab_size;
+    p.window = (int)c.sliding_window;
+    p.att_splits = m.mk_att_splits;
+    p.slots = m.mk_slots;
+    p.xcap = (int)std::max(c.hidden_size, c.intermediate_size);
+    p.inflight_layers = std::min(m.mk_slots, env_int("CHEETAH_MK_INFLIGHT", 1));
+    p.inflight_lm = std::min(m.mk_slots, env_int("CHEETAH_MK_INFLIGHT_LM", 3));
+    p.eps = c.rms_eps;
+    p.scale_log2 = (1.0f / sqrtf((float)c.head_dim)) * 1.4426950408889634f;
+    p.embed = m.embed;
+    p.lm_head = m.lm_head;
+    p.final_norm = m.final_norm;
+    p.rope_cos = m.rope_cos;
+    p.rope_sin = m.rope_sin;
+    p.k_pool = m.k_pool;
+    p.v_pool = m.v_pool;
+    p.layer_stride_bytes = m.layer_stride_bytes;
+    p.num_pages = m.num_pages;
+    p.page_tokens = m.page_tokens;
+    p.max_pages = s.max_pages;
+    p.page_table = s.page_table;
+    p.step = s.d_step;
+    p.steps = steps;
+    p.hidden = s.hidden;
+    p.q = s.q;
+    p.opart = s.mk_opart;
+    p.hnew = s.mk_hnew;
+    p.act = s.act;
+    p.att_part = s.mk_att_part;
+    p.ctrl = s.mk_ctrl;
+    p.argmax_slots = s.mk_argmax;
+    p.argmax_out = s.argmax;
+    p.token_log = token_log;
+    p.logits = logits;
+    p.error = s.d_error;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(m.sms);
+    cfg.blockDim = dim3(kMkThreads);
+    cfg.dynamicSmemBytes = m.mk_smem;
+    cfg.stream = s.stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    CH_CUDA_TRY(cudaLaunchKernelEx(&cfg, mk_kernel_for(c), p));
+    return 0;
+}
+
 int enqueue_decode_step(Seq &s, bool chain) {
     Model &m = *s.m;
+    if (m.mk_enabled && !chain) {
+        if (ensure_mk_buffers(s) != 0) return -1;
+        return launch_megakernel(s, 1, s.logits, nullptr);
+    }
     const CheetahCudaConfig &c = m.cfg;
     const int hidden = c.hidden_size, inter = c.intermediate_size;
     const int q_dim = c.q_heads * c.head_dim, kv_dim = c.kv_heads * c.head_dim;
@@ -702,6 +830,13 @@ int run_decode_step(Seq &s, uint32_t token, size_t position) {
     s.h_step->token = (int32_t)token;
     s.h_step->position = (int32_t)position;
     s.h_step->seq_len = (int32_t)(position + 1);
+    if (s.m->mk_enabled) {
+        // One cooperative launch per step, issued directly (no graph).
+        CH_CUDA_TRY(cudaMemcpyAsync(s.d_step, s.h_step, sizeof(StepState), cudaMemcpyHostToDevice, s.stream));
+        if (enqueue_decode_step(s, false) != 0) return -1;
+        s.positions = position + 1;
+        return 0;
+    }
     if (s.graph == nullptr) {
         if (env_flag("CHEETAH_CUDA_GRAPH", true)) {
             if (build_decode_graph(s, false, &s.graph) != 0) return -1;
@@ -824,8 +959,29 @@ int open_model(const char *prepared_dir, const CheetahCudaConfig *config, const 
         if (wfmt == kWQ4) return rows * 4 + rows * (size_t)q4_row_bytes((long long)cols) + 256;
         return rows * cols * 2 + 256;
     };
-    const size_t per_layer = linear_bytes(QD + 2 * KD, H) + linear_bytes(H, QD) + 2 * linear_bytes(I, H) +
-                             linear_bytes(H, I) + (2 * H + (QD + 2 * KD) + H) * 4 + 8 * 256;
+    // Persistent decode kernel: bf16 weights and KV, a 4-pair QKV tile and a
+    // down row fit a 32 KB slot, and at least three slots fit beside the
+    // activation vectors in shared memory of a cooperative 1-CTA-per-SM grid.
+    {
+        int coop = 0, optin = 0;
+        cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, device);
+        cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
+        const int xcap = (int)std::max(H, I);
+        const size_t fixed = mk_smem_bytes(0, xcap, (int)H, (int)c.head_dim);
+        const size_t budget = optin > 4096 ? (size_t)optin - 4096 : 0;  // static shared state
+        const int slots = budget > fixed ? (int)std::min<size_t>(kMkMaxSlots, (budget - fixed) / kMkSlotBytes) : 0;
+        m->mk_enabled = env_flag("CHEETAH_CUDA_MEGAKERNEL", true) && coop != 0 && wfmt == kWBf16 && !m->kv_f32 &&
+                        4 * H <= (size_t)kMkSlotBytes && 2 * I <= (size_t)kMkSlotBytes &&
+                        c.q_heads <= (uint32_t)kMkMaxHeads && slots >= 3;
+        if (m->mk_enabled) {
+            m->mk_slots = slots;
+            m->mk_smem = mk_smem_bytes(slots, xcap, (int)H, (int)c.head_dim);
+            m->mk_att_splits = std::max(1, m->sms / (int)c.q_heads);
+        }
+    }
+    size_t per_layer = linear_bytes(QD + 2 * KD, H) + linear_bytes(H, QD) + 2 * linear_bytes(I, H) +
+                       linear_bytes(H, I) + (2 * H + (QD + 2 * KD) + H) * 4 + 8 * 256;
+    if (m->mk_enabled) per_layer += H * QD * 2 + (QD + 2 * KD) * H * 2 + 2 * 256;
     total += per_layer * c.num_layers;
     cudaError_t err = cudaMalloc(&m->arena, total);
     if (err != cudaSuccess) return fail(std::string("CUDA backend: weight allocation failed: ") + cudaGetErrorString(err));
@@ -906,6 +1062,18 @@ int open_model(const char *prepared_dir, const CheetahCudaConfig *config, const 
         out->row_stride = rb;
         return true;
     };
+    // Device copy of host rows for the persistent decode kernel.
+    auto place_copy = [&](const void *src, size_t rows, size_t cols, const uint16_t **out) -> bool {
+        uint8_t *dst = (uint8_t *)m->take(rows * cols * 2);
+        if (dst == nullptr) {
+            error = "CUDA backend: decode kernel weight arena exhausted";
+            return false;
+        }
+        if (!upload(dst, src, rows * cols * 2)) return false;
+        m->mk_copy_bytes += rows * cols * 2;
+        *out = reinterpret_cast<const uint16_t *>(dst);
+        return true;
+    };
     m->layers.resize(c.num_layers);
     for (uint32_t layer = 0; layer < c.num_layers; ++layer) {
         const std::string p = "model.layers." + std::to_string(layer) + ".";
@@ -923,6 +1091,18 @@ int open_model(const char *prepared_dir, const CheetahCudaConfig *config, const 
                 memcpy(staged.data() + row0 * H, bytes, rows_of[k] * H * 2);
                 row0 += rows_of[k];
             }
+            if (m->mk_enabled) {
+                // Pair order: first rows (head * d + i, i < d/2) of every
+                // head, then the partners (+ d/2).
+                const size_t hd = c.head_dim, half = hd / 2, pairs = (QD + 2 * KD) / 2;
+                std::vector<uint16_t> order(staged.size());
+                for (size_t i = 0; i < pairs; ++i) {
+                    const size_t row = (i / half) * hd + (i % half);
+                    memcpy(order.data() + i * H, staged.data() + row * H, H * 2);
+                    memcpy(order.data() + (pairs + i) * H, staged.data() + (row + half) * H, H * 2);
+                }
+                if (!place_copy(order.data(), QD + 2 * KD, H, &w.mk_qkv)) return fail(error);
+            }
             if (m->qkv_interleaved) {
                 const size_t hd = c.head_dim, half = hd / 2, heads = (QD + 2 * KD) / hd;
                 std::vector<uint16_t> perm(staged.size());
@@ -938,6 +1118,20 @@ int open_model(const char *prepared_dir, const CheetahCudaConfig *config, const 
         }
         if (!check_unit(p + "self_attn.o_proj.weight", {H, QD}, &bytes) ||
             !place_linear((const uint16_t *)bytes, H, QD, &w.qo)) return fail(error);
+        if (m->mk_enabled) {
+            // W_o[:, head] blocks, head-major: [q_heads][H][head_dim].
+            const size_t hd = c.head_dim;
+            std::vector<uint16_t> heads_major(H * QD);
+            const uint16_t *src = (const uint16_t *)bytes;
+            for (size_t h = 0; h < c.q_heads; ++h)
+                for (size_t r = 0; r < H; ++r)
+                    memcpy(heads_major.data() + (h * H + r) * hd, src + r * QD + h * hd, hd * 2);
+            uint16_t *dst = (uint16_t *)m->take(heads_major.size() * 2);
+            if (dst == nullptr || !upload(dst, heads_major.data(), heads_major.size() * 2))
+                return fail("CUDA backend: decode kernel weight upload failed");
+            w.mk_wo = dst;
+            m->mk_copy_bytes += heads_major.size() * 2;
+        }
         if (!check_unit(p + "mlp.gate_proj.weight", {I, H}, &bytes) ||
             !place_linear((const uint16_t *)bytes, I, H, &w.qgate)) return fail(error);
         if (!check_unit(p + "mlp.up_proj.weight", {I, H}, &bytes) ||
@@ -986,6 +1180,22 @@ int open_model(const char *prepared_dir, const CheetahCudaConfig *config, const 
     }
 
     cudaFree(staging);
+
+    if (m->mk_enabled) {
+        std::vector<MkLayer> table(c.num_layers);
+        for (uint32_t layer = 0; layer < c.num_layers; ++layer) {
+            const LayerWeights &w = m->layers[layer];
+            table[layer] = MkLayer{w.mk_qkv, w.bqkv, w.mk_wo, w.bo, w.wgate, w.wup, w.wdown, w.ln1, w.ln2};
+        }
+        cudaError_t e = cudaMalloc(&m->mk_layers, table.size() * sizeof(MkLayer));
+        if (e == cudaSuccess) e = cudaMemcpy(m->mk_layers, table.data(), table.size() * sizeof(MkLayer), cudaMemcpyHostToDevice);
+        const MkKernel kernel = mk_kernel_for(c);
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)m->mk_smem);
+        int per_sm = 0;
+        if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kMkThreads, m->mk_smem);
+        if (e != cudaSuccess) return fail(std::string("CUDA backend: decode kernel setup failed: ") + cudaGetErrorString(e));
+        if (per_sm < 1) m->mk_enabled = false;  // the multi-kernel decode path runs instead
+    }
 
     // Prefill GEMM operands (bf16 models with the standard QKV row order).
     bool weight_maps_ok = false;
@@ -1387,6 +1597,7 @@ int check_device_error(Seq &s) {
     CH_CUDA_TRY(cudaMemcpy(&code, s.d_error, 4, cudaMemcpyDeviceToHost));
     if (code != 0) {
         cudaMemset(s.d_error, 0, 4);
+        if (s.mk_ctrl) cudaMemset(s.mk_ctrl, 0, kMkCtrlWords * 4);
         set_error("CUDA backend: device-side guard tripped (code " + std::to_string(code) +
                   "): a bounded wait timed out or a KV page id was out of range.");
         return -1;
@@ -1666,6 +1877,27 @@ int generate_greedy(Seq *s, uint32_t first_token, size_t offset, size_t steps, u
         std::vector<int32_t> ids(s->pages.begin() + first_page, s->pages.end());
         CH_CUDA_TRY(cudaMemcpy(s->page_table + first_page, ids.data(), ids.size() * 4, cudaMemcpyHostToDevice));
     }
+    if (s->m->mk_enabled) {
+        // One cooperative launch runs every step; token i is logged at i.
+        if (ensure_mk_buffers(*s) != 0) return -1;
+        StepState first = {};
+        first.token = (int32_t)first_token;
+        first.position = (int32_t)offset;
+        first.seq_len = (int32_t)offset + 1;
+        first.page_index = -1;
+        first.page_id = -1;
+        *s->h_step = first;
+        CH_CUDA_TRY(cudaMemcpyAsync(s->d_step, s->h_step, sizeof(StepState), cudaMemcpyHostToDevice, s->stream));
+        if (launch_megakernel(*s, (int)steps, nullptr, s->token_log) != 0) return -1;
+        s->positions = offset + steps;
+        if (tokens_out == nullptr) return 0;  // asynchronous: caller synchronises the stream
+        std::vector<int32_t> log(steps);
+        CH_CUDA_TRY(cudaMemcpyAsync(log.data(), s->token_log, steps * 4, cudaMemcpyDeviceToHost, s->stream));
+        CH_CUDA_TRY(cudaStreamSynchronize(s->stream));
+        if (check_device_error(*s) != 0) return -1;
+        for (size_t i = 0; i < steps; ++i) tokens_out[i] = (uint32_t)log[i];
+        return 0;
+    }
     if (s->chain_graph == nullptr && build_decode_graph(*s, true, &s->chain_graph) != 0) return -1;
     StepState init = {};
     init.token = (int32_t)first_token;
@@ -1704,6 +1936,14 @@ extern "C" {
 const char *cheetah_cuda_last_error(void) { return cheetah::last_error(); }
 int cheetah_cuda_abi_version(void) { return CHEETAH_CUDA_ABI_VERSION; }
 
+#ifdef CHEETAH_MK_TRACE
+// Profiling builds only: copy the persistent decode kernel's phase timestamps.
+__attribute__((visibility("default"))) int cheetah_cuda_debug_mk_trace(unsigned long long *out) {
+    CH_CUDA_TRY(cudaMemcpyFromSymbol(out, cheetah::g_mk_trace, sizeof(cheetah::g_mk_trace)));
+    return 0;
+}
+#endif
+
 int cheetah_cuda_device_count(int *count) {
     CH_REQUIRE(count != nullptr, "cheetah_cuda_device_count: null argument");
     int n = 0;
@@ -1729,7 +1969,7 @@ int cheetah_cuda_model_free(CheetahCudaModel *model) {
 int cheetah_cuda_model_info(const CheetahCudaModel *model, CheetahCudaModelInfo *info) {
     CH_REQUIRE(model != nullptr && info != nullptr, "cheetah_cuda_model_info: null argument");
     Model *m = const_cast<Model *>(reinterpret_cast<const Model *>(model));
-    info->weight_bytes = m->arena_used;
+    info->weight_bytes = m->arena_used - m->mk_copy_bytes;  // distinct weights, not the decode-kernel copies
     info->kv_pool_bytes = (uint64_t)m->layer_stride_bytes * m->cfg.num_layers * 2;
     info->kv_pages_total = (uint32_t)m->num_pages;
     {
@@ -1738,6 +1978,8 @@ int cheetah_cuda_model_info(const CheetahCudaModel *model, CheetahCudaModelInfo 
     }
     info->device = m->device;
     info->quant = m->quant;
+    info->persistent_decode = m->mk_enabled ? 1 : 0;
+    info->reserved = 0;
     return 0;
 }
 

@@ -395,11 +395,17 @@ def resolve_config(model: PreparedModel, max_positions: Optional[int] = None) ->
 SHAPES = {"qwen2-0.5b": QWEN2_0_5B, "qwen2-7b": QWEN2_7B, "tiny": TINY, "tiny-7b-heads": TINY_7B_HEADS}
 
 
+def cached_synthetic_path(name: str, seed: int = 0, root: Optional[os.PathLike] = None) -> Path:
+    """Where `cached_synthetic` keeps the model (complete once `.complete` exists)."""
+    base = Path(root or os.environ.get("CHEETAH_MODEL_CACHE", "/tmp/cheetah_models"))
+    return base / f"{name}_seed{seed}"
+
+
 def cached_synthetic(name: str, seed: int = 0, root: Optional[os.PathLike] = None) -> Path:
     """Seeded synthetic prepared model, written once per machine under
     `$CHEETAH_MODEL_CACHE` (default /tmp/cheetah_models) and reused."""
-    base = Path(root or os.environ.get("CHEETAH_MODEL_CACHE", "/tmp/cheetah_models"))
-    target = base / f"{name}_seed{seed}"
+    target = cached_synthetic_path(name, seed, root)
+    base = target.parent
     marker = target / ".complete"
     if marker.exists():
         return target

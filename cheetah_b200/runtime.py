@@ -49,6 +49,7 @@ class ModelInfo(C.Structure):
         ("weight_bytes", C.c_uint64), ("kv_pool_bytes", C.c_uint64),
         ("kv_pages_total", C.c_uint32), ("kv_pages_free", C.c_uint32),
         ("device", C.c_int32), ("quant", C.c_int32),
+        ("persistent_decode", C.c_int32), ("reserved", C.c_int32),
     ]
 
 

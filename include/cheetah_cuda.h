@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define CHEETAH_CUDA_ABI_VERSION 1
+#define CHEETAH_CUDA_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define CHEETAH_CUDA_API __attribute__((visibility("default")))
@@ -72,6 +72,8 @@ typedef struct CheetahCudaModelInfo {
     uint32_t kv_pages_free;
     int32_t device;
     int32_t quant;            /* 0 bf16, 1 q8, 2 q4 */
+    int32_t persistent_decode; /* 1: single-sequence decode runs as one persistent kernel */
+    int32_t reserved;
 } CheetahCudaModelInfo;
 
 /* Thread-local description of the last failure on this thread

@@ -34,7 +34,7 @@ def test_ctypes_signatures_cover_the_header():
 
 
 def test_abi_version():
-    assert R.lib().cheetah_cuda_abi_version() == 1
+    assert R.lib().cheetah_cuda_abi_version() == 2
 
 
 def test_device_count_never_fails():

@@ -1,0 +1,137 @@
+"""The persistent single-sequence decode kernel (one cooperative launch per
+step, or per run of greedy steps) against the CPU oracle and against the
+multi-kernel decode path, through the C-ABI sequence entries.
+
+The persistent kernel serves bf16-weight, bf16-KV models whose shapes fit
+its shared-memory tiles; `CHEETAH_CUDA_MEGAKERNEL=0` at model open selects
+the multi-kernel path for the same model."""
+
+import numpy as np
+import pytest
+
+import oracle as O
+from cheetah_b200.prepared import PreparedModel, resolve_config
+
+pytestmark = pytest.mark.gpu
+torch = pytest.importorskip("torch")
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+
+
+def _model(root, monkeypatch, persistent, max_positions=2048, config=None):
+    from cheetah_b200 import runtime as R
+    monkeypatch.setenv("CHEETAH_CUDA_MEGAKERNEL", "1" if persistent else "0")
+    model = R.CudaModel(root, kv_dtype="bf16", max_positions=max_positions, config=config)
+    assert model.info()["persistent_decode"] == (1 if persistent else 0)
+    return model
+
+
+def _tokens(n, vocab, seed):
+    return np.random.default_rng(seed).integers(0, vocab, n).astype(np.uint32)
+
+
+@pytest.mark.parametrize("fixture", ["tiny_prepared", "tiny7b_prepared"])
+def test_persistent_decode_matches_oracle_and_multikernel_path(fixture, request, monkeypatch):
+    root = request.getfixturevalue(fixture)
+    pm = PreparedModel(root)
+    cfg = resolve_config(pm)
+    ref = O.OracleModel(pm, cfg, "bf16")
+    fast = _model(root, monkeypatch, True)
+    slow = _model(root, monkeypatch, False)
+    prompt = _tokens(45, cfg["vocab_size"], 3)
+    a, b = fast.new_sequence(), slow.new_sequence()
+    la, lb = a.forward(prompt, 0), b.forward(prompt, 0)
+    want = ref.forward(prompt, 0)
+    tok = int(np.argmax(want))
+    assert int(np.argmax(la)) == tok == int(np.argmax(lb))
+    pos = len(prompt)
+    for step in range(20):
+        want = ref.forward([tok], pos)
+        ga, gb = np.empty_like(want), np.empty_like(want)
+        ta = a.forward_greedy([tok], pos, logits_out=ga)
+        tb = b.forward_greedy([tok], pos, logits_out=gb)
+        assert np.abs(ga - want).max() < 2e-3, f"step {step}"
+        assert np.abs(ga - gb).max() < 2e-3, f"step {step}"
+        assert ta == tb == int(np.argmax(want)), f"greedy divergence at step {step}"
+        # Packed-key argmax keeps the larger index on ties (`engine.rs:2247-2253`).
+        assert ta == int(np.nonzero(ga == ga.max())[0][-1])
+        tok = ta
+        pos += 1
+    # Both paths appended the same K/V rows for the decoded positions.
+    ka, va = a.kv_layer(1)
+    kb, vb = b.kv_layer(1)
+    assert np.abs(ka - kb).max() < 2e-2 and np.abs(va - vb).max() < 2e-2
+
+
+def test_persistent_chain_equals_per_token_and_is_reproducible(tiny_prepared, monkeypatch):
+    """One launch for 48 greedy steps gives the per-token launches' tokens;
+    the arithmetic is in fixed order, so logits repeat bit for bit."""
+    model = _model(tiny_prepared, monkeypatch, True)
+    cfg = model.cfg
+    prompt = _tokens(70, cfg["vocab_size"], 5)
+    a = model.new_sequence()
+    first = int(np.argmax(a.forward(prompt, 0)))
+    chain = a.generate_greedy(first, 70, 48)
+    b = model.new_sequence()
+    b.forward(prompt, 0)
+    tok, expect = first, []
+    for i in range(48):
+        tok = b.forward_greedy([tok], 70 + i)
+        expect.append(tok)
+    assert chain.tolist() == expect
+    ka, va = a.kv_layer(0)
+    kb, vb = b.kv_layer(0)
+    np.testing.assert_array_equal(ka, kb)
+    np.testing.assert_array_equal(va, vb)
+    np.testing.assert_array_equal(a.forward([7], 118), b.forward([7], 118))
+    runs = []
+    for _ in range(2):
+        c = model.new_sequence()
+        c.forward(prompt, 0)
+        runs.append(c.forward([first], 70))
+    np.testing.assert_array_equal(runs[0], runs[1])
+
+
+def test_persistent_decode_long_context_and_window(tiny_prepared, monkeypatch):
+    """Key chunks spread over many pages (1.5k positions), and a sliding
+    window that hides the early keys (`ops.rs:1366-1372`)."""
+    pm = PreparedModel(tiny_prepared)
+    for window in (0, 200):
+        cfg = dict(resolve_config(pm, 2048))
+        cfg["sliding_window"] = window
+        ref = O.OracleModel(pm, cfg, "bf16")
+        model = _model(tiny_prepared, monkeypatch, True, config=cfg)
+        seq = model.new_sequence()
+        prompt = _tokens(1500, cfg["vocab_size"], 11 + window)
+        seq.forward(prompt, 0)
+        ref.forward(prompt, 0)
+        for i, tok in enumerate([3, 99, 512]):
+            got = seq.forward([tok], 1500 + i)
+            want = ref.forward([tok], 1500 + i)
+            assert np.abs(got - want).max() < 2e-3, (window, i)
+        model.close()
+
+
+def test_persistent_decode_qwen2_05b_chain_matches_oracle(monkeypatch):
+    """Config 1 shape: a 512-token prompt, then 64 greedy steps in one launch;
+    tokens identical to the reference CPU path."""
+    from cheetah_b200.prepared import cached_synthetic
+    root = cached_synthetic("qwen2-0.5b")
+    pm = PreparedModel(root)
+    cfg = resolve_config(pm, 1024)
+    ref = O.OracleModel(pm, cfg, "bf16")
+    model = _model(root, monkeypatch, True, max_positions=1024)
+    prompt = np.random.default_rng(1).integers(0, cfg["vocab_size"], 512).astype(np.uint32)
+    seq = model.new_sequence()
+    first = int(np.argmax(seq.forward(prompt, 0)))
+    assert first == int(np.argmax(ref.forward(prompt, 0)))
+    chain = seq.generate_greedy(first, 512, 64).tolist()
+    tok, expect = first, []
+    for i in range(64):
+        tok = int(np.argmax(ref.forward([tok], 512 + i)))
+        expect.append(tok)
+    assert chain == expect
