@@ -182,6 +182,12 @@ def run_reference(args):
     return 0
 
 
+# DRAM bytes (read + write) of one decode step of the persistent kernel,
+# Qwen2-0.5B, context ~600: ncu dram__bytes_read.sum + dram__bytes_write.sum
+# of a one-step launch (summary and command in profiles/).
+DECODE_STEP_DRAM_BYTES = 998049536
+
+
 def gemv_roofline(torch, R, hbm_peak, reps=20):
     """Time the lm_head-shaped bf16 GEMV (151936 x 896, 272 MB > L2) with CUDA
     events on its launching stream."""
@@ -434,6 +440,33 @@ def serve_bench(args):
     return 0
 
 
+def op_bench(args):
+    """Config 3 (chunked prefill) or config 2 (decode attention) alone, one GPU."""
+    import torch
+    from cheetah_b200 import runtime as R
+    from cheetah_b200.prepared import PreparedModel, resolve_config
+    torch.cuda.set_device(dist_env()[2])
+    hbm_peak, _, peak_kind = peaks()
+    if args.workload == "attention":
+        rows = attention_microbench(torch, R, hbm_peak, quick=args.quick_attention)
+        best = max((r for r in rows if r["L"] == 32768), key=lambda r: r["GBps"])
+        line = {"metric": METRIC, "value": best["GBps"], "unit": "GB/s", "n_gpus": 1, "steps": 1,
+                "warmup": 3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic (seeded N(0,1) Q/K/V, shuffled pages)",
+                "config": {"workload": "config 2: paged GQA decode attention microbench"},
+                "attention": rows, "peak_kind": peak_kind}
+    else:
+        model_dir = synthetic_model("qwen2-0.5b")
+        cfg = resolve_config(PreparedModel(model_dir))
+        pre = prefill_bench(torch, R, model_dir, cfg)
+        line = {"metric": METRIC, "value": pre["tok_per_s"], "unit": "tok/s", "n_gpus": 1, "steps": 1,
+                "warmup": 1, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic (seeded random-init bf16 weights, uniform-random prompt ids)",
+                "config": {"workload": pre["workload"]}, "prefill": pre}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def run_ours(args):
     import torch
     from cheetah_b200 import runtime as R
@@ -506,14 +539,15 @@ def run_ours(args):
            "api": "cheetah_cuda_forward_ex (host token in, host logits + greedy id out)"}
     del seq2
 
-    # Algorithmic bytes per decode token at the mean context of the timed run.
+    # Algorithmic bytes per decode token at the mean context of the timed run:
+    # every weight byte once + the bf16 K/V rows of the context.
     info = model.info()
     mean_ctx = pos + args.steps / 2
     kv_bytes_per_pos = cfg["num_layers"] * cfg["kv_heads"] * cfg["head_dim"] * 2 * 2
     weight_bytes = info["weight_bytes"]
     step_bytes = weight_bytes + kv_bytes_per_pos * mean_ctx
-    step_gbs = step_bytes / (elapsed / args.steps * world) / 1e9 if world == 1 else \
-        step_bytes / (elapsed / args.steps) / 1e9
+    step_gbs = step_bytes / (elapsed / args.steps) / 1e9
+    persistent = bool(info.get("persistent_decode", 0))
 
     line = {
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
@@ -527,15 +561,23 @@ def run_ours(args):
                    "kv_cache": "paged bf16, 64-token pages", "l2": "inputs larger than L2 "
                    f"(weights {weight_bytes / 1e6:.0f} MB per step > 126 MB L2)"},
         "e2e": e2e,
-        "gpu_launches": args.steps * (2 + 5 * cfg["num_layers"]),
+        # The timed greedy run is one cooperative launch of the persistent
+        # decode kernel (all steps); the multi-kernel path launches an
+        # embedding, 5 kernels per layer and the lm_head per step.
+        "gpu_launches": 1 if persistent else args.steps * (2 + 5 * cfg["num_layers"]),
         "clocks": clock_info,
-        "step_roofline": {"bytes_per_token": step_bytes, "achieved_GBps": step_gbs,
-                          "frac_measured": step_gbs / hbm_peak, "frac_8TBps": step_gbs / 8000.0},
+        # Dominant kernel: the persistent decode kernel, per decode step.
+        # traffic: DRAM bytes of one step from an ncu capture of a one-step
+        # launch at context ~600 (DECODE_STEP_DRAM_BYTES).
+        "roofline": {"bound": "hbm", "kernel": "decode_megakernel" if persistent else "decode step (multi-kernel)",
+                     "achieved": step_gbs, "peak": hbm_peak, "unit": "GB/s", "frac": step_gbs / hbm_peak,
+                     "traffic": DECODE_STEP_DRAM_BYTES if persistent else None,
+                     "algorithmic_bytes_per_step": step_bytes, "us_per_step": 1e6 * elapsed / args.steps,
+                     "frac_8TBps": step_gbs / 8000.0, "peak_kind": peak_kind},
     }
 
     if rank == 0:
-        line["roofline"] = gemv_roofline(torch, R, hbm_peak)
-        line["roofline"]["peak_kind"] = peak_kind
+        line["lm_head_gemv"] = gemv_roofline(torch, R, hbm_peak)
         # The op microbench and prefill figures are single-GPU measurements;
         # a multi-rank run reports the scaled decode line only.
         if not args.no_attention and world == 1:
@@ -566,7 +608,7 @@ def main():
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--workload", default="decode-0.5b",
                     choices=["decode-0.5b", "decode-7b-q8", "decode-7b-q4", "decode-7b-bf16",
-                             "serve-0.5b", "serve-7b"])
+                             "serve-0.5b", "serve-7b", "prefill-0.5b", "attention"])
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -576,6 +618,8 @@ def main():
         return decode_7b(args)
     if args.workload.startswith("serve"):
         return serve_bench(args)
+    if args.workload in ("prefill-0.5b", "attention"):
+        return op_bench(args)
     return run_ours(args)
 
 
