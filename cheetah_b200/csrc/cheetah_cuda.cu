@@ -1937,9 +1937,14 @@ const char *cheetah_cuda_last_error(void) { return cheetah::last_error(); }
 int cheetah_cuda_abi_version(void) { return CHEETAH_CUDA_ABI_VERSION; }
 
 #ifdef CHEETAH_MK_TRACE
-// Profiling builds only: copy the persistent decode kernel's phase timestamps.
+// Profiling builds only: copy the persistent decode kernel's phase timestamps
+// (global timer) and cycle stamps.
 __attribute__((visibility("default"))) int cheetah_cuda_debug_mk_trace(unsigned long long *out) {
     CH_CUDA_TRY(cudaMemcpyFromSymbol(out, cheetah::g_mk_trace, sizeof(cheetah::g_mk_trace)));
+    return 0;
+}
+__attribute__((visibility("default"))) int cheetah_cuda_debug_mk_cycles(long long *out) {
+    CH_CUDA_TRY(cudaMemcpyFromSymbol(out, cheetah::g_mk_cycles, sizeof(cheetah::g_mk_cycles)));
     return 0;
 }
 #endif

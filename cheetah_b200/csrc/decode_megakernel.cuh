@@ -622,6 +622,17 @@ __device__ __forceinline__ float mk_dot(const uint8_t *wa, const float *x, int K
     return warp_sum(__fadd_rn(__fadd_rn(acc[0], acc[1]), __fadd_rn(acc[2], acc[3])));
 }
 
+__device__ __forceinline__ uint32_t mk_lds32(uint32_t addr) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
+    return v;
+}
+__device__ __forceinline__ uint2 mk_lds64(uint32_t addr) {
+    uint2 v;
+    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
+    return v;
+}
+
 // Online-softmax partial of one head over key positions [a, b) (log2
 // domain). Positions [a, sb) were staged in shared memory (stK / stV rows,
 // row = position - a); later ones (this step's position among them) are read
@@ -641,6 +652,7 @@ __device__ void mk_attention_chunk(const MkParams &p, int layer, int head, int a
     const int kvh = head / (p.q_heads / p.kv_heads);
     const uint16_t *kbase = reinterpret_cast<const uint16_t *>(p.k_pool + (long long)layer * p.layer_stride_bytes);
     const uint16_t *vbase = reinterpret_cast<const uint16_t *>(p.v_pool + (long long)layer * p.layer_stride_bytes);
+    const uint32_t stV_s = smem_u32(stV);
     float m = -INFINITY, l = 0.0f;
     float o[kDims];
 #pragma unroll
@@ -675,6 +687,30 @@ __device__ void mk_attention_chunk(const MkParams &p, int layer, int head, int a
 #pragma unroll
         for (int d = 0; d < kDims; ++d) o[d] *= corr;
         m = m_new;
+        if (blk + n <= sb) {
+            // Every position of the block is staged: V rows straight from
+            // shared memory, probabilities broadcast from their lanes.
+            const uint32_t vrow = stV_s + (uint32_t)(((blk - a) * HD + lane * kDims) * 2);
+#pragma unroll
+            for (int k = 0; k < kWarp; ++k) {
+                const float pk = __shfl_sync(0xFFFFFFFFu, pr, k);
+                if (k < n) {
+                    const uint32_t va = vrow + (uint32_t)(k * HD * 2);
+                    if constexpr (HD == 64) {
+                        const uint32_t v = mk_lds32(va);
+                        o[0] = fmaf(pk, bf16_lo(v), o[0]);
+                        o[1] = fmaf(pk, bf16_hi(v), o[1]);
+                    } else {
+                        const uint2 v = mk_lds64(va);
+                        o[0] = fmaf(pk, bf16_lo(v.x), o[0]);
+                        o[1] = fmaf(pk, bf16_hi(v.x), o[1]);
+                        o[2] = fmaf(pk, bf16_lo(v.y), o[2]);
+                        o[3] = fmaf(pk, bf16_hi(v.y), o[3]);
+                    }
+                }
+            }
+            continue;
+        }
         for (int k0 = 0; k0 < n; k0 += kPre) {
             VT vv[kPre];
 #pragma unroll
@@ -867,9 +903,14 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_megakernel(const MkParam
             MkV4 wln{};
             if constexpr (SMALL) wln = mk_ld4<false>(w.ln1, H);
             float pre_ba = 0.0f, pre_bb = 0.0f, pre_c = 1.0f, pre_s = 0.0f;
+            long long pre_row = -1;
             if (lane == 0 && tq.count() > 0 && warp < tq.hi(0) - tq.lo(0)) {
                 const int pair = tq.lo(0) + warp;
                 const int hh = pair / half, i = pair - hh * half;
+                if (hh >= p.q_heads) {
+                    const int kvh = hh < p.q_heads + p.kv_heads ? hh - p.q_heads : hh - p.q_heads - p.kv_heads;
+                    pre_row = mk_kv_row(p, pos, kvh);
+                }
                 if (w.bqkv) {
                     pre_ba = w.bqkv[mk_pair_row(p, pair, 0)];
                     pre_bb = w.bqkv[mk_pair_row(p, pair, 1)];
@@ -944,7 +985,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_megakernel(const MkParam
                         } else {
                             const bool is_k = hh < p.q_heads + p.kv_heads;
                             const int kvh = is_k ? hh - p.q_heads : hh - p.q_heads - p.kv_heads;
-                            const long long row = mk_kv_row(p, pos, kvh);
+                            const long long row = pre ? pre_row : mk_kv_row(p, pos, kvh);
                             if (row >= 0) {
                                 uint16_t *cache = reinterpret_cast<uint16_t *>(
                                     (is_k ? p.k_pool : p.v_pool) + (long long)l * p.layer_stride_bytes);
@@ -976,12 +1017,26 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_megakernel(const MkParam
                 const int cap = (int)(((size_t)p.xcap + H) * 4 / (4 * HD));
                 uint16_t *stV = stK + (size_t)cap * HD;
                 if (threadIdx.x == kWarp) mk_stage_kv<HD>(p, l, kvh, a, b, pos, cap, stK, stV, sh);
+                // This step's key (the last position) joins the staged rows
+                // once QKV has written it: its pool row is resolved now.
+                const bool has_cur = pos >= a && pos < b && pos - a < cap;
+                const long long cur_row = has_cur ? mk_kv_row(p, pos, kvh) : -1;
                 MK_TRACE(t, tb + 11);
                 mk_wait_count(&ctrl[kMkCntQkv], (lg + 1) * G, sh, p.error, t, tb + 12);
                 MK_TRACE(t, tb + 2);
                 for (int d = threadIdx.x; d < HD; d += kMkConsumers) qh[d] = __ldcg(p.q + head * HD + d);
-                const int sb = sh.staged;
-                if (sb > a && !sh.abort) {
+                const int sbulk = sh.staged;  // end of the bulk-staged rows
+                int sb = sbulk;
+                if (has_cur && cur_row >= 0 && sb == pos && !sh.abort) {
+                    const uint16_t *kc = reinterpret_cast<const uint16_t *>(p.k_pool + (long long)l * p.layer_stride_bytes);
+                    const uint16_t *vc = reinterpret_cast<const uint16_t *>(p.v_pool + (long long)l * p.layer_stride_bytes);
+                    for (int d = threadIdx.x; d < HD; d += kMkConsumers) {
+                        stK[(size_t)(pos - a) * HD + d] = __ldcg(kc + cur_row * HD + d);
+                        stV[(size_t)(pos - a) * HD + d] = __ldcg(vc + cur_row * HD + d);
+                    }
+                    sb = pos + 1;
+                }
+                if (sbulk > a && !sh.abort) {
                     if (!mk_bar_wait(smem_u32(&sh.kv_bar), (uint32_t)(sh.kv_uses - 1) & 1u, &sh.abort, true) &&
                         !sh.abort)
                         mk_flag_error(sh, p.error, kMkErrWait);
