@@ -73,7 +73,17 @@ __device__ unsigned long long g_mk_trace[256][128];
             g_mk_trace[blockIdx.x][(ev)] = t__;                                                 \
         }                                                                                       \
     } while (0)
+// Cycle stamps of consumer thread 0 (SM clock) in layer 1 of the first step.
+__device__ long long g_mk_cycles[256][32];
+#define MK_CYC(step, layer, ev)                                                              \
+    do {                                                                                      \
+        if ((step) == 0 && (layer) == 1 && threadIdx.x == 0 && (ev) < 32)                      \
+            g_mk_cycles[blockIdx.x][(ev)] = clock64();                                       \
+    } while (0)
 #else
+#define MK_CYC(step, layer, ev) \
+    do {                        \
+    } while (0)
 #define MK_TRACE(step, ev) \
     do {                   \
     } while (0)
