@@ -560,10 +560,13 @@ int ensure_mk_buffers(Seq &s) {
         set_error("CUDA backend: decode kernel scratch allocation failed.");
         return -1;
     }
-    CH_CUDA_TRY(cudaMemset(s.mk_ctrl, 0, kMkCtrlWords * 4));
-    CH_CUDA_TRY(cudaMemset(s.mk_argmax, 0, 2 * 8));
-    CH_CUDA_TRY(cudaMemset(s.mk_att_part, 0, parts * 4));
-    CH_CUDA_TRY(cudaMemset(s.mk_opart, 0, (size_t)c.q_heads * c.hidden_size * 4));
+    // Stream-ordered before the kernel's first launch on this sequence
+    // (a plain cudaMemset would run on the legacy stream, unordered with
+    // the sequence's non-blocking stream).
+    CH_CUDA_TRY(cudaMemsetAsync(s.mk_ctrl, 0, kMkCtrlWords * 4, s.stream));
+    CH_CUDA_TRY(cudaMemsetAsync(s.mk_argmax, 0, 2 * 8, s.stream));
+    CH_CUDA_TRY(cudaMemsetAsync(s.mk_att_part, 0, parts * 4, s.stream));
+    CH_CUDA_TRY(cudaMemsetAsync(s.mk_opart, 0, (size_t)c.q_heads * c.hidden_size * 4, s.stream));
     return 0;
 }
 
@@ -1433,7 +1436,15 @@ int launch_prefill_gemm_bn(const CUtensorMap &a, const CUtensorMap &b, const CUt
                            const PrefillGemmParams &p, cudaStream_t st, bool pdl) {
     auto kernel = prefill_gemm_kernel<EPI, BN>;
     const size_t smem = prefill_gemm_smem<BN>();
-    CH_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    // The attribute is per function and device; set it once per device.
+    static std::atomic<uint32_t> attr_devices{0};
+    int dev = 0;
+    CH_CUDA_TRY(cudaGetDevice(&dev));
+    const uint32_t bit = dev < 32 ? 1u << dev : 0u;
+    if (bit == 0 || !(attr_devices.load() & bit)) {
+        CH_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        attr_devices.fetch_or(bit);
+    }
     const int n_tiles = EPI == kPgSwiglu ? (p.N + BN / 2 - 1) / (BN / 2) : (p.N + BN - 1) / BN;
     dim3 grid(n_tiles, (p.M + kGemmBM - 1) / kGemmBM);
     CH_CUDA_TRY(launch_ex(kernel, grid, dim3(kGemmThreads), smem, st, pdl, a, b, b2, p));
@@ -1596,8 +1607,8 @@ int check_device_error(Seq &s) {
     int code = 0;
     CH_CUDA_TRY(cudaMemcpy(&code, s.d_error, 4, cudaMemcpyDeviceToHost));
     if (code != 0) {
-        cudaMemset(s.d_error, 0, 4);
-        if (s.mk_ctrl) cudaMemset(s.mk_ctrl, 0, kMkCtrlWords * 4);
+        cudaMemsetAsync(s.d_error, 0, 4, s.stream);
+        if (s.mk_ctrl) cudaMemsetAsync(s.mk_ctrl, 0, kMkCtrlWords * 4, s.stream);
         set_error("CUDA backend: device-side guard tripped (code " + std::to_string(code) +
                   "): a bounded wait timed out or a KV page id was out of range.");
         return -1;
@@ -1634,8 +1645,8 @@ int ensure_batch_workspace(Model &m, int cap, int table_cap) {
         set_error("CUDA backend: batch workspace allocation failed.");
         return -1;
     }
-    cudaMemset(m.b_tickets, 0, R * c.kv_heads * 4);
-    cudaMemset(m.b_error, 0, 4);
+    cudaMemsetAsync(m.b_tickets, 0, R * c.kv_heads * 4, m.batch_stream);
+    cudaMemsetAsync(m.b_error, 0, 4, m.batch_stream);
     if (make_bf16_tensor_map(&m.map_bxb, m.b_xb, R, H, kGemmBM) != 0 ||
         make_bf16_tensor_map(&m.map_bab, m.b_ab, R, QD, kGemmBM) != 0 ||
         make_bf16_tensor_map(&m.map_bact, m.b_act, R, I, kGemmBM) != 0) {
@@ -1833,7 +1844,7 @@ int forward_batch(Model *mp, Seq *const *seqs, const uint32_t *tokens, const siz
     int code = 0;
     CH_CUDA_TRY(cudaMemcpy(&code, m.b_error, 4, cudaMemcpyDeviceToHost));
     if (code != 0) {
-        cudaMemset(m.b_error, 0, 4);
+        cudaMemsetAsync(m.b_error, 0, 4, m.batch_stream);
         set_error("CUDA backend: device-side guard tripped in a batched step (code " + std::to_string(code) + ").");
         return -1;
     }

@@ -913,11 +913,15 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_megakernel(const MkParam
             MkV4 wln{};
             if constexpr (SMALL) wln = mk_ld4<false>(w.ln1, H);
             float pre_ba = 0.0f, pre_bb = 0.0f, pre_c = 1.0f, pre_s = 0.0f;
-            long long pre_row = -1;
+            // The K/V append row is resolved here too, except in the first
+            // layer of the run's first step, where this CTA may still install
+            // the position's page (below): there it is resolved at use.
+            long long pre_row = -2;
+            const bool page_may_change = t == 0 && l == 0;
             if (lane == 0 && tq.count() > 0 && warp < tq.hi(0) - tq.lo(0)) {
                 const int pair = tq.lo(0) + warp;
                 const int hh = pair / half, i = pair - hh * half;
-                if (hh >= p.q_heads) {
+                if (hh >= p.q_heads && !page_may_change) {
                     const int kvh = hh < p.q_heads + p.kv_heads ? hh - p.q_heads : hh - p.q_heads - p.kv_heads;
                     pre_row = mk_kv_row(p, pos, kvh);
                 }
@@ -995,7 +999,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_megakernel(const MkParam
                         } else {
                             const bool is_k = hh < p.q_heads + p.kv_heads;
                             const int kvh = is_k ? hh - p.q_heads : hh - p.q_heads - p.kv_heads;
-                            const long long row = pre ? pre_row : mk_kv_row(p, pos, kvh);
+                            const long long row = (pre && pre_row != -2) ? pre_row : mk_kv_row(p, pos, kvh);
                             if (row >= 0) {
                                 uint16_t *cache = reinterpret_cast<uint16_t *>(
                                     (is_k ? p.k_pool : p.v_pool) + (long long)l * p.layer_stride_bytes);

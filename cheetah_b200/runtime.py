@@ -24,7 +24,8 @@ import numpy as np
 
 from .prepared import PreparedModel, resolve_config
 
-LIB_PATH = Path(__file__).resolve().parent / "libcheetah_cuda.so"
+# The in-tree build; CHEETAH_CUDA_LIB selects another build of the same ABI.
+LIB_PATH = Path(os.environ.get("CHEETAH_CUDA_LIB") or Path(__file__).resolve().parent / "libcheetah_cuda.so")
 
 KV_BF16, KV_F32 = 0, 1
 

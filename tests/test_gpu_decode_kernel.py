@@ -135,3 +135,28 @@ def test_persistent_decode_qwen2_05b_chain_matches_oracle(monkeypatch):
         tok = int(np.argmax(ref.forward([tok], 512 + i)))
         expect.append(tok)
     assert chain == expect
+
+
+def test_persistent_decode_appends_kv_at_page_boundaries(tiny_prepared, monkeypatch):
+    """Tokens whose positions open a new KV page (installed by the kernel
+    itself, positions 0 and 64) land in every layer's cache as on the
+    multi-kernel path."""
+    fast = _model(tiny_prepared, monkeypatch, True)
+    slow = _model(tiny_prepared, monkeypatch, False)
+    cfg = fast.cfg
+    width = cfg["kv_heads"] * cfg["head_dim"]
+    for prompt_len in (0, 64):
+        a, b = fast.new_sequence(), slow.new_sequence()
+        if prompt_len:
+            prompt = _tokens(prompt_len, cfg["vocab_size"], 13)
+            a.forward(prompt, 0)
+            b.forward(prompt, 0)
+        ga = a.forward([7], prompt_len)
+        gb = b.forward([7], prompt_len)
+        assert np.abs(ga - gb).max() < 2e-3
+        for layer in range(cfg["num_layers"]):
+            ka, va = (x.reshape(-1, width) for x in a.kv_layer(layer))
+            kb, vb = (x.reshape(-1, width) for x in b.kv_layer(layer))
+            # the page-opening position's row is written, and matches
+            assert np.abs(ka[prompt_len]).max() > 0 and np.abs(va[prompt_len]).max() > 0, layer
+            assert np.abs(ka - kb).max() < 1e-2 and np.abs(va - vb).max() < 1e-2, layer
