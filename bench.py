@@ -324,7 +324,9 @@ def decode_7b(args):
     info = model.info()
     ctx = 1024 + args.warmup + args.steps / 2
     kv = cfg["num_layers"] * cfg["kv_heads"] * cfg["head_dim"] * 2 * 2 * ctx
-    step_bytes = info["weight_bytes"] + kv
+    # An untied embedding table is not streamed per token: one bf16 row is.
+    embed = 0 if cfg["tie_word_embeddings"] else (cfg["vocab_size"] - 1) * cfg["hidden_size"] * 2
+    step_bytes = info["weight_bytes"] - embed + kv
     gbs = step_bytes / (sec / args.steps) / 1e9
     line = {"metric": METRIC, "value": args.steps / sec, "unit": "tok/s", "n_gpus": 1, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1e3 * sec / args.steps, "higher_is_better": True,

@@ -31,6 +31,7 @@
 #include "gemv_tma.cuh"
 #include "kernels_misc.cuh"
 #include "quant.cuh"
+#include "gemv_qmma.cuh"
 #include "gemm_tcgen05.cuh"
 #include "prefill_attention.cuh"
 #include "store.h"
@@ -187,10 +188,63 @@ int launch_tma_gemv(const GemvParams &p, const TmaGemvPlan &plan, cudaStream_t s
     }
 }
 
-// Decode GEMV dispatch: the bulk-prefetch kernel when its plan exists, the
-// register-streaming kernel otherwise.
+// Tensor-core q8/q4 GEMV: one input vector, dense 16-byte aligned code rows
+// (q8: cols bytes, q4: cols / 2 bytes), widths a multiple of one 64-byte
+// step, whole 16-row tiles.
+bool qmma_eligible(int epi, const GemvParams &p) {
+    if (!env_flag("CHEETAH_CUDA_QMMA", true)) return false;
+    if (p.batch != 1 || (p.wt != kWQ8 && p.wt != kWQ4) || p.scale0 == nullptr || epi == kEpiLogits) return false;
+    const int step = p.wt == kWQ8 ? 64 : 128;
+    if (p.cols % step != 0 || p.cols > 48 * 1024) return false;
+    if (p.row_stride != (p.wt == kWQ8 ? (long long)p.cols : (long long)p.cols / 2)) return false;
+    if (((uintptr_t)p.w0 & 15) != 0 || (epi == kEpiSwiglu && ((uintptr_t)p.w1 & 15) != 0)) return false;
+    if (epi == kEpiSwiglu ? p.rows % 8 != 0 : p.rows % 16 != 0) return false;
+    if (epi == kEpiQkv && (p.head_dim / 2) % 8 != 0) return false;
+    return true;
+}
+
+template <int EPI, int WT, int KS>
+int launch_qmma_ks(const GemvParams &p, cudaStream_t stream, bool pdl, int sms) {
+    auto kernel = gemv_qmma_kernel<EPI, WT, KS>;
+    const size_t smem = (size_t)p.cols * 4 * (p.norm_w ? 2 : 1);
+    if (smem > 48 * 1024)
+        CH_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    int per_sm = 0;
+    CH_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kQmThreads, smem));
+    per_sm = std::max(1, std::min(per_sm, 4));
+    const int tiles = qm_num_tiles(EPI, p.rows);
+    const int per_cta = kQmWarps / KS;
+    const int needed = (tiles + per_cta - 1) / per_cta;
+    const int grid = std::max(1, std::min(needed, sms * per_sm));
+    CH_CUDA_TRY(launch_ex(kernel, dim3(grid), dim3(kQmThreads), smem, stream, pdl, p));
+    return 0;
+}
+
+// Warps per tile: enough warps in all (about 16 per SM) to keep HBM busy,
+// at least two 64-byte steps per warp.
+template <int EPI, int WT>
+int launch_qmma(const GemvParams &p, cudaStream_t stream, bool pdl, int sms) {
+    const int tiles = qm_num_tiles(EPI, p.rows);
+    const int steps = p.cols / (WT == kWQ8 ? 64 : 128);
+    int ks = 1;
+    while (ks < 8 && tiles * ks < 16 * sms && steps >= 4 * ks) ks *= 2;
+    switch (ks) {
+    case 1: return launch_qmma_ks<EPI, WT, 1>(p, stream, pdl, sms);
+    case 2: return launch_qmma_ks<EPI, WT, 2>(p, stream, pdl, sms);
+    case 4: return launch_qmma_ks<EPI, WT, 4>(p, stream, pdl, sms);
+    default: return launch_qmma_ks<EPI, WT, 8>(p, stream, pdl, sms);
+    }
+}
+
+// Decode GEMV dispatch: the tensor-core kernel for q8/q4 shapes it covers,
+// the bulk-prefetch kernel when its plan exists, the register-streaming
+// kernel otherwise.
 template <int EPI>
 int run_gemv(const GemvParams &p, cudaStream_t stream, bool pdl, int sms) {
+    if constexpr (EPI != kEpiLogits) {
+        if (qmma_eligible(EPI, p))
+            return p.wt == kWQ8 ? launch_qmma<EPI, kWQ8>(p, stream, pdl, sms) : launch_qmma<EPI, kWQ4>(p, stream, pdl, sms);
+    }
     TmaGemvPlan plan;
     if (p.batch == 1 && p.wt == kWBf16 && plan_tma_gemv(EPI, p.rows, p.cols, &plan)) {
         return launch_tma_gemv<EPI>(p, plan, stream, pdl, sms);
@@ -1050,11 +1104,15 @@ int open_model(const char *prepared_dir, const CheetahCudaConfig *config, const 
             return true;
         }
         if (!upload(staging, host, rows * cols * 2)) return false;
-        const long long rb = wfmt == kWQ8 ? q8_row_bytes((long long)cols) : q4_row_bytes((long long)cols);
+        // q4 rows whose width is a multiple of 128 are stored cols / 2 bytes
+        // apart (16-byte aligned for the tensor-core GEMV) instead of the
+        // reference's padded row size; the codes and scales are the same.
+        long long rb = wfmt == kWQ8 ? q8_row_bytes((long long)cols) : q4_row_bytes((long long)cols);
+        if (wfmt == kWQ4 && cols % 128 == 0) rb = (long long)cols / 2;
         uint8_t *buf = (uint8_t *)m->take(rows * 4 + rows * (size_t)rb);
         const int blocks = (int)((rows * kWarp + 255) / 256);
-        if (wfmt == kWQ8) quantize_rows_kernel<8><<<blocks, 256>>>(staging, (int)rows, (int)cols, buf);
-        else quantize_rows_kernel<4><<<blocks, 256>>>(staging, (int)rows, (int)cols, buf);
+        if (wfmt == kWQ8) quantize_rows_kernel<8><<<blocks, 256>>>(staging, (int)rows, (int)cols, buf, rb);
+        else quantize_rows_kernel<4><<<blocks, 256>>>(staging, (int)rows, (int)cols, buf, rb);
         cudaError_t e = cudaDeviceSynchronize();
         if (e != cudaSuccess) {
             error = std::string("CUDA backend: quantisation failed: ") + cudaGetErrorString(e);

@@ -17,8 +17,12 @@ __host__ __device__ inline long long q8_row_bytes(long long cols) { return (cols
 // q4.rs:50: (cols + 1).div_ceil(2).div_ceil(4) * 4 (over-pads even widths by 4).
 __host__ __device__ inline long long q4_row_bytes(long long cols) { return ((cols + 2) / 2 + 3) / 4 * 4; }
 
+// out_rb: bytes between output code rows; 0 = the reference row size. A
+// smaller stride (q4 rows of cols / 2 bytes, 16-byte aligned for 128-bit
+// loads) drops only the reference layout's padding bytes.
 template <int BITS>
-__global__ void quantize_rows_kernel(const uint16_t *__restrict__ w, int rows, int cols, uint8_t *__restrict__ out) {
+__global__ void quantize_rows_kernel(const uint16_t *__restrict__ w, int rows, int cols, uint8_t *__restrict__ out,
+                                     long long out_rb = 0) {
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) / kWarp;
     const int lane = threadIdx.x % kWarp;
     if (warp >= rows) return;
@@ -29,7 +33,8 @@ __global__ void quantize_rows_kernel(const uint16_t *__restrict__ w, int rows, i
     const float limit = BITS == 8 ? 127.0f : 7.0f;
     const float scale = max_abs > 0.0f ? __fdiv_rn(max_abs, limit) : 1.0f;
     if (lane == 0) reinterpret_cast<float *>(out)[warp] = scale;
-    const long long rb = BITS == 8 ? q8_row_bytes(cols) : q4_row_bytes(cols);
+    const long long ref_rb = BITS == 8 ? q8_row_bytes(cols) : q4_row_bytes(cols);
+    const long long rb = out_rb > 0 && out_rb < ref_rb ? out_rb : ref_rb;
     uint8_t *codes = out + (long long)rows * 4 + (long long)warp * rb;
     auto code_of = [&](int c) -> int {
         if (c >= cols) return 0;

@@ -38,5 +38,16 @@ def tiny7b_prepared(tmp_path_factory):
     return root
 
 
+@pytest.fixture(scope="session")
+def tiny15b_prepared(tmp_path_factory):
+    """Seeded synthetic model with the 1.5B width and head geometry
+    (hidden 1536, 12q/2kv/128), untied, two layers."""
+    from cheetah_b200.prepared import TINY_15B_HEADS, write_prepared
+
+    root = tmp_path_factory.mktemp("tiny_qwen2_15bheads")
+    write_prepared(root, TINY_15B_HEADS, seed=0)
+    return root
+
+
 def reference_tree() -> Path:
     return Path(os.environ.get("CHEETAH_REFERENCE", "/root/reference"))

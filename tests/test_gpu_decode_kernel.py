@@ -34,7 +34,7 @@ def _tokens(n, vocab, seed):
     return np.random.default_rng(seed).integers(0, vocab, n).astype(np.uint32)
 
 
-@pytest.mark.parametrize("fixture", ["tiny_prepared", "tiny7b_prepared"])
+@pytest.mark.parametrize("fixture", ["tiny_prepared", "tiny7b_prepared", "tiny15b_prepared"])
 def test_persistent_decode_matches_oracle_and_multikernel_path(fixture, request, monkeypatch):
     root = request.getfixturevalue(fixture)
     pm = PreparedModel(root)
