@@ -1,31 +1,29 @@
-// Tensor-core GEMV for q8 / q4 weights (decode, one input vector).
+// Integer tensor-core GEMV for q8 / q4 weights (decode, one input vector).
 //
 // y = scale[r] * sum_k code[r][k] * x[k]  (`ops.rs:544-630`, per-row scales
-// of `q8.rs:91-125` / `q4.rs:126-161`), computed with mma.sync
-// m16n8k16 f16 x f16 -> f32:
-//   A  16 weight rows x 16 codes. int8 and int4 codes are exact in f16; a
-//      code is widened by placing its biased value in the mantissa of 1024
-//      (PRMT / LOP3) and subtracting the bias (one f16x2 subtraction per two
-//      codes), so a q8 code costs about one instruction, not three.
-//   B  the input vector as two f16 columns, hi = f16(x') and lo =
-//      f16(x' - hi), x' = x * 2^e with e chosen from max|x| so that x' stays
-//      far from the f16 overflow and subnormal ranges; hi + lo carries 22
-//      significant bits of x', and the products are exact in the f32
-//      accumulator. The result is scaled back by 2^-e (exact).
+// of `q8.rs:91-125` / `q4.rs:126-161`), computed with integer mma.sync:
+//   A  16 weight rows x 32 codes as s8 (m16n8k32): q8 codes exactly as
+//      stored, no widening instructions; q4 nibbles sign-extended to bytes
+//      in registers (three ALU operations per four codes).
+//   B  the input as a fixed-point integer x' = rint(x * 2^e), e chosen from
+//      max|x| so that |x'| < 2^29, written as four signed base-256 digits,
+//      one B column per digit: the bytes of (x' + 0x80808080) ^ 0x80808080
+//      are the balanced signed digits of x'.
+//   The int32 column sums S_n are exact; sum_n S_n * base^n is formed in 64
+//   bits, partial sums of warps that split a row are added as integers (so
+//   the result does not depend on the split), and the row result is
+//   float(S) * 2^-e * scale. x' keeps 29 bits below max|x|, finer than the
+//   f32 inputs' own rounding for every element within 2^5 of the largest.
 //   The reduction index is permuted: each lane reads 16 contiguous bytes of
 //   its two rows per step (128-bit streaming loads, no shared-memory staging
-//   of weights), and the table of B fragments in shared memory follows the
-//   same permutation, so sum_k A[r][k] B[k] is the row dot product. The
-//   table holds the fragments of a group of 4 (q8) or 8 (q4) inputs where
-//   those inputs were: x is staged into shared memory with one wave of
-//   cp.async and converted in place.
+//   of weights); the digit table in shared memory follows the same order and
+//   occupies exactly the bytes of x it was made from (x is staged with one
+//   wave of cp.async and converted in place).
 // Tiles of 16 rows follow the epilogue: QKV tiles hold 8 rotate-half pairs
 // (rows g and g + 8 of the tile are partners), SwiGLU tiles 8 gate rows and
 // the 8 up rows of the same indices, other tiles 16 consecutive rows. The
 // epilogues are the register-streaming GEMV's (`epilogue_rows`).
 #pragma once
-
-#include <cuda_fp16.h>
 
 #include "common.cuh"
 #include "gemv.cuh"
@@ -55,17 +53,17 @@ __device__ __forceinline__ void qm_tile_rows(const GemvParams &p, int tile, int 
 
 __host__ __device__ inline int qm_num_tiles(int epi, int rows) { return epi == kEpiSwiglu ? rows / 8 : rows / 16; }
 
-__device__ __forceinline__ uint32_t qm_hsub2(uint32_t a, uint32_t b) {
-    uint32_t d;
-    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-    return d;
+__device__ __forceinline__ void qm_imma(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint2 b) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b.x), "r"(b.y));
 }
 
-__device__ __forceinline__ void qm_mma(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint2 b) {
-    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%0,%1,%2,%3};"
-        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b.x), "r"(b.y));
+// Four 4-bit two's-complement codes (low nibbles of the bytes of u) as
+// signed bytes: ((c ^ 8) + 0x78) ^ 0x80 per byte, no carries between bytes.
+__device__ __forceinline__ uint32_t qm_nibbles_s8(uint32_t u) {
+    return (((u & 0x0F0F0F0Fu) ^ 0x08080808u) + 0x78787878u) ^ 0x80808080u;
 }
 
 __device__ __forceinline__ void qm_cp_async16(uint32_t dst, const void *src) {
@@ -81,76 +79,68 @@ __device__ __forceinline__ uint4 qm_ldg(const uint8_t *p) {
     return v;
 }
 
-// f16 pair (hi or lo part) of two scaled inputs.
-__device__ __forceinline__ uint32_t qm_pack(float a, float b) {
-    const __half2 h = __floats2half2_rn(a, b);
-    return *reinterpret_cast<const uint32_t *>(&h);
-}
-__device__ __forceinline__ void qm_split(float v, float &hi, float &lo) {
-    hi = __half2float(__float2half_rn(v));
-    lo = __fsub_rn(v, hi);  // exact: v and hi agree in their top bits
-}
-
-// One step (64 bytes of each of the lane's two rows, 16 at this lane):
-// MMAs over the codes in `wlo` (row g) and `whi` (row g + 8). `tab` is the
-// step's part of the table; lane (n, q) = (lane / 4, lane % 4) of the B
-// fragment reads the entry of input group 4q + j of the step, part n.
+// One step: 16 bytes of each of the lane's two rows (a0/a2 from row g,
+// a1/a3 from row g + 8). `tab` is the step's part of the digit table:
+// groups of 8 inputs, digit n as the 8-byte entry n of the group.
+//   q8: 16 codes per lane, two MMAs; MMA h takes group 2q + h, whose b0/b1
+//       are inputs 0-3 / 4-7.
+//   q4: 32 codes per lane, four MMAs; MMA i takes word i: a0 = its even
+//       codes (low nibbles), a2 = its odd codes, group 4q + i with b0/b1 =
+//       inputs 0,2,4,6 / 1,3,5,7.
 template <int WT>
-__device__ __forceinline__ void qm_step(float (&acc0)[4], float (&acc1)[4], uint4 wlo, uint4 whi, const uint2 *tab,
+__device__ __forceinline__ void qm_step(int (&acc0)[4], int (&acc1)[4], uint4 wlo, uint4 whi, const uint2 *tab,
                                         int lane) {
-    const uint32_t lo[4] = {wlo.x, wlo.y, wlo.z, wlo.w};
-    const uint32_t hi[4] = {whi.x, whi.y, whi.z, whi.w};
+    const int n = lane >> 2, q = lane & 3;
     if (WT == kWQ8) {
-        // word j: codes k0..k0+3, k0 = 64s + 16q + 4j; a0/a2 = (c0,c1)/(c2,c3).
-        const uint32_t bias = 0x64806480u;  // f16 (1152, 1152) = 1024 + 128
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const uint32_t bl = lo[j] ^ 0x80808080u, bh = hi[j] ^ 0x80808080u;
-            const uint32_t a0 = qm_hsub2(__byte_perm(bl, 0x64646464u, 0x4140), bias);
-            const uint32_t a2 = qm_hsub2(__byte_perm(bl, 0x64646464u, 0x4342), bias);
-            const uint32_t a1 = qm_hsub2(__byte_perm(bh, 0x64646464u, 0x4140), bias);
-            const uint32_t a3 = qm_hsub2(__byte_perm(bh, 0x64646464u, 0x4342), bias);
-            const uint2 b = lane < 8 ? tab[2 * (4 * (lane & 3) + j) + (lane >> 2)] : make_uint2(0u, 0u);
-            if (j & 1) qm_mma(acc1, a0, a1, a2, a3, b);
-            else qm_mma(acc0, a0, a1, a2, a3, b);
-        }
+        const uint2 b0 = n < 4 ? tab[(2 * q + 0) * 4 + n] : make_uint2(0u, 0u);
+        const uint2 b1 = n < 4 ? tab[(2 * q + 1) * 4 + n] : make_uint2(0u, 0u);
+        qm_imma(acc0, wlo.x, whi.x, wlo.y, whi.y, b0);
+        qm_imma(acc1, wlo.z, whi.z, wlo.w, whi.w, b1);
     } else {
-        // word j: codes k0..k0+7, k0 = 128s + 32q + 8j (low nibble first);
-        // half h: a0 = (c_2h, c_2h+4), a2 = (c_2h+1, c_2h+5).
-        const uint32_t bias = 0x64086408u;  // f16 (1032, 1032) = 1024 + 8
+        const uint32_t lo[4] = {wlo.x, wlo.y, wlo.z, wlo.w};
+        const uint32_t hi[4] = {whi.x, whi.y, whi.z, whi.w};
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const uint32_t bl = lo[j] ^ 0x88888888u, bh = hi[j] ^ 0x88888888u;
-            uint32_t tl[4], th[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                tl[i] = qm_hsub2(((bl >> (4 * i)) & 0x000F000Fu) | 0x64006400u, bias);
-                th[i] = qm_hsub2(((bh >> (4 * i)) & 0x000F000Fu) | 0x64006400u, bias);
-            }
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const uint2 b = lane < 8 ? tab[4 * (4 * (lane & 3) + j) + 2 * h + (lane >> 2)] : make_uint2(0u, 0u);
-                if (h) qm_mma(acc1, tl[2 * h], th[2 * h], tl[2 * h + 1], th[2 * h + 1], b);
-                else qm_mma(acc0, tl[2 * h], th[2 * h], tl[2 * h + 1], th[2 * h + 1], b);
-            }
+        for (int i = 0; i < 4; ++i) {
+            const uint2 b = n < 4 ? tab[(4 * q + i) * 4 + n] : make_uint2(0u, 0u);
+            const uint32_t a0 = qm_nibbles_s8(lo[i]), a2 = qm_nibbles_s8(lo[i] >> 4);
+            const uint32_t a1 = qm_nibbles_s8(hi[i]), a3 = qm_nibbles_s8(hi[i] >> 4);
+            if (i & 1) qm_imma(acc1, a0, a1, a2, a3, b);
+            else qm_imma(acc0, a0, a1, a2, a3, b);
         }
     }
 }
 
+// Signed base-256 digits of rint(v) (|v| < 2^29), one per byte.
+__device__ __forceinline__ uint32_t qm_digits(float v) {
+    const uint32_t u = (uint32_t)__float2int_rn(v);
+    return (u + 0x80808080u) ^ 0x80808080u;
+}
+
+// Digit n of four inputs' digit strings as one word (byte u = input u).
+__device__ __forceinline__ void qm_transpose4(uint32_t w0, uint32_t w1, uint32_t w2, uint32_t w3, uint32_t (&out)[4]) {
+    const uint32_t t0 = __byte_perm(w0, w1, 0x5140), t1 = __byte_perm(w2, w3, 0x5140);
+    const uint32_t t2 = __byte_perm(w0, w1, 0x7362), t3 = __byte_perm(w2, w3, 0x7362);
+    out[0] = __byte_perm(t0, t1, 0x5410);
+    out[1] = __byte_perm(t0, t1, 0x7632);
+    out[2] = __byte_perm(t2, t3, 0x5410);
+    out[3] = __byte_perm(t2, t3, 0x7632);
+}
+
 // Grid: CTAs over groups of kQmWarps / KS tiles (grid-stride); KS warps
-// split a tile's steps and their partials are summed in warp order.
-// Dynamic shared memory: x, converted in place into the B table (4 bytes
-// per input element), then the RMSNorm weights when norm_w is set.
+// split a tile's steps and their partial sums are added as integers.
+// Dynamic shared memory: x, converted in place into the digit table (4
+// bytes per input element), then the RMSNorm weights when norm_w is set.
 template <int EPI, int WT, int KS>
 __global__ void __launch_bounds__(kQmThreads) gemv_qmma_kernel(const GemvParams p) {
-    constexpr int kT = kQmWarps / KS;                 // tiles per CTA pass
+    constexpr int kT = kQmWarps / KS;  // tiles per CTA pass
     constexpr int kElemsPerStep = WT == kWQ8 ? 64 : 128;
-    constexpr int kU = 4;  // steps of loads in flight per lane
+    constexpr int kDigits = 4;  // base-256 digits of x'
+    constexpr int kU = 4;       // steps of loads in flight per lane
     extern __shared__ __align__(16) float qm_x[];
     uint2 *qm_tab = reinterpret_cast<uint2 *>(qm_x);
     __shared__ float red[kQmWarps];
     __shared__ float redm[kQmWarps];
-    __shared__ float part[kQmWarps][16];
+    __shared__ long long part[kQmWarps][16];
     const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
     const int g = lane >> 2, q = lane & 3;
     const int tile_in = warp / KS, ks = warp % KS;
@@ -203,8 +193,7 @@ __global__ void __launch_bounds__(kQmThreads) gemv_qmma_kernel(const GemvParams 
     pdl_launch_dependents();
 
     // Prologue: x (RMS-normalised when norm_w is set; the same arithmetic
-    // as the register-streaming GEMV), scaled by 2^e, as f16 hi/lo
-    // fragments in the permuted order.
+    // as the register-streaming GEMV), as digits of rint(x * 2^e).
     float inv = 1.0f, inv_esc = 1.0f;
     {
         const float *nw = qm_x + K;
@@ -237,11 +226,12 @@ __global__ void __launch_bounds__(kQmThreads) gemv_qmma_kernel(const GemvParams 
             inv = 1.0f / sqrtf(total / (float)K + p.eps);
             m *= inv;
         }
-        // 2^e with m * 2^e in [2^13, 2^14): far below the f16 maximum (65504).
+        // 2^e with m * 2^e in [2^27, 2^28): |x'| < 2^29 even where the
+        // normalised product rounds above m, so the top digit stays small.
         int e = 0;
         if (m > 0.0f && isfinite(m)) {
             const int ex = (int)((__float_as_uint(m) >> 23) & 0xFF) - 127;
-            e = max(-100, min(100, 13 - ex));
+            e = max(-100, min(100, 27 - ex));
         }
         const float esc = __uint_as_float((uint32_t)(127 + e) << 23);
         inv_esc = __uint_as_float((uint32_t)(127 - e) << 23);
@@ -249,41 +239,31 @@ __global__ void __launch_bounds__(kQmThreads) gemv_qmma_kernel(const GemvParams 
             const float v = p.norm_w ? __fmul_rn(qm_x[i], __fmul_rn(inv, nw[i])) : qm_x[i];
             return __fmul_rn(v, esc);
         };
-        if (WT == kWQ8) {
-            // group G = inputs 4G..4G+3 -> entries 2G (hi) and 2G + 1 (lo):
-            // b0 = (x0, x1), b1 = (x2, x3) of MMA j = G % 4 of step G / 16,
-            // quad q = G % 16 / 4.
-            for (int G = threadIdx.x; G < K / 4; G += kQmThreads) {
-                float h[4], l[4];
+        // Group of 8 inputs -> 4 entries (digit n): q8 b0/b1 = inputs 0-3 /
+        // 4-7, q4 b0/b1 = inputs 0,2,4,6 / 1,3,5,7.
+        for (int G = threadIdx.x; G < K / 8; G += kQmThreads) {
+            uint32_t d[8];
 #pragma unroll
-                for (int u = 0; u < 4; ++u) qm_split(xv(4 * G + u), h[u], l[u]);
-                qm_tab[2 * G] = make_uint2(qm_pack(h[0], h[1]), qm_pack(h[2], h[3]));
-                qm_tab[2 * G + 1] = make_uint2(qm_pack(l[0], l[1]), qm_pack(l[2], l[3]));
+            for (int u = 0; u < 8; ++u) d[u] = qm_digits(xv(8 * G + u));
+            uint32_t o0[4], o1[4];
+            if (WT == kWQ8) {
+                qm_transpose4(d[0], d[1], d[2], d[3], o0);
+                qm_transpose4(d[4], d[5], d[6], d[7], o1);
+            } else {
+                qm_transpose4(d[0], d[2], d[4], d[6], o0);
+                qm_transpose4(d[1], d[3], d[5], d[7], o1);
             }
-        } else {
-            // group G = inputs 8G..8G+7 -> entries 4G + 2h + n: MMA 2j + h
-            // takes b0 = (x_2h, x_2h+4), b1 = (x_2h+1, x_2h+5).
-            for (int G = threadIdx.x; G < K / 8; G += kQmThreads) {
-                float h[8], l[8];
 #pragma unroll
-                for (int u = 0; u < 8; ++u) qm_split(xv(8 * G + u), h[u], l[u]);
-#pragma unroll
-                for (int hh = 0; hh < 2; ++hh) {
-                    const int o = 2 * hh;
-                    qm_tab[4 * G + 2 * hh] = make_uint2(qm_pack(h[o], h[o + 4]), qm_pack(h[o + 1], h[o + 5]));
-                    qm_tab[4 * G + 2 * hh + 1] = make_uint2(qm_pack(l[o], l[o + 4]), qm_pack(l[o + 1], l[o + 5]));
-                }
-            }
+            for (int n = 0; n < 4; ++n) qm_tab[4 * G + n] = make_uint2(o0[n], o1[n]);
         }
     }
     __syncthreads();
 
     unsigned long long best = 0ull;
     for (; tile - tile_in < tiles; tile += tile_stride) {
-        float acc0[4] = {0.0f, 0.0f, 0.0f, 0.0f}, acc1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        int acc0[4] = {0, 0, 0, 0}, acc1[4] = {0, 0, 0, 0};
         if (tile < tiles) {
-            // The next batch's loads are issued before this batch's MMAs
-            // (measured faster than refilling each slot as it is consumed).
+            // The next batch's loads are issued before this batch's MMAs.
             for (int s0 = s_begin; s0 < s_end; s0 += kU) {
                 uint4 cl[kU], chh[kU];
 #pragma unroll
@@ -310,9 +290,17 @@ __global__ void __launch_bounds__(kQmThreads) gemv_qmma_kernel(const GemvParams 
             load_scales(tile);
             tile = cur;
         }
-        // Columns 0 (hi) and 1 (lo) of lane q == 0: rows g and g + 8.
-        float vlo = __fadd_rn(__fadd_rn(acc0[0], acc1[0]), __fadd_rn(acc0[1], acc1[1]));
-        float vhi = __fadd_rn(__fadd_rn(acc0[2], acc1[2]), __fadd_rn(acc0[3], acc1[3]));
+        // Lane q holds columns (digits) 2q and 2q + 1 of rows g and g + 8.
+        long long vlo = 0, vhi = 0;
+        if (2 * q < kDigits) {
+            const int s0 = 8 * 2 * q, s1 = 8 * (2 * q + 1);
+            vlo = ((long long)acc0[0] + acc1[0]) * (1ll << s0) + ((long long)acc0[1] + acc1[1]) * (1ll << s1);
+            vhi = ((long long)acc0[2] + acc1[2]) * (1ll << s0) + ((long long)acc0[3] + acc1[3]) * (1ll << s1);
+        }
+        vlo += __shfl_xor_sync(0xFFFFFFFFu, vlo, 1);
+        vhi += __shfl_xor_sync(0xFFFFFFFFu, vhi, 1);
+        vlo += __shfl_xor_sync(0xFFFFFFFFu, vlo, 2);
+        vhi += __shfl_xor_sync(0xFFFFFFFFu, vhi, 2);
         if (KS > 1) {
             if (q == 0) {
                 part[warp][g] = vlo;
@@ -320,12 +308,10 @@ __global__ void __launch_bounds__(kQmThreads) gemv_qmma_kernel(const GemvParams 
             }
             __syncthreads();
             if (ks == 0 && q == 0) {
-                vlo = part[warp][g];
-                vhi = part[warp][g + 8];
 #pragma unroll
                 for (int k = 1; k < KS; ++k) {
-                    vlo = __fadd_rn(vlo, part[warp + k][g]);
-                    vhi = __fadd_rn(vhi, part[warp + k][g + 8]);
+                    vlo += part[warp + k][g];
+                    vhi += part[warp + k][g + 8];
                 }
             }
             __syncthreads();
@@ -333,9 +319,9 @@ __global__ void __launch_bounds__(kQmThreads) gemv_qmma_kernel(const GemvParams 
         if (ks == 0 && q == 0 && tile < tiles) {
             int rl, rh;
             qm_tile_rows<EPI>(p, tile, g, rl, rh);
-            vlo = __fmul_rn(__fmul_rn(vlo, inv_esc), sl);
-            vhi = __fmul_rn(__fmul_rn(vhi, inv_esc), sh);
-            epilogue_rows<EPI>(p, 0, rl, rh, vlo, vhi, best);
+            const float flo = __fmul_rn(__fmul_rn(__ll2float_rn(vlo), inv_esc), sl);
+            const float fhi = __fmul_rn(__fmul_rn(__ll2float_rn(vhi), inv_esc), sh);
+            epilogue_rows<EPI>(p, 0, rl, rh, flo, fhi, best);
         }
     }
 }
