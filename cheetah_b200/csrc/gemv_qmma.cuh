@@ -135,7 +135,11 @@ __global__ void __launch_bounds__(kQmThreads) gemv_qmma_kernel(const GemvParams 
     constexpr int kT = kQmWarps / KS;  // tiles per CTA pass
     constexpr int kElemsPerStep = WT == kWQ8 ? 64 : 128;
     constexpr int kDigits = 4;  // base-256 digits of x'
-    constexpr int kU = 4;       // steps of loads in flight per lane
+    // Steps of loads in flight per lane. q8: batches of 4, the next batch
+    // issued before this one's MMAs; q4 (more MMA work per byte): a ring of
+    // 8, a slot refilled as soon as it is consumed (measured best for each).
+    constexpr bool kRing = WT == kWQ4;
+    constexpr int kU = kRing ? 8 : 4;
     extern __shared__ __align__(16) float qm_x[];
     uint2 *qm_tab = reinterpret_cast<uint2 *>(qm_x);
     __shared__ float red[kQmWarps];
@@ -263,19 +267,33 @@ __global__ void __launch_bounds__(kQmThreads) gemv_qmma_kernel(const GemvParams 
     for (; tile - tile_in < tiles; tile += tile_stride) {
         int acc0[4] = {0, 0, 0, 0}, acc1[4] = {0, 0, 0, 0};
         if (tile < tiles) {
-            // The next batch's loads are issued before this batch's MMAs.
             for (int s0 = s_begin; s0 < s_end; s0 += kU) {
-                uint4 cl[kU], chh[kU];
+                if constexpr (kRing) {
 #pragma unroll
-                for (int u = 0; u < kU; ++u) {
-                    cl[u] = la[u];
-                    chh[u] = ha[u];
-                }
-                if (s0 + kU < s_end) load(s0 + kU);
+                    for (int u = 0; u < kU; ++u) {
+                        const int s = s0 + u;
+                        if (s < s_end) {
+                            qm_step<WT>(acc0, acc1, la[u], ha[u], qm_tab + (size_t)s * (kElemsPerStep / 2), lane);
+                            if (s + kU < s_end) {
+                                la[u] = qm_ldg(plo + (long long)(s + kU) * 64);
+                                ha[u] = qm_ldg(phi + (long long)(s + kU) * 64);
+                            }
+                        }
+                    }
+                } else {
+                    uint4 cl[kU], chh[kU];
 #pragma unroll
-                for (int u = 0; u < kU; ++u) {
-                    if (s0 + u < s_end)
-                        qm_step<WT>(acc0, acc1, cl[u], chh[u], qm_tab + (size_t)(s0 + u) * (kElemsPerStep / 2), lane);
+                    for (int u = 0; u < kU; ++u) {
+                        cl[u] = la[u];
+                        chh[u] = ha[u];
+                    }
+                    if (s0 + kU < s_end) load(s0 + kU);
+#pragma unroll
+                    for (int u = 0; u < kU; ++u) {
+                        if (s0 + u < s_end)
+                            qm_step<WT>(acc0, acc1, cl[u], chh[u], qm_tab + (size_t)(s0 + u) * (kElemsPerStep / 2),
+                                        lane);
+                    }
                 }
             }
         }
