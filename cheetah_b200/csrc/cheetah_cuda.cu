@@ -429,6 +429,9 @@ struct Model {
     unsigned long long *b_argmax = nullptr, *h_argmax = nullptr;
     float *b_part_o = nullptr, *b_part_ml = nullptr;
     unsigned int *b_tickets = nullptr;
+    // Split-K GEMM partial tiles (SMs x 128 x 128 f32) and tile tickets.
+    float *b_split_ws = nullptr;
+    unsigned *b_split_tickets = nullptr;
     int *b_error = nullptr;
     CUtensorMap map_bxb{}, map_bab{}, map_bact{};
     std::map<uint64_t, cudaGraphExec_t> batch_graphs;  // (rows, table stride, logits) -> captured step
@@ -454,6 +457,8 @@ struct Model {
         cudaFree(b_part_o);
         cudaFree(b_part_ml);
         cudaFree(b_tickets);
+        cudaFree(b_split_ws);
+        cudaFree(b_split_tickets);
         cudaFree(b_error);
         b_meta = h_meta = nullptr;
         b_hid = b_q = b_logits = nullptr;
@@ -461,6 +466,8 @@ struct Model {
         b_argmax = h_argmax = nullptr;
         b_part_o = b_part_ml = nullptr;
         b_tickets = nullptr;
+        b_split_ws = nullptr;
+        b_split_tickets = nullptr;
         b_error = nullptr;
         batch_cap = batch_table_cap = 0;
     }
@@ -1491,7 +1498,7 @@ int ensure_prefill_buffers(Seq &s, int rows) {
 
 template <int EPI, int BN>
 int launch_prefill_gemm_bn(const CUtensorMap &a, const CUtensorMap &b, const CUtensorMap &b2,
-                           const PrefillGemmParams &p, cudaStream_t st, bool pdl) {
+                           const PrefillGemmParams &p, cudaStream_t st, bool pdl, int splits = 1) {
     auto kernel = prefill_gemm_kernel<EPI, BN>;
     const size_t smem = prefill_gemm_smem<BN>();
     // The attribute is per function and device; set it once per device.
@@ -1504,21 +1511,32 @@ int launch_prefill_gemm_bn(const CUtensorMap &a, const CUtensorMap &b, const CUt
         attr_devices.fetch_or(bit);
     }
     const int n_tiles = EPI == kPgSwiglu ? (p.N + BN / 2 - 1) / (BN / 2) : (p.N + BN - 1) / BN;
-    dim3 grid(n_tiles, (p.M + kGemmBM - 1) / kGemmBM);
+    dim3 grid(n_tiles, (p.M + kGemmBM - 1) / kGemmBM, splits);
     CH_CUDA_TRY(launch_ex(kernel, grid, dim3(kGemmThreads), smem, st, pdl, a, b, b2, p));
     return 0;
 }
 
 // Tile width: 64-column tiles double the CTA count of the narrow GEMMs
-// (QKV, o_proj, down at chunk sizes of a few hundred rows).
+// (QKV, o_proj, down at chunk sizes of a few hundred rows). With a split-K
+// workspace (batched decode: one row tile), a grid of fewer than half the
+// SMs is split along K into up to SMs / tiles parts of at least eight
+// k-blocks each (the workspace holds SMs tiles of 128 x 128 f32).
 template <int EPI>
 int launch_prefill_gemm(const CUtensorMap &a, const CUtensorMap &b, const CUtensorMap &b2, const PrefillGemmParams &p,
                         cudaStream_t st, bool pdl, int sms) {
     const int m_tiles = (p.M + kGemmBM - 1) / kGemmBM;
     const bool narrow = EPI != kPgSwiglu && (EPI != kPgQkv || p.head_dim == 64) &&
                         ((p.N + 127) / 128) * m_tiles < sms;
-    if (narrow) return launch_prefill_gemm_bn<EPI, 64>(a, b, b2, p, st, pdl);
-    return launch_prefill_gemm_bn<EPI, 128>(a, b, b2, p, st, pdl);
+    const int bn = narrow ? 64 : 128;
+    const int tiles = m_tiles * (EPI == kPgSwiglu ? (p.N + bn / 2 - 1) / (bn / 2) : (p.N + bn - 1) / bn);
+    int splits = 1;
+    if (p.split_ws != nullptr && p.split_tickets != nullptr && 2 * tiles <= sms &&
+        env_flag("CHEETAH_CUDA_GEMM_SPLITK", true)) {
+        const int k_total = (p.K + kGemmBK - 1) / kGemmBK;
+        splits = std::max(1, std::min(k_total / 8, sms / tiles));
+    }
+    if (narrow) return launch_prefill_gemm_bn<EPI, 64>(a, b, b2, p, st, pdl, splits);
+    return launch_prefill_gemm_bn<EPI, 128>(a, b, b2, p, st, pdl, splits);
 }
 
 // One prompt chunk through every layer on the tensor cores
@@ -1697,13 +1715,16 @@ int ensure_batch_workspace(Model &m, int cap, int table_cap) {
               cudaMalloc(&m.b_argmax, R * 8) == cudaSuccess && cudaMallocHost(&m.h_argmax, R * 8) == cudaSuccess &&
               cudaMalloc(&m.b_part_o, parts * kMaxGroup * c.head_dim * 4) == cudaSuccess &&
               cudaMalloc(&m.b_part_ml, parts * kMaxGroup * 2 * 4) == cudaSuccess &&
-              cudaMalloc(&m.b_tickets, R * c.kv_heads * 4) == cudaSuccess && cudaMalloc(&m.b_error, 4) == cudaSuccess;
+              cudaMalloc(&m.b_tickets, R * c.kv_heads * 4) == cudaSuccess && cudaMalloc(&m.b_error, 4) == cudaSuccess &&
+              cudaMalloc(&m.b_split_ws, (size_t)m.sms * kGemmBM * 128 * 4) == cudaSuccess &&
+              cudaMalloc(&m.b_split_tickets, (size_t)m.sms * 4) == cudaSuccess;
     if (!ok) {
         m.free_batch();
         set_error("CUDA backend: batch workspace allocation failed.");
         return -1;
     }
     cudaMemsetAsync(m.b_tickets, 0, R * c.kv_heads * 4, m.batch_stream);
+    cudaMemsetAsync(m.b_split_tickets, 0, (size_t)m.sms * 4, m.batch_stream);
     cudaMemsetAsync(m.b_error, 0, 4, m.batch_stream);
     if (make_bf16_tensor_map(&m.map_bxb, m.b_xb, R, H, kGemmBM) != 0 ||
         make_bf16_tensor_map(&m.map_bab, m.b_ab, R, QD, kGemmBM) != 0 ||
@@ -1756,6 +1777,8 @@ int enqueue_batch_step(Model &m, int M, int table_stride, bool want_logits) {
         g.v_cache = m.v_pool + layer * m.layer_stride_bytes;
         g.kv_f32 = m.kv_f32;
         g.error = m.b_error;
+        g.split_ws = m.b_split_ws;
+        g.split_tickets = m.b_split_tickets;
         if (launch_prefill_gemm<kPgQkv>(m.map_bxb, w.map_qkv, w.map_qkv, g, st, pdl, m.sms) != 0) return -1;
 
         MmaAttnParams ap = {};
@@ -1788,6 +1811,8 @@ int enqueue_batch_step(Model &m, int M, int table_stride, bool want_logits) {
         o.out_f32 = m.b_hid;
         o.ld_out = H;
         o.error = m.b_error;
+        o.split_ws = m.b_split_ws;
+        o.split_tickets = m.b_split_tickets;
         if (launch_prefill_gemm<kPgResidual>(m.map_bab, w.map_o, w.map_o, o, st, pdl, m.sms) != 0) return -1;
         CH_CUDA_TRY(launch_ex(norm_rows_bf16_kernel, dim3(M), dim3(256), 0, st, pdl, (const float *)m.b_hid, M, H,
                               w.ln2, c.rms_eps, m.b_xb));
@@ -1798,6 +1823,8 @@ int enqueue_batch_step(Model &m, int M, int table_stride, bool want_logits) {
         gu.out_bf16 = m.b_act;
         gu.ld_out = I;
         gu.error = m.b_error;
+        gu.split_ws = m.b_split_ws;
+        gu.split_tickets = m.b_split_tickets;
         if (launch_prefill_gemm<kPgSwiglu>(m.map_bxb, w.map_gate, w.map_up, gu, st, pdl, m.sms) != 0) return -1;
         PrefillGemmParams dn = {};
         dn.M = M;
@@ -1806,6 +1833,8 @@ int enqueue_batch_step(Model &m, int M, int table_stride, bool want_logits) {
         dn.out_f32 = m.b_hid;
         dn.ld_out = H;
         dn.error = m.b_error;
+        dn.split_ws = m.b_split_ws;
+        dn.split_tickets = m.b_split_tickets;
         if (launch_prefill_gemm<kPgResidual>(m.map_bact, w.map_down, w.map_down, dn, st, pdl, m.sms) != 0) return -1;
     }
     CH_CUDA_TRY(launch_ex(norm_rows_bf16_kernel, dim3(M), dim3(256), 0, st, pdl, (const float *)m.b_hid, M, H,
@@ -1903,6 +1932,8 @@ int forward_batch(Model *mp, Seq *const *seqs, const uint32_t *tokens, const siz
     CH_CUDA_TRY(cudaMemcpy(&code, m.b_error, 4, cudaMemcpyDeviceToHost));
     if (code != 0) {
         cudaMemsetAsync(m.b_error, 0, 4, m.batch_stream);
+        // A split whose wait gave up never took its ticket: start them over.
+        cudaMemsetAsync(m.b_split_tickets, 0, (size_t)m.sms * 4, m.batch_stream);
         set_error("CUDA backend: device-side guard tripped in a batched step (code " + std::to_string(code) + ").");
         return -1;
     }

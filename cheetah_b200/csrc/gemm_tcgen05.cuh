@@ -24,6 +24,12 @@
 //               (`qwen2.rs:442-463`);
 //   kPgSwiglu   B tile = 64 gate rows || 64 up rows; silu(g) * u
 //               (`ops.rs:743`) -> bf16.
+// Split-K (gridDim.z = S > 1, for grids far smaller than the SM count, as in
+// batched decode): CTA z accumulates k-blocks [z*KB/S, (z+1)*KB/S), writes
+// its f32 tile to a workspace and takes a ticket; the tile's last CTA sums
+// the S partial tiles in split order (deterministic), stores the sum into its
+// own TMEM accumulator and runs the epilogue above unchanged. The last CTA
+// resets the ticket, so tickets are zero between launches.
 #pragma once
 
 #include <cuda.h>
@@ -63,6 +69,10 @@ struct PrefillGemmParams {
     float *out_q_f32;         // kPgQkv: q [M][q_dim] f32 instead of bf16
     // kPgLogits: logits [M][ld_out] f32 + per-row packed argmax
     unsigned long long *argmax;
+    // Split-K (gridDim.z > 1): [splits][tiles][128][BN] f32 partial tiles
+    // and one ticket per tile (zero between launches).
+    float *split_ws;
+    unsigned *split_tickets;
 };
 
 __device__ __forceinline__ uint64_t umma_smem_desc(uint32_t addr) {
@@ -122,6 +132,83 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
+        "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
+        "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+        "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+        "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+        "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+        "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+        "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+        "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+        "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+        : "memory");
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// Split-K exchange by the four epilogue warps (thread = tile row `r`): this
+// CTA's partial tile to the workspace, then a ticket; the last of the S
+// CTAs of the tile sums the partials in split order into its TMEM
+// accumulator. Returns true in that CTA.
+template <int BN>
+__device__ __forceinline__ bool split_k_reduce(const PrefillGemmParams &p, uint32_t lane_addr, int r, int *last_s) {
+    const int S = gridDim.z;
+    const int tiles = gridDim.x * gridDim.y;
+    const int tile_id = blockIdx.y * gridDim.x + blockIdx.x;
+    const size_t split_stride = (size_t)tiles * kGemmBM * BN;
+    float *row_base = p.split_ws + ((size_t)tile_id * kGemmBM + r) * BN;
+    // Only rows below M carry results; the others are never read.
+    const bool live = blockIdx.y * kGemmBM + r < p.M;
+#pragma unroll 1
+    for (int c0 = 0; c0 < BN; c0 += 32) {
+        float v[32];
+        tmem_ld32(lane_addr + c0, v);
+        float4 *d4 = reinterpret_cast<float4 *>(row_base + blockIdx.z * split_stride + c0);
+        if (live) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) d4[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+        }
+    }
+    __threadfence();
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    if (threadIdx.x == 2 * kWarp) {
+        const unsigned old = atomicAdd(p.split_tickets + tile_id, 1u);
+        const int last = old == (unsigned)S - 1u;
+        if (last) p.split_tickets[tile_id] = 0u;
+        *last_s = last;
+    }
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    if (!*last_s) return false;
+    __threadfence();
+#pragma unroll 1
+    for (int c0 = 0; c0 < BN; c0 += 32) {
+        float v[32];
+        const float4 *s0 = reinterpret_cast<const float4 *>(row_base + c0);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float4 a = live ? __ldcg(s0 + i) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            v[4 * i] = a.x; v[4 * i + 1] = a.y; v[4 * i + 2] = a.z; v[4 * i + 3] = a.w;
+        }
+        for (int z = 1; z < S && live; ++z) {
+            const float4 *sz = reinterpret_cast<const float4 *>(row_base + z * split_stride + c0);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const float4 a = __ldcg(sz + i);
+                v[4 * i] = __fadd_rn(v[4 * i], a.x);
+                v[4 * i + 1] = __fadd_rn(v[4 * i + 1], a.y);
+                v[4 * i + 2] = __fadd_rn(v[4 * i + 2], a.z);
+                v[4 * i + 3] = __fadd_rn(v[4 * i + 3], a.w);
+            }
+        }
+        tmem_st32(lane_addr + c0, v);
+    }
+    return true;
+}
+
 // 16 consecutive values as bf16 (two 16-byte stores; dst 16-byte aligned).
 __device__ __forceinline__ void store_bf16x16(uint16_t *dst, const float (&v)[16]) {
     uint32_t w[8];
@@ -155,13 +242,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     __shared__ __align__(8) uint64_t done_bar;
     __shared__ uint32_t tmem_base_s;
     __shared__ int abort_s;
+    __shared__ int split_last_s;
 
     uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(gsmem) + 1023) & ~uintptr_t(1023));
     const int warp = threadIdx.x / kWarp;
     const int lane = threadIdx.x % kWarp;
     const int n_tile = blockIdx.x;
     const int m_tile = blockIdx.y;
-    const int k_blocks = (p.K + kGemmBK - 1) / kGemmBK;
+    const int k_total = (p.K + kGemmBK - 1) / kGemmBK;
+    // This CTA's k-blocks (all of them without split-K).
+    const int kb0 = (int)(((long long)k_total * blockIdx.z) / gridDim.z);
+    const int kb1 = (int)(((long long)k_total * (blockIdx.z + 1)) / gridDim.z);
+    const int k_blocks = kb1 - kb0;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kGemmStages; ++s) {
@@ -198,15 +290,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 uint8_t *b_dst = a_dst + kABytes;
                 const uint32_t bar = smem_u32(&full_bar[s]);
                 mbar_expect_tx(bar, kStageBytes);
-                tma_load_2d(smem_u32(a_dst), &a_map, kb * kGemmBK, m_tile * kGemmBM, bar);
+                const int kx = (kb0 + kb) * kGemmBK;
+                tma_load_2d(smem_u32(a_dst), &a_map, kx, m_tile * kGemmBM, bar);
                 if (EPI == kPgSwiglu) {
-                    tma_load_2d(smem_u32(b_dst), &b_map, kb * kGemmBK, n_tile * (BN / 2), bar);
-                    tma_load_2d(smem_u32(b_dst + kBBytes / 2), &b2_map, kb * kGemmBK, n_tile * (BN / 2), bar);
+                    tma_load_2d(smem_u32(b_dst), &b_map, kx, n_tile * (BN / 2), bar);
+                    tma_load_2d(smem_u32(b_dst + kBBytes / 2), &b2_map, kx, n_tile * (BN / 2), bar);
                 } else {
                     // Weight maps use 64-row boxes; a BN-row tile is BN/64 boxes.
 #pragma unroll
                     for (int r = 0; r < BN / 64; ++r) {
-                        tma_load_2d(smem_u32(b_dst + r * 64 * 128), &b_map, kb * kGemmBK, n_tile * BN + r * 64, bar);
+                        tma_load_2d(smem_u32(b_dst + r * 64 * 128), &b_map, kx, n_tile * BN + r * 64, bar);
                     }
                 }
             }
@@ -239,9 +332,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const bool live = row < p.M;
         const bool ok = mbar_wait(smem_u32(&done_bar), 0);
         tc_fence_after();
+        const uint32_t acc_addr = tmem + ((uint32_t)(quad * 32) << 16);
+        const bool run = ok && (gridDim.z == 1 || split_k_reduce<BN>(p, acc_addr, quad * 32 + lane, &split_last_s));
         if (!ok) {
             if (p.error) *p.error = 4;
-        } else {
+        } else if (run) {
             const uint32_t lane_addr = tmem + ((uint32_t)(quad * 32) << 16);
             if (EPI == kPgResidual) {
                 // hidden[row][n] += acc (+ bias): 32 columns per step, float4 traffic.

@@ -135,10 +135,12 @@ __global__ void __launch_bounds__(kQmThreads) gemv_qmma_kernel(const GemvParams 
     constexpr int kT = kQmWarps / KS;  // tiles per CTA pass
     constexpr int kElemsPerStep = WT == kWQ8 ? 64 : 128;
     constexpr int kDigits = 4;  // base-256 digits of x'
-    // Steps of loads in flight per lane. q8: batches of 4, the next batch
-    // issued before this one's MMAs; q4 (more MMA work per byte): a ring of
-    // 8, a slot refilled as soon as it is consumed (measured best for each).
-    constexpr bool kRing = WT == kWQ4;
+    // Steps of loads in flight per lane: a ring of 8, a slot refilled as
+    // soon as it is consumed, for q4 (more MMA work per byte) and for tiles
+    // split over 8 warps (few steps per warp: all of them in flight before
+    // the dependency wait); batches of 4, the next batch issued before this
+    // one's MMAs, for whole-row q8 tiles. Measured best for each.
+    constexpr bool kRing = WT == kWQ4 || KS == 8;
     constexpr int kU = kRing ? 8 : 4;
     extern __shared__ __align__(16) float qm_x[];
     uint2 *qm_tab = reinterpret_cast<uint2 *>(qm_x);
