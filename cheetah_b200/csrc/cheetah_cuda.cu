@@ -537,6 +537,8 @@ struct Seq {
     float *phid = nullptr;
     uint16_t *pxb = nullptr, *pqb = nullptr, *pab = nullptr, *pact = nullptr;
     float *ppart_o = nullptr, *ppart_ml = nullptr;  // prefill attention key-range splits
+    float *psplit_ws = nullptr;                     // prefill split-K GEMM partial tiles
+    unsigned *psplit_tickets = nullptr;
     CUtensorMap map_xb{}, map_ab{}, map_act{};
     cudaGraphExec_t graph = nullptr;
     cudaGraphExec_t chain_graph = nullptr;
@@ -559,6 +561,8 @@ struct Seq {
         cudaFree(pact);
         cudaFree(ppart_o);
         cudaFree(ppart_ml);
+        cudaFree(psplit_ws);
+        cudaFree(psplit_tickets);
         cudaFree(mk_opart);
         cudaFree(mk_att_part);
         cudaFree(mk_hnew);
@@ -1476,17 +1480,24 @@ int ensure_prefill_buffers(Seq &s, int rows) {
     cudaFree(s.pact);
     cudaFree(s.ppart_o);
     cudaFree(s.ppart_ml);
+    cudaFree(s.psplit_ws);
+    cudaFree(s.psplit_tickets);
+    s.psplit_ws = nullptr;
+    s.psplit_tickets = nullptr;
     s.chunk_cap = 0;
     const size_t R = (size_t)rows;
     bool ok = cudaMalloc(&s.ptokens, R * 4) == cudaSuccess && cudaMalloc(&s.phid, R * H * 4) == cudaSuccess &&
               cudaMalloc(&s.pxb, R * H * 2) == cudaSuccess && cudaMalloc(&s.pqb, R * QD * 2) == cudaSuccess &&
               cudaMalloc(&s.pab, R * QD * 2) == cudaSuccess && cudaMalloc(&s.pact, R * I * 2) == cudaSuccess &&
               cudaMalloc(&s.ppart_o, (size_t)kPrefillMaxSplits * R * QD * 4) == cudaSuccess &&
-              cudaMalloc(&s.ppart_ml, (size_t)kPrefillMaxSplits * R * c.q_heads * 2 * 4) == cudaSuccess;
+              cudaMalloc(&s.ppart_ml, (size_t)kPrefillMaxSplits * R * c.q_heads * 2 * 4) == cudaSuccess &&
+              cudaMalloc(&s.psplit_ws, (size_t)m.sms * kGemmBM * 128 * 4) == cudaSuccess &&
+              cudaMalloc(&s.psplit_tickets, (size_t)m.sms * 4) == cudaSuccess;
     if (!ok) {
         set_error("CUDA backend: prefill buffer allocation failed.");
         return -1;
     }
+    CH_CUDA_TRY(cudaMemsetAsync(s.psplit_tickets, 0, (size_t)m.sms * 4, s.stream));
     if (make_bf16_tensor_map(&s.map_xb, s.pxb, R, H, kGemmBM) != 0 ||
         make_bf16_tensor_map(&s.map_ab, s.pab, R, QD, kGemmBM) != 0 ||
         make_bf16_tensor_map(&s.map_act, s.pact, R, I, kGemmBM) != 0) {
@@ -1655,6 +1666,8 @@ int run_prefill_chunk(Seq &s, const uint32_t *tokens, int M, size_t offset, bool
         dn.out_f32 = s.phid;
         dn.ld_out = H;
         dn.error = s.d_error;
+        dn.split_ws = s.psplit_ws;
+        dn.split_tickets = s.psplit_tickets;
         if (launch_prefill_gemm<kPgResidual>(s.map_act, w.map_down, w.map_down, dn, st, pdl, m.sms) != 0) return -1;
     }
     if (last) {
@@ -1685,6 +1698,7 @@ int check_device_error(Seq &s) {
     if (code != 0) {
         cudaMemsetAsync(s.d_error, 0, 4, s.stream);
         if (s.mk_ctrl) cudaMemsetAsync(s.mk_ctrl, 0, kMkCtrlWords * 4, s.stream);
+        if (s.psplit_tickets) cudaMemsetAsync(s.psplit_tickets, 0, (size_t)s.m->sms * 4, s.stream);
         set_error("CUDA backend: device-side guard tripped (code " + std::to_string(code) +
                   "): a bounded wait timed out or a KV page id was out of range.");
         return -1;
