@@ -94,6 +94,7 @@ QWEN2_7B = Qwen2Shape(3584, 28, 28, 4, 128, 18944, 152064, tie_word_embeddings=F
 TINY = Qwen2Shape(256, 2, 14, 2, 64, 512, 1000, max_position_embeddings=4096)
 TINY_7B_HEADS = Qwen2Shape(512, 2, 28, 4, 128, 768, 1024, tie_word_embeddings=False,
                            max_position_embeddings=4096)
+TINY_WIDE_MLP = Qwen2Shape(256, 2, 14, 2, 64, 16384, 1000, max_position_embeddings=4096)
 TINY_15B_HEADS = Qwen2Shape(1536, 2, 12, 2, 128, 2048, 1024, tie_word_embeddings=False,
                             max_position_embeddings=4096)
 

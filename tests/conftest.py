@@ -49,5 +49,16 @@ def tiny15b_prepared(tmp_path_factory):
     return root
 
 
+@pytest.fixture(scope="session")
+def tinywide_prepared(tmp_path_factory):
+    """Seeded synthetic model with the 0.5B head geometry and a 16384-wide
+    MLP: long down_proj rows (many steps per warp in the quantised GEMV)."""
+    from cheetah_b200.prepared import TINY_WIDE_MLP, write_prepared
+
+    root = tmp_path_factory.mktemp("tiny_qwen2_widemlp")
+    write_prepared(root, TINY_WIDE_MLP, seed=0)
+    return root
+
+
 def reference_tree() -> Path:
     return Path(os.environ.get("CHEETAH_REFERENCE", "/root/reference"))

@@ -57,7 +57,7 @@ def test_quantised_gemv_matches_oracle(fmt, rows, cols):
     assert np.all(np.abs(y - ref) <= 2e-6 * scale + 1e-7), np.abs(y - ref).max()
 
 
-@pytest.mark.parametrize("fixture", ["tiny_prepared", "tiny7b_prepared"])
+@pytest.mark.parametrize("fixture", ["tiny_prepared", "tiny7b_prepared", "tinywide_prepared"])
 @pytest.mark.parametrize("quant", ["q8", "q4"])
 def test_quantised_decoder_matches_oracle(fixture, quant, request):
     from cheetah_b200 import runtime as R
