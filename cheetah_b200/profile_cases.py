@@ -10,9 +10,13 @@ seeded input and exits, so an `ncu -k ... -s N -c 1` capture ends by itself:
   decode-7b           Qwen2-7B architecture (synthetic weights), q8/q4/bf16:
                       a 16-token prompt, then greedy decode steps through
                       the captured decode graph; prints ms per step.
+  batch-decode        Qwen2-0.5B architecture: --batch sequences prefilled
+                      with --context tokens each, then --steps batched decode
+                      steps (cheetah_cuda_forward_batch); prints ms per step.
 
 Usage: python -m cheetah_b200.profile_cases gemv-q8 [--rows R --cols C]
        python -m cheetah_b200.profile_cases decode-7b [--quant q8] [--steps N]
+       python -m cheetah_b200.profile_cases batch-decode [--batch B --context L]
 """
 
 from __future__ import annotations
@@ -57,16 +61,49 @@ def decode_7b_case(quant: str, steps: int) -> None:
     print(f"decode-7b {quant}: {a.elapsed_time(b) / steps:.4f} ms/step")
 
 
+def batch_decode_case(batch: int, context: int, steps: int) -> None:
+    import os
+    import time
+    # Each prompt is prefilled as one chunk (about 200 launches per sequence),
+    # so the batched steps start after a predictable number of launches.
+    os.environ.setdefault("CHEETAH_PREFILL_CHUNK", str(context))
+    from cheetah_b200 import runtime as R
+    from cheetah_b200.prepared import PreparedModel, cached_synthetic, resolve_config
+    root = cached_synthetic("qwen2-0.5b")
+    cfg = resolve_config(PreparedModel(root))
+    model = R.CudaModel(root, max_positions=context + steps + 8,
+                        kv_pool_tokens=batch * (context + steps + 128))
+    rng = np.random.default_rng(3)
+    seqs, toks = [], []
+    for _ in range(batch):
+        seq = model.new_sequence()
+        prompt = rng.integers(0, cfg["vocab_size"], context).astype(np.uint32)
+        toks.append(int(np.argmax(seq.forward(prompt, 0))))
+        seqs.append(seq)
+    pos = context
+    for i in range(steps + 2):
+        if i == 2:
+            t0 = time.perf_counter()
+        toks = model.forward_batch(seqs, toks, [pos] * batch).tolist()
+        pos += 1
+    ms = (time.perf_counter() - t0) * 1e3 / steps
+    print(f"batch-decode B={batch} L={context}: {ms:.4f} ms/step (host-synchronous calls)")
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    ap.add_argument("case", choices=["gemv-q8", "gemv-q4", "decode-7b"])
+    ap.add_argument("case", choices=["gemv-q8", "gemv-q4", "decode-7b", "batch-decode"])
     ap.add_argument("--rows", type=int, default=18944)
     ap.add_argument("--cols", type=int, default=3584)
     ap.add_argument("--quant", default="q8", choices=["q8", "q4", "bf16"])
     ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--batch", type=int, default=32)
+    ap.add_argument("--context", type=int, default=4096)
     args = ap.parse_args(argv)
     if args.case.startswith("gemv"):
         gemv_case(args.case.split("-")[1], args.rows, args.cols)
+    elif args.case == "batch-decode":
+        batch_decode_case(args.batch, args.context, args.steps)
     else:
         decode_7b_case(args.quant, args.steps)
     return 0
