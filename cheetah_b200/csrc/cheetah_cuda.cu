@@ -523,6 +523,7 @@ struct Seq {
     StepState *h_step = nullptr;
     float *h_logits = nullptr;
     unsigned long long *h_argmax = nullptr;
+    int *h_error = nullptr;  // pinned copy of d_error, read with the step's results
     float *part_o = nullptr, *part_ml = nullptr;
     unsigned int *tickets = nullptr;
     int *d_error = nullptr;
@@ -584,6 +585,7 @@ struct Seq {
         cudaFreeHost(h_step);
         cudaFreeHost(h_logits);
         cudaFreeHost(h_argmax);
+        cudaFreeHost(h_error);
         m->release_pages(pages);
         model_unref(m);
     }
@@ -1364,7 +1366,7 @@ int new_seq(Model *m, Seq **out) {
               cudaMalloc(&s->token_log, (size_t)c.max_positions * 4) == cudaSuccess &&
               cudaMallocHost(&s->h_step, sizeof(StepState)) == cudaSuccess &&
               cudaMallocHost(&s->h_logits, (size_t)c.vocab_size * 4) == cudaSuccess &&
-              cudaMallocHost(&s->h_argmax, 8) == cudaSuccess;
+              cudaMallocHost(&s->h_argmax, 8) == cudaSuccess && cudaMallocHost(&s->h_error, 4) == cudaSuccess;
     if (!ok) {
         delete s;
         set_error("CUDA backend: sequence allocation failed.");
@@ -1421,16 +1423,24 @@ int forward(Seq *s, const uint32_t *tokens, size_t n, size_t offset, float *logi
             if (i + 1 < n) CH_CUDA_TRY(cudaStreamSynchronize(s->stream));  // h_step is reused
         }
     }
+    // Results and the device error word come back in one stream round trip;
+    // logits go straight into a caller buffer in pinned (page-locked or
+    // registered) host memory, through the sequence's pinned buffer otherwise.
+    bool direct = false;
     if (logits_out) {
-        CH_CUDA_TRY(cudaMemcpyAsync(s->h_logits, s->logits, (size_t)c.vocab_size * 4,
+        cudaPointerAttributes attr{};
+        direct = cudaPointerGetAttributes(&attr, logits_out) == cudaSuccess && attr.type == cudaMemoryTypeHost;
+        if (!direct) cudaGetLastError();
+        CH_CUDA_TRY(cudaMemcpyAsync(direct ? logits_out : s->h_logits, s->logits, (size_t)c.vocab_size * 4,
                                     cudaMemcpyDeviceToHost, s->stream));
     }
     if (argmax_out) {
         CH_CUDA_TRY(cudaMemcpyAsync(s->h_argmax, s->argmax, 8, cudaMemcpyDeviceToHost, s->stream));
     }
+    CH_CUDA_TRY(cudaMemcpyAsync(s->h_error, s->d_error, 4, cudaMemcpyDeviceToHost, s->stream));
     CH_CUDA_TRY(cudaStreamSynchronize(s->stream));
-    if (check_device_error(*s) != 0) return -1;
-    if (logits_out) memcpy(logits_out, s->h_logits, (size_t)c.vocab_size * 4);
+    if (*s->h_error != 0 && check_device_error(*s) != 0) return -1;
+    if (logits_out && !direct) memcpy(logits_out, s->h_logits, (size_t)c.vocab_size * 4);
     if (argmax_out) *argmax_out = (uint32_t)(*s->h_argmax & 0xFFFFFFFFull);
     return 0;
 }

@@ -160,3 +160,23 @@ def test_persistent_decode_appends_kv_at_page_boundaries(tiny_prepared, monkeypa
             # the page-opening position's row is written, and matches
             assert np.abs(ka[prompt_len]).max() > 0 and np.abs(va[prompt_len]).max() > 0, layer
             assert np.abs(ka - kb).max() < 1e-2 and np.abs(va - vb).max() < 1e-2, layer
+
+
+def test_logits_into_pinned_and_pageable_host_buffers_agree(tiny_prepared, monkeypatch):
+    """forward_ex writes logits straight into a page-locked caller buffer and
+    through its own staging buffer otherwise; both give the same values."""
+    model = _model(tiny_prepared, monkeypatch, True)
+    cfg = model.cfg
+    prompt = _tokens(33, cfg["vocab_size"], 21)
+    a, b = model.new_sequence(), model.new_sequence()
+    a.forward(prompt, 0)
+    b.forward(prompt, 0)
+    pinned = torch.empty(cfg["vocab_size"], dtype=torch.float32, pin_memory=True).numpy()
+    pageable = np.empty(cfg["vocab_size"], dtype=np.float32)
+    tok = 5
+    for i in range(4):
+        ta = a.forward_greedy([tok], 33 + i, logits_out=pinned)
+        tb = b.forward_greedy([tok], 33 + i, logits_out=pageable)
+        np.testing.assert_array_equal(pinned, pageable)
+        assert ta == tb == int(np.nonzero(pageable == pageable.max())[0][-1])
+        tok = ta
