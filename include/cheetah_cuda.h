@@ -105,7 +105,10 @@ CHEETAH_CUDA_API int cheetah_cuda_seq_positions(const CheetahCudaSeq *seq, size_
  * `tokens[0..n)` at absolute positions `offset..offset+n` and write the final
  * position's `vocab_size` f32 logits to `logits_out` (host memory). `offset`
  * must equal the sequence's cached position count. Errors: empty input, a
- * token id >= vocab (`ops.rs:1065-1078`), capacity exceeded. */
+ * token id >= vocab (`ops.rs:1065-1078`), capacity exceeded. A `logits_out`
+ * in page-locked host memory (cudaMallocHost / cudaHostRegister) is written
+ * by the device directly; any other host buffer receives a copy from the
+ * sequence's own page-locked buffer (one extra host memcpy per call). */
 CHEETAH_CUDA_API int cheetah_cuda_forward(CheetahCudaSeq *seq, const uint32_t *tokens, size_t n, size_t offset,
                          float *logits_out);
 /* As above; `logits_out` may be NULL (no logits copy) and `argmax_out`
