@@ -343,14 +343,16 @@ def decode_7b(args):
 
 def serve_bench(args):
     """Config 5: 64 concurrent sequences, prompts ~U[128, 8192], outputs
-    ~U[32, 512] (seed 2); half share a 1024-token prefix (prefilled once,
-    restored from a device snapshot like the engine's prefix cache). The 64
-    sequences are sharded across the ranks (strong scaling); each rank
+    ~U[32, 512] (seed 2); half share a 1024-token prefix (prefilled once per
+    rank, restored from a device snapshot like the engine's prefix cache). The
+    64 sequences are sharded across the ranks by the KV-token planner
+    (cheetah_b200.dispatch.plan_shards; strong scaling); each rank
     prefills its share, then decodes it with batched steps
     (cheetah_cuda_forward_batch) until every sequence has its output length.
     value = generated tokens of all ranks / max-over-ranks decode time."""
     import torch
     from cheetah_b200 import runtime as R
+    from cheetah_b200.dispatch import SeqRequest, plan_shards
     from cheetah_b200.prepared import PreparedModel, cached_synthetic, resolve_config
 
     world, rank, local = dist_env()
@@ -368,7 +370,9 @@ def serve_bench(args):
     out_len = rng.integers(32, 513, n_seq)
     shared = rng.permutation(n_seq)[: n_seq // 2]
     prefix = rng.integers(0, cfg["vocab_size"], 1024).astype(np.uint32)
-    mine = [i for i in range(n_seq) if i % world == rank]
+    reqs = [SeqRequest(i, int(prompt_len[i]), int(out_len[i]),
+                       0 if (i in shared and prompt_len[i] > 1024) else None) for i in range(n_seq)]
+    mine = plan_shards(reqs, world)[rank]
     pool = int(sum(prompt_len[i] + out_len[i] + 64 for i in mine)) + 4096
     model = R.CudaModel(model_dir, max_positions=8192 + 512 + 128, kv_pool_tokens=pool, device=local)
     prompts = {}
