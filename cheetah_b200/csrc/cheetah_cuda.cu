@@ -44,6 +44,10 @@ thread_local std::string g_last_error;
 void set_error(const std::string &message) { g_last_error = message; }
 const char *last_error() { return g_last_error.c_str(); }
 
+// Chained batched greedy steps run in chunks of at most this many steps
+// between host reads of the token log.
+constexpr int kChainSteps = 256;
+
 namespace {
 
 bool env_flag(const char *name, bool fallback) {
@@ -433,8 +437,12 @@ struct Model {
     float *b_split_ws = nullptr;
     unsigned *b_split_tickets = nullptr;
     int *b_error = nullptr;
+    // Chained greedy steps: [0] live rows, [1] step index within the chunk;
+    // token log [kChainSteps][cap] and its pinned host copy.
+    int32_t *b_chain = nullptr, *h_chain = nullptr;
+    int32_t *b_log = nullptr, *h_log = nullptr;
     CUtensorMap map_bxb{}, map_bab{}, map_bact{};
-    std::map<uint64_t, cudaGraphExec_t> batch_graphs;  // (rows, table stride, logits) -> captured step
+    std::map<uint64_t, cudaGraphExec_t> batch_graphs;  // (rows, table stride, logits, chained) -> captured step
     CUtensorMap k_map{};
     CUtensorMap v_map{};
     std::mutex pool_mutex;
@@ -460,6 +468,11 @@ struct Model {
         cudaFree(b_split_ws);
         cudaFree(b_split_tickets);
         cudaFree(b_error);
+        cudaFree(b_chain);
+        cudaFreeHost(h_chain);
+        cudaFree(b_log);
+        cudaFreeHost(h_log);
+        b_chain = h_chain = b_log = h_log = nullptr;
         b_meta = h_meta = nullptr;
         b_hid = b_q = b_logits = nullptr;
         b_xb = b_ab = b_act = nullptr;
@@ -1741,7 +1754,10 @@ int ensure_batch_workspace(Model &m, int cap, int table_cap) {
               cudaMalloc(&m.b_part_ml, parts * kMaxGroup * 2 * 4) == cudaSuccess &&
               cudaMalloc(&m.b_tickets, R * c.kv_heads * 4) == cudaSuccess && cudaMalloc(&m.b_error, 4) == cudaSuccess &&
               cudaMalloc(&m.b_split_ws, (size_t)m.sms * kGemmBM * 128 * 4) == cudaSuccess &&
-              cudaMalloc(&m.b_split_tickets, (size_t)m.sms * 4) == cudaSuccess;
+              cudaMalloc(&m.b_split_tickets, (size_t)m.sms * 4) == cudaSuccess &&
+              cudaMalloc(&m.b_chain, 2 * 4) == cudaSuccess && cudaMallocHost(&m.h_chain, 2 * 4) == cudaSuccess &&
+              cudaMalloc(&m.b_log, (size_t)kChainSteps * R * 4) == cudaSuccess &&
+              cudaMallocHost(&m.h_log, (size_t)kChainSteps * R * 4) == cudaSuccess;
     if (!ok) {
         m.free_batch();
         set_error("CUDA backend: batch workspace allocation failed.");
@@ -1761,15 +1777,41 @@ int ensure_batch_workspace(Model &m, int cap, int table_cap) {
     return 0;
 }
 
+// After a chained batched step: every row's next token is its greedy id (the
+// padding rows copy row 0), its position and length advance by one, and the
+// live rows' ids are logged at the chunk's step index.
+__global__ void batch_advance_kernel(const unsigned long long *__restrict__ argmax, int32_t *__restrict__ meta,
+                                     int cap, int rows, int32_t *__restrict__ chain, int32_t *__restrict__ log,
+                                     int max_steps) {
+    const int r = threadIdx.x;
+    const int live = chain[0];
+    const int step = chain[1];
+    if (r < rows) {
+        const int32_t tok = (int32_t)(argmax[r < live ? r : 0] & 0xFFFFFFFFull);
+        meta[r] = tok;
+        meta[cap + r] += 1;
+        meta[2 * cap + r] += 1;
+        if (r < live && step < max_steps) log[(long long)step * cap + r] = tok;
+    }
+    __syncthreads();
+    if (r == 0) chain[1] = step + 1;
+}
+
 // Enqueue one padded batched decode step (M rows) on the model's batch
-// stream: metadata upload, embeddings, every layer, final norm, lm_head + argmax.
-int enqueue_batch_step(Model &m, int M, int table_stride, bool want_logits) {
+// stream: metadata upload, embeddings, every layer, final norm, lm_head +
+// argmax. A chained step skips the upload (the metadata is already on the
+// device) and ends with batch_advance_kernel, so the next step consumes this
+// step's greedy ids.
+int enqueue_batch_step(Model &m, int M, int table_stride, bool want_logits, bool chained = false) {
     cudaStream_t st = m.batch_stream;
     const bool pdl = m.pdl;
     const int cap = m.batch_cap;
     const CheetahCudaConfig &c = m.cfg;
     const int H = c.hidden_size, I = c.intermediate_size, QD = c.q_heads * c.head_dim, KD = c.kv_heads * c.head_dim;
-    CH_CUDA_TRY(cudaMemcpyAsync(m.b_meta, m.h_meta, (size_t)(3 * cap + M * table_stride) * 4, cudaMemcpyHostToDevice, st));
+    if (!chained) {
+        CH_CUDA_TRY(cudaMemcpyAsync(m.b_meta, m.h_meta, (size_t)(3 * cap + M * table_stride) * 4,
+                                    cudaMemcpyHostToDevice, st));
+    }
     const int32_t *d_tok = m.b_meta, *d_pos = m.b_meta + cap, *d_len = m.b_meta + 2 * cap;
     const int32_t *d_tab = m.b_meta + 3 * cap;
     CH_CUDA_TRY(cudaMemsetAsync(m.b_argmax, 0, (size_t)M * 8, st));
@@ -1872,6 +1914,97 @@ int enqueue_batch_step(Model &m, int M, int table_stride, bool want_logits) {
     lm.argmax = m.b_argmax;
     lm.error = m.b_error;
     if (launch_prefill_gemm_bn<kPgLogits, 128>(m.map_bxb, m.map_lm_head, m.map_lm_head, lm, st, pdl) != 0) return -1;
+    if (chained) {
+        batch_advance_kernel<<<1, 128, 0, st>>>(m.b_argmax, m.b_meta, cap, M, m.b_chain, m.b_log, kChainSteps);
+        CH_CUDA_TRY(cudaGetLastError());
+    }
+    return 0;
+}
+
+// Validate a batch, give every sequence pages up to offsets[b] + steps, size
+// the workspace and stage the padded metadata in h_meta. Rows are padded to a
+// multiple of 8 with copies of row 0 (they recompute and rewrite row 0's K/V
+// bit for bit), so a handful of captured graphs serve every batch size.
+int prepare_batch(Model &m, Seq *const *seqs, const uint32_t *tokens, const size_t *offsets, size_t B, size_t steps,
+                  const char *api, int *M_out, int *table_stride_out) {
+    const CheetahCudaConfig &c = m.cfg;
+    CH_REQUIRE(B > 0 && B <= 128, std::string(api) + ": batch must be 1..128");
+    CH_REQUIRE(m.gemm_prefill, std::string(api) + ": needs bf16 weights and a bf16 KV cache");
+    CH_CUDA_TRY(cudaSetDevice(m.device));
+    size_t max_pages_used = 1;
+    for (size_t b = 0; b < B; ++b) {
+        Seq *s = seqs[b];
+        CH_REQUIRE(s != nullptr && s->m == &m, std::string(api) + ": sequence of another model");
+        for (size_t b2 = 0; b2 < b; ++b2) CH_REQUIRE(seqs[b2] != s, std::string(api) + ": sequence repeated");
+        CH_REQUIRE(tokens[b] < c.vocab_size, "Native backend: token id " + std::to_string(tokens[b]) +
+                                                 " exceeds the vocabulary size " + std::to_string(c.vocab_size) + ".");
+        CH_REQUIRE(offsets[b] == s->positions, "CUDA backend: offset " + std::to_string(offsets[b]) +
+                                                   " does not match the " + std::to_string(s->positions) +
+                                                   " cached positions.");
+        CH_REQUIRE(offsets[b] + steps <= c.max_positions,
+                   "CUDA backend: position " + std::to_string(offsets[b] + steps - 1) +
+                       " exceeds the sequence capacity " + std::to_string(c.max_positions) + ".");
+        CH_CUDA_TRY(cudaStreamSynchronize(s->stream));
+        if (ensure_pages_upto(*s, offsets[b] + steps) != 0) return -1;
+        max_pages_used = std::max(max_pages_used, s->pages.size());
+    }
+    const int table_stride = (int)((max_pages_used + 15) / 16 * 16);
+    const int M = (int)((B + 7) / 8 * 8);
+    if (ensure_batch_workspace(m, std::max(M, 8), table_stride) != 0) return -1;
+    // Metadata: tokens | positions | lengths | page tables (stride table_stride).
+    const int cap = m.batch_cap;
+    int32_t *h_tok = m.h_meta, *h_pos = m.h_meta + cap, *h_len = m.h_meta + 2 * cap, *h_tab = m.h_meta + 3 * cap;
+    for (int r = 0; r < M; ++r) {
+        const size_t b = r < (int)B ? (size_t)r : 0;
+        h_tok[r] = (int32_t)tokens[b];
+        h_pos[r] = (int32_t)offsets[b];
+        h_len[r] = (int32_t)offsets[b] + 1;
+        const Seq *s = seqs[b];
+        for (int i = 0; i < table_stride; ++i) h_tab[r * table_stride + i] = i < (int)s->pages.size() ? s->pages[i] : -1;
+    }
+    *M_out = M;
+    *table_stride_out = table_stride;
+    return 0;
+}
+
+// The captured graph of one batched step for (rows, table stride, logits,
+// chained), or nullptr when graphs are switched off.
+int batch_graph(Model &m, int M, int table_stride, bool want_logits, bool chained, cudaGraphExec_t *out) {
+    *out = nullptr;
+    const uint64_t key = ((uint64_t)M << 40) | ((uint64_t)table_stride << 8) | (chained ? 2u : 0u) |
+                         (want_logits ? 1u : 0u);
+    auto it = m.batch_graphs.find(key);
+    if (it == m.batch_graphs.end() && env_flag("CHEETAH_CUDA_GRAPH", true)) {
+        cudaGraph_t graph = nullptr;
+        CH_CUDA_TRY(cudaStreamBeginCapture(m.batch_stream, cudaStreamCaptureModeThreadLocal));
+        const int rc = enqueue_batch_step(m, M, table_stride, want_logits, chained);
+        const cudaError_t end_err = cudaStreamEndCapture(m.batch_stream, &graph);
+        if (rc != 0 || end_err != cudaSuccess) {
+            if (graph) cudaGraphDestroy(graph);
+            if (rc == 0) set_error(std::string("batch graph capture failed: ") + cudaGetErrorString(end_err));
+            return -1;
+        }
+        cudaGraphExec_t exec = nullptr;
+        const cudaError_t inst = cudaGraphInstantiate(&exec, graph, 0);
+        cudaGraphDestroy(graph);
+        CH_REQUIRE(inst == cudaSuccess, std::string("batch graph instantiate failed: ") + cudaGetErrorString(inst));
+        it = m.batch_graphs.emplace(key, exec).first;
+    }
+    if (it != m.batch_graphs.end()) *out = it->second;
+    return 0;
+}
+
+// Report and clear the batch error word after a synchronising call.
+int check_batch_error(Model &m) {
+    int code = 0;
+    CH_CUDA_TRY(cudaMemcpy(&code, m.b_error, 4, cudaMemcpyDeviceToHost));
+    if (code != 0) {
+        cudaMemsetAsync(m.b_error, 0, 4, m.batch_stream);
+        // A split whose wait gave up never took its ticket: start them over.
+        cudaMemsetAsync(m.b_split_tickets, 0, (size_t)m.sms * 4, m.batch_stream);
+        set_error("CUDA backend: device-side guard tripped in a batched step (code " + std::to_string(code) + ").");
+        return -1;
+    }
     return 0;
 }
 
@@ -1886,64 +2019,15 @@ int forward_batch(Model *mp, Seq *const *seqs, const uint32_t *tokens, const siz
                "cheetah_cuda_forward_batch: null argument");
     Model &m = *mp;
     const CheetahCudaConfig &c = m.cfg;
-    CH_REQUIRE(B > 0 && B <= 128, "cheetah_cuda_forward_batch: batch must be 1..128");
-    CH_REQUIRE(m.gemm_prefill, "cheetah_cuda_forward_batch: needs bf16 weights and a bf16 KV cache");
     std::lock_guard<std::mutex> lock(m.batch_mutex);
-    CH_CUDA_TRY(cudaSetDevice(m.device));
-    // Validate, allocate pages, and sync each sequence's own stream.
-    size_t max_pages_used = 1;
-    for (size_t b = 0; b < B; ++b) {
-        Seq *s = seqs[b];
-        CH_REQUIRE(s != nullptr && s->m == mp, "cheetah_cuda_forward_batch: sequence of another model");
-        for (size_t b2 = 0; b2 < b; ++b2) CH_REQUIRE(seqs[b2] != s, "cheetah_cuda_forward_batch: sequence repeated");
-        CH_REQUIRE(tokens[b] < c.vocab_size, "Native backend: token id " + std::to_string(tokens[b]) +
-                                                 " exceeds the vocabulary size " + std::to_string(c.vocab_size) + ".");
-        CH_REQUIRE(offsets[b] == s->positions, "CUDA backend: offset " + std::to_string(offsets[b]) +
-                                                   " does not match the " + std::to_string(s->positions) +
-                                                   " cached positions.");
-        CH_CUDA_TRY(cudaStreamSynchronize(s->stream));
-        if (ensure_pages_upto(*s, offsets[b] + 1) != 0) return -1;
-        max_pages_used = std::max(max_pages_used, s->pages.size());
-    }
-    const int table_stride = (int)((max_pages_used + 15) / 16 * 16);
-    // Rows are padded to a multiple of 8 with copies of row 0 (they recompute
-    // and rewrite row 0's K/V bit for bit), so a handful of captured graphs
-    // serve every batch size.
-    const int M = (int)((B + 7) / 8 * 8);
-    if (ensure_batch_workspace(m, std::max(M, 8), table_stride) != 0) return -1;
-    // Metadata: tokens | positions | lengths | page tables (stride table_stride).
-    const int cap = m.batch_cap;
-    int32_t *h_tok = m.h_meta, *h_pos = m.h_meta + cap, *h_len = m.h_meta + 2 * cap, *h_tab = m.h_meta + 3 * cap;
-    for (int r = 0; r < M; ++r) {
-        const size_t b = r < (int)B ? (size_t)r : 0;
-        h_tok[r] = (int32_t)tokens[b];
-        h_pos[r] = (int32_t)offsets[b];
-        h_len[r] = (int32_t)offsets[b] + 1;
-        const Seq *s = seqs[b];
-        for (int i = 0; i < table_stride; ++i) h_tab[r * table_stride + i] = i < (int)s->pages.size() ? s->pages[i] : -1;
-    }
+    int M = 0, table_stride = 0;
+    if (prepare_batch(m, seqs, tokens, offsets, B, 1, "cheetah_cuda_forward_batch", &M, &table_stride) != 0) return -1;
     const bool want_logits = logits_out != nullptr;
-    const uint64_t key = ((uint64_t)M << 40) | ((uint64_t)table_stride << 8) | (want_logits ? 1u : 0u);
-    auto it = m.batch_graphs.find(key);
-    if (it == m.batch_graphs.end() && env_flag("CHEETAH_CUDA_GRAPH", true)) {
-        cudaGraph_t graph = nullptr;
-        CH_CUDA_TRY(cudaStreamBeginCapture(m.batch_stream, cudaStreamCaptureModeThreadLocal));
-        const int rc = enqueue_batch_step(m, M, table_stride, want_logits);
-        const cudaError_t end_err = cudaStreamEndCapture(m.batch_stream, &graph);
-        if (rc != 0 || end_err != cudaSuccess) {
-            if (graph) cudaGraphDestroy(graph);
-            if (rc == 0) set_error(std::string("batch graph capture failed: ") + cudaGetErrorString(end_err));
-            return -1;
-        }
-        cudaGraphExec_t exec = nullptr;
-        const cudaError_t inst = cudaGraphInstantiate(&exec, graph, 0);
-        cudaGraphDestroy(graph);
-        CH_REQUIRE(inst == cudaSuccess, std::string("batch graph instantiate failed: ") + cudaGetErrorString(inst));
-        it = m.batch_graphs.emplace(key, exec).first;
-    }
+    cudaGraphExec_t exec = nullptr;
+    if (batch_graph(m, M, table_stride, want_logits, false, &exec) != 0) return -1;
     cudaStream_t st = m.batch_stream;
-    if (it != m.batch_graphs.end()) {
-        CH_CUDA_TRY(cudaGraphLaunch(it->second, st));
+    if (exec != nullptr) {
+        CH_CUDA_TRY(cudaGraphLaunch(exec, st));
     } else if (enqueue_batch_step(m, M, table_stride, want_logits) != 0) {
         return -1;
     }
@@ -1952,19 +2036,55 @@ int forward_batch(Model *mp, Seq *const *seqs, const uint32_t *tokens, const siz
     }
     CH_CUDA_TRY(cudaMemcpyAsync(m.h_argmax, m.b_argmax, (size_t)B * 8, cudaMemcpyDeviceToHost, st));
     CH_CUDA_TRY(cudaStreamSynchronize(st));
-    int code = 0;
-    CH_CUDA_TRY(cudaMemcpy(&code, m.b_error, 4, cudaMemcpyDeviceToHost));
-    if (code != 0) {
-        cudaMemsetAsync(m.b_error, 0, 4, m.batch_stream);
-        // A split whose wait gave up never took its ticket: start them over.
-        cudaMemsetAsync(m.b_split_tickets, 0, (size_t)m.sms * 4, m.batch_stream);
-        set_error("CUDA backend: device-side guard tripped in a batched step (code " + std::to_string(code) + ").");
-        return -1;
-    }
+    if (check_batch_error(m) != 0) return -1;
     for (size_t b = 0; b < B; ++b) {
         seqs[b]->positions = offsets[b] + 1;
         if (argmax_out) argmax_out[b] = (uint32_t)(m.h_argmax[b] & 0xFFFFFFFFull);
     }
+    return 0;
+}
+
+// `steps` greedy tokens for each of B sequences with no host round trip
+// between steps: the metadata is uploaded once, and each replayed step ends
+// by feeding its greedy ids to the next (batch_advance_kernel). The host
+// reads the token log every kChainSteps steps. tokens_out[b * steps + i] is
+// sequence b's greedy token after consuming position offsets[b] + i.
+int forward_batch_greedy(Model *mp, Seq *const *seqs, const uint32_t *tokens, const size_t *offsets, size_t B,
+                         size_t steps, uint32_t *tokens_out) {
+    CH_REQUIRE(mp != nullptr && seqs != nullptr && tokens != nullptr && offsets != nullptr && tokens_out != nullptr,
+               "cheetah_cuda_forward_batch_greedy: null argument");
+    CH_REQUIRE(steps > 0, "cheetah_cuda_forward_batch_greedy: steps must be positive");
+    Model &m = *mp;
+    std::lock_guard<std::mutex> lock(m.batch_mutex);
+    int M = 0, table_stride = 0;
+    if (prepare_batch(m, seqs, tokens, offsets, B, steps, "cheetah_cuda_forward_batch_greedy", &M, &table_stride) != 0)
+        return -1;
+    cudaGraphExec_t exec = nullptr;
+    if (batch_graph(m, M, table_stride, false, true, &exec) != 0) return -1;
+    cudaStream_t st = m.batch_stream;
+    const int cap = m.batch_cap;
+    CH_CUDA_TRY(cudaMemcpyAsync(m.b_meta, m.h_meta, (size_t)(3 * cap + M * table_stride) * 4, cudaMemcpyHostToDevice,
+                                st));
+    for (size_t done = 0; done < steps;) {
+        const size_t n = std::min(steps - done, (size_t)kChainSteps);
+        m.h_chain[0] = (int32_t)B;
+        m.h_chain[1] = 0;
+        CH_CUDA_TRY(cudaMemcpyAsync(m.b_chain, m.h_chain, 2 * 4, cudaMemcpyHostToDevice, st));
+        for (size_t i = 0; i < n; ++i) {
+            if (exec != nullptr) {
+                CH_CUDA_TRY(cudaGraphLaunch(exec, st));
+            } else if (enqueue_batch_step(m, M, table_stride, false, true) != 0) {
+                return -1;
+            }
+        }
+        CH_CUDA_TRY(cudaMemcpyAsync(m.h_log, m.b_log, n * (size_t)cap * 4, cudaMemcpyDeviceToHost, st));
+        CH_CUDA_TRY(cudaStreamSynchronize(st));
+        for (size_t i = 0; i < n; ++i)
+            for (size_t b = 0; b < B; ++b) tokens_out[b * steps + done + i] = (uint32_t)m.h_log[i * cap + b];
+        done += n;
+    }
+    if (check_batch_error(m) != 0) return -1;
+    for (size_t b = 0; b < B; ++b) seqs[b]->positions = offsets[b] + steps;
     return 0;
 }
 
@@ -2154,6 +2274,12 @@ int cheetah_cuda_forward_batch(CheetahCudaModel *model, CheetahCudaSeq *const *s
                                const size_t *offsets, size_t batch, float *logits_out, uint32_t *argmax_out) {
     return cheetah::forward_batch(reinterpret_cast<Model *>(model), reinterpret_cast<Seq *const *>(seqs), tokens,
                                   offsets, batch, logits_out, argmax_out);
+}
+
+int cheetah_cuda_forward_batch_greedy(CheetahCudaModel *model, CheetahCudaSeq *const *seqs, const uint32_t *tokens,
+                                      const size_t *offsets, size_t batch, size_t steps, uint32_t *tokens_out) {
+    return cheetah::forward_batch_greedy(reinterpret_cast<Model *>(model), reinterpret_cast<Seq *const *>(seqs),
+                                         tokens, offsets, batch, steps, tokens_out);
 }
 
 int cheetah_cuda_generate_greedy(CheetahCudaSeq *seq, uint32_t first_token, size_t offset, size_t steps,

@@ -81,6 +81,7 @@ SIGNATURES = {
     "cheetah_cuda_forward": (_I, [_P, _P, _S, _S, _P]),
     "cheetah_cuda_forward_ex": (_I, [_P, _P, _S, _S, _P, _P]),
     "cheetah_cuda_forward_batch": (_I, [_P, _P, _P, _P, _S, _P, _P]),
+    "cheetah_cuda_forward_batch_greedy": (_I, [_P, _P, _P, _P, _S, _S, _P]),
     "cheetah_cuda_generate_greedy": (_I, [_P, C.c_uint32, _S, _S, _P]),
     "cheetah_cuda_seq_stream": (_I, [_P, C.POINTER(_P)]),
     "cheetah_cuda_seq_snapshot": (_I, [_P, C.POINTER(_P)]),
@@ -191,6 +192,18 @@ class CudaModel:
         _check(lib().cheetah_cuda_forward_batch(self._h, handles, _ptr(t), _ptr(o), B,
                                                 _ptr(logits) if want_logits else None, _ptr(am)))
         return (am, logits) if want_logits else am
+
+    def forward_batch_greedy(self, seqs, tokens, offsets, steps: int) -> np.ndarray:
+        """`steps` greedy tokens for each sequence with no host round trip
+        between steps (`cheetah_cuda_forward_batch_greedy`): uint32 [B, steps],
+        row b holding the ids generated after tokens[b]."""
+        B = len(seqs)
+        handles = (C.c_void_p * B)(*[s._h.value for s in seqs])
+        t = np.ascontiguousarray(np.asarray(tokens, dtype=np.uint32))
+        o = np.ascontiguousarray(np.asarray(offsets, dtype=np.uint64))
+        out = np.zeros((B, steps), dtype=np.uint32)
+        _check(lib().cheetah_cuda_forward_batch_greedy(self._h, handles, _ptr(t), _ptr(o), B, steps, _ptr(out)))
+        return out
 
 
 class CudaSnapshot:

@@ -129,6 +129,18 @@ CHEETAH_CUDA_API int cheetah_cuda_forward_batch(CheetahCudaModel *model, Cheetah
                                                 const uint32_t *tokens, const size_t *offsets, size_t batch,
                                                 float *logits_out, uint32_t *argmax_out);
 
+/* `steps` greedy tokens for each of `batch` sequences, kept on the device:
+ * step i of sequence b consumes its greedy token of step i-1 (step 0 consumes
+ * tokens[b]) at position offsets[b] + i, so there is no host round trip
+ * between steps; tokens_out[b * steps + i] receives that step's greedy token.
+ * The same results as `steps` calls of cheetah_cuda_forward_batch, each fed
+ * the previous call's ids: the serving loop's greedy batch
+ * (`engine.rs:1874`, `engine.rs:1920-1958`) between changes of the batch.
+ * Needs bf16 weights and a bf16 KV cache. */
+CHEETAH_CUDA_API int cheetah_cuda_forward_batch_greedy(CheetahCudaModel *model, CheetahCudaSeq *const *seqs,
+                                                       const uint32_t *tokens, const size_t *offsets,
+                                                       size_t batch, size_t steps, uint32_t *tokens_out);
+
 /* Greedy decode kept on the device: step i consumes the greedy token of step
  * i-1 (step 0 consumes `first_token`) at position `offset + i`; tokens_out[i]
  * receives step i's greedy token. No host round trip between steps — the

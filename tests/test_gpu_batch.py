@@ -70,3 +70,61 @@ def test_batched_decode_argmax_only_and_errors(tiny_prepared):
     c = other.new_sequence()
     with pytest.raises(R.CheetahCudaError, match="another model"):
         model.forward_batch([a, c], [5, 6], [4, 0])
+
+
+@pytest.mark.parametrize("lengths,steps", [([5, 70, 1, 130, 64], 300), ([17], 40),
+                                           ([3, 9, 33, 2, 15, 16, 47, 8, 100], 20)])
+def test_chained_greedy_batch_matches_step_by_step(tiny_prepared, lengths, steps):
+    """`cheetah_cuda_forward_batch_greedy` against `steps` calls of
+    forward_batch fed their own ids (identical tokens: same kernels, same
+    inputs), crossing page boundaries and, at 300 steps, the host's token-log
+    chunk; the KV written by the chained steps is then checked against the
+    oracle run over prompt + generated ids."""
+    from cheetah_b200 import runtime as R
+    pm = PreparedModel(tiny_prepared)
+    cfg = resolve_config(pm)
+    model = R.CudaModel(tiny_prepared, max_positions=1024)
+    rng = np.random.default_rng(5)
+    prompts = [rng.integers(0, cfg["vocab_size"], n).astype(np.uint32) for n in lengths]
+    chained, stepped, first = [], [], []
+    for prompt in prompts:
+        a, b = model.new_sequence(), model.new_sequence()
+        la, lb = a.forward(prompt, 0), b.forward(prompt, 0)
+        assert np.array_equal(la, lb)
+        chained.append(a)
+        stepped.append(b)
+        first.append(int(np.argmax(la)))
+    out = model.forward_batch_greedy(chained, first, lengths, steps)
+    assert out.shape == (len(lengths), steps)
+    toks, offs, want = list(first), list(lengths), []
+    for _ in range(steps):
+        am = model.forward_batch(stepped, toks, offs)
+        want.append(am.copy())
+        toks = [int(t) for t in am]
+        offs = [o + 1 for o in offs]
+    assert np.array_equal(out, np.stack(want, axis=1))
+    assert [s.positions() for s in chained] == [n + steps for n in lengths]
+    # The chained steps' K/V: the next token's logits against the oracle.
+    for b in {0, len(lengths) - 1}:
+        ids = np.concatenate([prompts[b], [first[b]], out[b, :-1]]).astype(np.uint32)
+        ref = O.OracleModel(pm, cfg)
+        ref.forward(ids, 0)
+        w = ref.forward([int(out[b, -1])], len(ids))
+        g = chained[b].forward([int(out[b, -1])], len(ids))
+        assert np.abs(g - w).max() < 2e-3
+
+
+def test_chained_greedy_batch_errors(tiny_prepared):
+    from cheetah_b200 import runtime as R
+    model = R.CudaModel(tiny_prepared, max_positions=64)
+    a = model.new_sequence()
+    a.forward([1, 2, 3], 0)
+    with pytest.raises(R.CheetahCudaError, match="capacity"):
+        model.forward_batch_greedy([a], [4], [3], 62)
+    with pytest.raises(R.CheetahCudaError, match="positive"):
+        model.forward_batch_greedy([a], [4], [3], 0)
+    with pytest.raises(R.CheetahCudaError, match="does not match"):
+        model.forward_batch_greedy([a], [4], [2], 4)
+    assert a.positions() == 3
+    out = model.forward_batch_greedy([a], [4], [3], 61)
+    assert out.shape == (1, 61) and a.positions() == 64
