@@ -34,6 +34,7 @@
 #include "gemv_qmma.cuh"
 #include "gemm_tcgen05.cuh"
 #include "prefill_attention.cuh"
+#include "prefill_attention_tc.cuh"
 #include "store.h"
 
 namespace cheetah {
@@ -554,6 +555,7 @@ struct Seq {
     float *psplit_ws = nullptr;                     // prefill split-K GEMM partial tiles
     unsigned *psplit_tickets = nullptr;
     CUtensorMap map_xb{}, map_ab{}, map_act{};
+    CUtensorMap map_qb{};  // q rows in 128-row boxes (tensor-core prefill attention)
     cudaGraphExec_t graph = nullptr;
     cudaGraphExec_t chain_graph = nullptr;
     // Persistent decode kernel scratch (allocated on first use).
@@ -1523,7 +1525,8 @@ int ensure_prefill_buffers(Seq &s, int rows) {
     CH_CUDA_TRY(cudaMemsetAsync(s.psplit_tickets, 0, (size_t)m.sms * 4, s.stream));
     if (make_bf16_tensor_map(&s.map_xb, s.pxb, R, H, kGemmBM) != 0 ||
         make_bf16_tensor_map(&s.map_ab, s.pab, R, QD, kGemmBM) != 0 ||
-        make_bf16_tensor_map(&s.map_act, s.pact, R, I, kGemmBM) != 0) {
+        make_bf16_tensor_map(&s.map_act, s.pact, R, I, kGemmBM) != 0 ||
+        make_bf16_tensor_map(&s.map_qb, s.pqb, R, QD, kTcRows) != 0) {
         return -1;
     }
     s.chunk_cap = rows;
@@ -1634,30 +1637,47 @@ int run_prefill_chunk(Seq &s, const uint32_t *tokens, int M, size_t offset, bool
         ap.window = c.sliding_window;
         ap.scale = 1.0f / sqrtf((float)c.head_dim);
         ap.error = s.d_error;
-        const size_t asmem = prefill_attention_smem();
-        // Key-range splits: about two CTAs per SM (each CTA covers >= 4 key tiles).
-        const int blocks = ((M + 15) / 16) * (int)c.kv_heads;
-        const int key_tiles = (int)((offset + M + 63) / 64);
-        ap.splits = std::max(1, std::min(std::min(kPrefillMaxSplits, (2 * m.sms + blocks - 1) / blocks),
-                                         std::max(1, key_tiles / 4)));
         ap.part_o = s.ppart_o;
         ap.part_ml = s.ppart_ml;
-        dim3 agrid((M + 15) / 16, c.kv_heads, ap.splits);
-        if (c.head_dim == 64) {
-            CH_CUDA_TRY(cudaFuncSetAttribute(prefill_attention_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)asmem));
-            CH_CUDA_TRY(launch_ex(prefill_attention_kernel<64>, agrid, dim3(kPrefillWarps * kWarp), asmem, st, pdl,
+        if (c.head_dim == 64 && env_flag("CHEETAH_PREFILL_TC", true)) {
+            // Tensor-core attention: one CTA per SM (512 TMEM columns each);
+            // key-range splits fill the SMs, each split >= 2 key tiles.
+            const int blocks = ((M + kTcRows - 1) / kTcRows) * (int)c.q_heads;
+            const int key_tiles = (int)((offset + M + kTcKeys - 1) / kTcKeys);
+            ap.splits = std::max(1, std::min(std::min(kPrefillMaxSplits, m.sms / blocks), key_tiles / 2));
+            const size_t tsmem = prefill_attention_tc_smem();
+            CH_CUDA_TRY(cudaFuncSetAttribute(prefill_attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)tsmem));
+            dim3 tgrid((M + kTcRows - 1) / kTcRows, c.q_heads, ap.splits);
+            CH_CUDA_TRY(launch_ex(prefill_attention_tc_kernel, tgrid, dim3(kTcThreads), tsmem, st, pdl, s.map_qb,
                                   m.k_map, m.v_map, ap));
             if (ap.splits > 1) {
                 CH_CUDA_TRY(launch_ex(prefill_merge_kernel<64>, dim3(2 * m.sms), dim3(256), 0, st, pdl, ap));
             }
         } else {
-            CH_CUDA_TRY(cudaFuncSetAttribute(prefill_attention_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)asmem));
-            CH_CUDA_TRY(launch_ex(prefill_attention_kernel<128>, agrid, dim3(kPrefillWarps * kWarp), asmem, st, pdl,
-                                  m.k_map, m.v_map, ap));
-            if (ap.splits > 1) {
-                CH_CUDA_TRY(launch_ex(prefill_merge_kernel<128>, dim3(2 * m.sms), dim3(256), 0, st, pdl, ap));
+            const size_t asmem = prefill_attention_smem();
+            // Key-range splits: about two CTAs per SM (each CTA covers >= 4 key tiles).
+            const int blocks = ((M + 15) / 16) * (int)c.kv_heads;
+            const int key_tiles = (int)((offset + M + 63) / 64);
+            ap.splits = std::max(1, std::min(std::min(kPrefillMaxSplits, (2 * m.sms + blocks - 1) / blocks),
+                                             std::max(1, key_tiles / 4)));
+            dim3 agrid((M + 15) / 16, c.kv_heads, ap.splits);
+            if (c.head_dim == 64) {
+                CH_CUDA_TRY(cudaFuncSetAttribute(prefill_attention_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 (int)asmem));
+                CH_CUDA_TRY(launch_ex(prefill_attention_kernel<64>, agrid, dim3(kPrefillWarps * kWarp), asmem, st, pdl,
+                                      m.k_map, m.v_map, ap));
+                if (ap.splits > 1) {
+                    CH_CUDA_TRY(launch_ex(prefill_merge_kernel<64>, dim3(2 * m.sms), dim3(256), 0, st, pdl, ap));
+                }
+            } else {
+                CH_CUDA_TRY(cudaFuncSetAttribute(prefill_attention_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 (int)asmem));
+                CH_CUDA_TRY(launch_ex(prefill_attention_kernel<128>, agrid, dim3(kPrefillWarps * kWarp), asmem, st, pdl,
+                                      m.k_map, m.v_map, ap));
+                if (ap.splits > 1) {
+                    CH_CUDA_TRY(launch_ex(prefill_merge_kernel<128>, dim3(2 * m.sms), dim3(256), 0, st, pdl, ap));
+                }
             }
         }
 

@@ -1,0 +1,373 @@
+// Causal GQA attention for a prefill chunk on the 5th-generation tensor cores
+// (head_dim 64, bf16 paged KV cache, pages of a multiple of 64 tokens): the
+// same contract and results as prefill_attention_kernel (the batched form of
+// `forward_layer_chunk`, `qwen2.rs:314-343`), with S = Q K^T and O = P V as
+// tcgen05.mma (kind::f16, f32 accumulation in TMEM).
+//
+// CTA = 128 consecutive tokens x one query head; 192 threads:
+//   warp 0      TMA producer: the Q tile once, then 128-key K and V tiles
+//               (two 64-key boxes each, 128-byte swizzle, no multicast)
+//               through a kTcStages-deep ring;
+//   warp 1      allocates 512 TMEM columns; lane 0 issues the MMAs:
+//               S_j = Q K_j^T (M=128, N=128 keys, K=64) into S buffer j%2,
+//               then, once the softmax has written P_j, O_t = P_j V_j
+//               (M=128, N=64, K=128 keys; V read MN-major) into the O_t
+//               columns. S_{j+1} is issued before PV_j, so the tensor core
+//               computes the next scores while the softmax runs;
+//   warps 2-5   softmax, one thread per query row (its TMEM lane): load the
+//               S row, causal/window mask, online max and sum in log2 units,
+//               P_j as bf16 into shared memory in the K-major swizzled
+//               layout the MMA reads, and O = O * alpha_{j-1} + O_t(j-1) in
+//               registers as each PV completes.
+// Key-range splits over blockIdx.z write unnormalised partials (O, m in log2
+// units, l) in prefill_attention_kernel's format, combined by
+// prefill_merge_kernel. All mbarrier waits are bounded (error flag, early
+// exit, TMEM freed).
+#pragma once
+
+#include "gemm_tcgen05.cuh"
+#include "prefill_attention.cuh"
+
+namespace cheetah {
+
+constexpr int kTcRows = 128;       // query rows per CTA
+constexpr int kTcKeys = 128;       // keys per tile
+constexpr int kTcStages = 3;       // K/V ring depth
+constexpr int kTcThreads = 192;
+constexpr int kTcTmemCols = 512;   // S0 | S1 | O_t (64) | unused
+constexpr int kTcOtCol = 2 * kTcKeys;
+constexpr int kTcQBytes = kTcRows * 64 * 2;        // 16 KB
+constexpr int kTcKvBytes = kTcKeys * 64 * 2;       // 16 KB per K or V tile
+constexpr int kTcPBytes = kTcRows * kTcKeys * 2;   // 32 KB
+
+inline size_t prefill_attention_tc_smem() {
+    return (size_t)kTcQBytes + (size_t)kTcStages * 2 * kTcKvBytes + kTcPBytes + 1024;
+}
+
+// MN-major operand with 128-byte swizzle (rows of 128 B along N, 8-row atoms
+// along K, SBO = 1024 B between K atoms); one 64-element atom along N.
+__device__ __forceinline__ uint64_t umma_smem_desc_mn(uint32_t addr) {
+    uint64_t desc = 0;
+    desc |= (uint64_t)((addr >> 4) & 0x3FFF);
+    desc |= (uint64_t)1 << 16;
+    desc |= (uint64_t)(1024 >> 4) << 32;
+    desc |= (uint64_t)1 << 46;
+    desc |= (uint64_t)2 << 61;
+    return desc;
+}
+
+__device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, float *v) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// 2^x with the hardware approximation (flushes subnormal results to zero);
+// the softmax weights are rounded to bf16 right after.
+__device__ __forceinline__ float fast_exp2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+__global__ void __launch_bounds__(kTcThreads, 1)
+    prefill_attention_tc_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constant__ CUtensorMap k_map,
+                                const __grid_constant__ CUtensorMap v_map, const PrefillAttnParams p) {
+    constexpr int HD = 64;
+    constexpr uint32_t kIdescS = umma_idesc_bf16(kTcRows, kTcKeys);
+    constexpr uint32_t kIdescPV = umma_idesc_bf16(kTcRows, HD) | (1u << 16);  // B (V) MN-major
+    extern __shared__ __align__(1024) uint8_t attn_tc_smem[];
+    __shared__ __align__(8) uint64_t q_full;
+    __shared__ __align__(8) uint64_t kv_full[kTcStages];
+    __shared__ __align__(8) uint64_t kv_empty[kTcStages];
+    __shared__ __align__(8) uint64_t s_full[2];
+    __shared__ __align__(8) uint64_t s_empty[2];
+    __shared__ __align__(8) uint64_t p_full;
+    __shared__ __align__(8) uint64_t o_full;
+    __shared__ uint32_t tmem_base_s;
+    __shared__ int abort_s;
+
+    uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(attn_tc_smem) + 1023) & ~uintptr_t(1023));
+    uint8_t *q_s = base;
+    uint8_t *ring = q_s + kTcQBytes;
+    uint8_t *p_s = ring + kTcStages * 2 * kTcKvBytes;
+    const int warp = threadIdx.x / kWarp;
+    const int lane = threadIdx.x % kWarp;
+    const int group = p.q_heads / p.kv_heads;
+    const int head = blockIdx.y;
+    const int kvh = head / group;
+    const int t0 = blockIdx.x * kTcRows;
+    const int t_last = min(p.T, t0 + kTcRows) - 1;
+    const int pos_first = p.offset + t0;
+    const int pos_last = p.offset + t_last;
+    int ws = 0;
+    if (p.window > 0) ws = max(0, pos_first + 1 - p.window);
+    const int all_lo = ws / kTcKeys;
+    const int all_hi = pos_last / kTcKeys + 1;
+    const int per_split = (all_hi - all_lo + p.splits - 1) / p.splits;
+    const int split = blockIdx.z;
+    const int tile_lo = all_lo + split * per_split;
+    const int tile_hi = min(all_hi, tile_lo + per_split);
+    const int n_tiles = max(0, tile_hi - tile_lo);
+
+    if (threadIdx.x == 0) {
+        mbar_init(smem_u32(&q_full), 1);
+        for (int s = 0; s < kTcStages; ++s) {
+            mbar_init(smem_u32(&kv_full[s]), 1);
+            mbar_init(smem_u32(&kv_empty[s]), 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(smem_u32(&s_full[b]), 1);
+            mbar_init(smem_u32(&s_empty[b]), kTcRows);
+        }
+        mbar_init(smem_u32(&p_full), kTcRows);
+        mbar_init(smem_u32(&o_full), 1);
+        abort_s = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_s)),
+                     "r"((uint32_t)kTcTmemCols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_base_s;
+
+    pdl_wait();
+    pdl_launch_dependents();
+
+    if (warp == 0) {
+        if (lane == 0 && n_tiles > 0) {
+            mbar_expect_tx(smem_u32(&q_full), kTcQBytes);
+            tma_load_2d(smem_u32(q_s), &q_map, head * HD, t0, smem_u32(&q_full));
+            for (int j = 0; j < n_tiles; ++j) {
+                const int s = j % kTcStages;
+                if (!mbar_wait(smem_u32(&kv_empty[s]), ((j / kTcStages) & 1) ^ 1)) {
+                    abort_s = 1;
+                    break;
+                }
+                const int tile = tile_lo + j;
+                // Rows of the pool for the tile's two 64-key boxes. A box past
+                // the chunk's last position holds only masked keys: it re-reads
+                // box 0 (always in range) so the ring holds finite values.
+                int rows[2];
+#pragma unroll
+                for (int b = 0; b < 2; ++b) {
+                    const int pos0 = tile * kTcKeys + b * 64;
+                    const int pidx = pos0 / p.page_tokens;
+                    const int page = pidx < p.max_pages ? p.page_table[pidx] : -1;
+                    if (page < 0 || page >= p.num_pages) {
+                        if (b == 0 || pos0 <= pos_last) {
+                            if (p.error) *p.error = 6;
+                        }
+                        rows[b] = b == 0 ? (int)p.layer_row_offset : rows[0];
+                    } else {
+                        rows[b] = (int)(p.layer_row_offset + ((long long)page * p.kv_heads + kvh) * p.page_tokens +
+                                        (pos0 - pidx * p.page_tokens));
+                    }
+                    if (b == 1 && pos0 > pos_last) rows[1] = rows[0];
+                }
+                uint8_t *ks = ring + s * 2 * kTcKvBytes;
+                uint8_t *vs = ks + kTcKvBytes;
+                const uint32_t bar = smem_u32(&kv_full[s]);
+                mbar_expect_tx(bar, 2 * kTcKvBytes);
+#pragma unroll
+                for (int b = 0; b < 2; ++b) {
+                    tma_load_2d(smem_u32(ks + b * 64 * 128), &k_map, 0, rows[b], bar);
+                    tma_load_2d(smem_u32(vs + b * 64 * 128), &v_map, 0, rows[b], bar);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && n_tiles > 0) {
+            const uint32_t q_addr = smem_u32(q_s);
+            const uint32_t p_addr = smem_u32(p_s);
+            bool ok = mbar_wait(smem_u32(&q_full), 0);
+            auto issue_s = [&](int j) -> bool {
+                const int s = j % kTcStages;
+                if (!mbar_wait(smem_u32(&kv_full[s]), (j / kTcStages) & 1)) return false;
+                if (!mbar_wait(smem_u32(&s_empty[j & 1]), ((j >> 1) & 1) ^ 1)) return false;
+                tc_fence_after();
+                const uint32_t k_addr = smem_u32(ring + s * 2 * kTcKvBytes);
+                const uint32_t d = tmem + (uint32_t)((j & 1) * kTcKeys);
+#pragma unroll
+                for (int k = 0; k < HD / 16; ++k) {
+                    umma_bf16(d, umma_smem_desc(q_addr + k * 32), umma_smem_desc(k_addr + k * 32), kIdescS,
+                              k > 0 ? 1u : 0u);
+                }
+                umma_commit(smem_u32(&s_full[j & 1]));
+                return true;
+            };
+            if (ok) ok = issue_s(0);
+            for (int j = 0; ok && j < n_tiles; ++j) {
+                if (j + 1 < n_tiles && !issue_s(j + 1)) {
+                    ok = false;
+                    break;
+                }
+                if (!mbar_wait(smem_u32(&p_full), j & 1)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const int s = j % kTcStages;
+                const uint32_t v_addr = smem_u32(ring + s * 2 * kTcKvBytes + kTcKvBytes);
+#pragma unroll
+                for (int k = 0; k < kTcKeys / 16; ++k) {
+                    umma_bf16(tmem + kTcOtCol, umma_smem_desc(p_addr + (k >> 2) * (kTcRows * 128) + (k & 3) * 32),
+                              umma_smem_desc_mn(v_addr + k * 2048), kIdescPV, k > 0 ? 1u : 0u);
+                }
+                umma_commit(smem_u32(&o_full));
+                umma_commit(smem_u32(&kv_empty[s]));
+            }
+            if (!ok) abort_s = 1;
+        }
+    } else {
+        // Softmax warps 2..5: TMEM lane quadrant = warp % 4; thread = query row.
+        const int quad = warp % 4;
+        const int r = quad * 32 + lane;
+        const int t = t0 + r;
+        const int qpos = p.offset + t;
+        const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+        const float scale_log2 = p.scale * 1.4426950408889634f;
+        float o[HD];
+#pragma unroll
+        for (int i = 0; i < HD; ++i) o[i] = 0.0f;
+        float m_run = -INFINITY, l_run = 0.0f, alpha_prev = 1.0f;
+        bool ok = true;
+        // O = O * alpha + O_t, 32 columns at a time.
+        auto fold = [&](float alpha) {
+#pragma unroll
+            for (int h = 0; h < HD / 32; ++h) {
+                float ot[32];
+                tmem_ld32_nowait(tmem + lane_off + kTcOtCol + h * 32, ot);
+                tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 32; ++i) o[h * 32 + i] = fmaf(o[h * 32 + i], alpha, ot[i]);
+            }
+        };
+        uint8_t *p_row0 = p_s + r * 128;
+        for (int j = 0; j < n_tiles; ++j) {
+            if (!mbar_wait(smem_u32(&s_full[j & 1]), (j >> 1) & 1)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            float sc[kTcKeys];
+            const uint32_t s_addr = tmem + lane_off + (uint32_t)((j & 1) * kTcKeys);
+#pragma unroll
+            for (int c = 0; c < kTcKeys / 32; ++c) tmem_ld32_nowait(s_addr + c * 32, sc + c * 32);
+            tmem_wait_ld();
+            tc_fence_before();
+            mbar_arrive(smem_u32(&s_empty[j & 1]));
+            const int kp0 = (tile_lo + j) * kTcKeys;
+            // Tiles wholly at or below the CTA's first position need no mask
+            // (no window); otherwise key i is visible iff wlo < i <= lim.
+            if (p.window > 0 || kp0 + kTcKeys - 1 > pos_first) {
+                const int lim = qpos - kp0;
+                const int wlo = p.window > 0 ? lim - p.window : -1;
+#pragma unroll
+                for (int i = 0; i < kTcKeys; ++i) sc[i] = (i <= lim && i > wlo) ? sc[i] : -INFINITY;
+            }
+            // Row max of the raw scores (scale > 0), eight partial chains.
+            float mx[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) mx[k] = sc[k];
+#pragma unroll
+            for (int i = 8; i < kTcKeys; ++i) mx[i & 7] = fmaxf(mx[i & 7], sc[i]);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) mx[k] = fmaxf(mx[k], mx[k + 4]);
+            const float tmax = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+            const float m_new = fmaxf(m_run, tmax * scale_log2);
+            const float alpha = m_new == -INFINITY ? 1.0f : exp2f(m_run - m_new);
+            // p = 2^(s * scale_log2 - m_new); a masked key (-inf) gives 0.
+            const float neg_m = m_new == -INFINITY ? 0.0f : -m_new;
+            float sums[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) sums[k] = 0.0f;
+            uint32_t packed[kTcKeys / 2];
+#pragma unroll
+            for (int i = 0; i < kTcKeys / 2; ++i) {
+                const float e0 = fast_exp2(fmaf(sc[2 * i], scale_log2, neg_m));
+                const float e1 = fast_exp2(fmaf(sc[2 * i + 1], scale_log2, neg_m));
+                sums[i & 7] += e0 + e1;
+                packed[i] = pack_bf16(e0, e1);
+            }
+#pragma unroll
+            for (int k = 0; k < 4; ++k) sums[k] += sums[k + 4];
+            const float rsum = (sums[0] + sums[1]) + (sums[2] + sums[3]);
+            l_run = l_run * alpha + rsum;
+            m_run = m_new;
+            if (j > 0) {
+                // PV_{j-1} done: fold O_t into O; P's buffer is free again.
+                if (!mbar_wait(smem_u32(&o_full), (j - 1) & 1)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                fold(alpha_prev);
+                tc_fence_before();
+            }
+            // P_j row r, K-major with 128-byte swizzle: keys 64b..64b+63 in
+            // block b, 16-byte chunk c of the row at (c ^ (r & 7)).
+#pragma unroll
+            for (int c = 0; c < kTcKeys / 8; ++c) {
+                const int blk = c >> 3, cc = c & 7;
+                uint4 *dst = reinterpret_cast<uint4 *>(p_row0 + blk * (kTcRows * 128) + ((cc ^ (r & 7)) << 4));
+                *dst = make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2], packed[4 * c + 3]);
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            mbar_arrive(smem_u32(&p_full));
+            alpha_prev = alpha;
+        }
+        if (ok && n_tiles > 0) {
+            if (mbar_wait(smem_u32(&o_full), (n_tiles - 1) & 1)) {
+                tc_fence_after();
+                fold(alpha_prev);
+            } else {
+                ok = false;
+            }
+        }
+        if (!ok) {
+            abort_s = 1;
+        } else if (t <= t_last) {
+            if (p.splits > 1) {
+                const long long rh = ((long long)split * p.T + t) * p.q_heads + head;
+                float4 *dst = reinterpret_cast<float4 *>(p.part_o + rh * HD);
+#pragma unroll
+                for (int i = 0; i < HD / 4; ++i) dst[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+                *reinterpret_cast<float2 *>(p.part_ml + rh * 2) = make_float2(m_run, l_run);
+            } else {
+                const float inv = l_run > 0.0f ? 1.0f / l_run : 0.0f;
+                uint4 *dst = reinterpret_cast<uint4 *>(p.out + (long long)t * p.q_heads * HD + head * HD);
+#pragma unroll
+                for (int i = 0; i < HD / 8; ++i) {
+                    dst[i] = make_uint4(pack_bf16(o[8 * i] * inv, o[8 * i + 1] * inv),
+                                        pack_bf16(o[8 * i + 2] * inv, o[8 * i + 3] * inv),
+                                        pack_bf16(o[8 * i + 4] * inv, o[8 * i + 5] * inv),
+                                        pack_bf16(o[8 * i + 6] * inv, o[8 * i + 7] * inv));
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (abort_s && threadIdx.x == 0 && p.error) *p.error = 8;
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)kTcTmemCols));
+    }
+}
+
+}  // namespace cheetah

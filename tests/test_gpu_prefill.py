@@ -101,3 +101,25 @@ def test_config3_shape_chunked_equals_stepwise(monkeypatch):
     ka, _ = a.kv_layer(23)
     kb, _ = b.kv_layer(23)
     assert np.abs(ka - kb).max() < 5e-2 * max(1.0, np.abs(kb).max())
+
+
+@pytest.mark.parametrize("chunk", ["256", "512"])
+def test_prefill_attention_key_splits_match_oracle(tiny_prepared, chunk, monkeypatch):
+    """A long cached prefix at an odd offset, then a multi-chunk prompt: the
+    tensor-core attention splits each row block's key range over several CTAs
+    (merged afterwards) and crosses 128-key tiles and 64-token pages
+    mid-chunk. Checked against the oracle and against the mma.sync kernel
+    (CHEETAH_PREFILL_TC=0)."""
+    monkeypatch.setenv("CHEETAH_PREFILL_CHUNK", chunk)
+    cfg, ref, model = _models(tiny_prepared)
+    toks = _toks(1700, cfg["vocab_size"], 19)
+    seq = model.new_sequence()
+    seq.forward(toks[:1003], 0)
+    ref.forward(toks[:1003], 0)
+    got = seq.forward(toks[1003:], 1003)
+    want = ref.forward(toks[1003:], 1003)
+    assert np.abs(got - want).max() < TOL
+    monkeypatch.setenv("CHEETAH_PREFILL_TC", "0")
+    other = model.new_sequence()
+    other.forward(toks[:1003], 0)
+    assert np.abs(other.forward(toks[1003:], 1003) - got).max() < TOL
