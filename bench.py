@@ -75,14 +75,21 @@ def synthetic_model(name):
 
 
 class ClockSampler:
-    """nvidia-smi clocks/throttle reasons sampled during the timed region."""
+    """nvidia-smi clocks/throttle reasons sampled during the timed region.
+    The constructor returns once the sampler has produced its first line (so
+    sampling is running when the timed region starts); stop() waits for one
+    sample past the end and keeps the samples taken from construction to one
+    interval after stop()."""
 
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, device_index: int, interval_ms: int = 50):
+    def __init__(self, device_index: int, interval_ms: int = 25):
+        import threading
         self.device_index = device_index
+        self.interval = interval_ms / 1e3
+        self.lines = []
         self.proc = None
         try:
             self.proc = subprocess.Popen(
@@ -91,19 +98,37 @@ class ClockSampler:
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except (OSError, ValueError):
             self.proc = None
+        if self.proc is not None:
+            self.reader = threading.Thread(target=self._read, daemon=True)
+            self.reader.start()
+            deadline = time.monotonic() + 5.0
+            while not self.lines and time.monotonic() < deadline and self.proc.poll() is None:
+                time.sleep(0.005)
+        self.t0 = time.monotonic()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append((time.monotonic(), line))
 
     def stop(self):
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        t1 = time.monotonic()
+        deadline = t1 + 1.0
+        while (not self.lines or self.lines[-1][0] < t1) and time.monotonic() < deadline:
+            time.sleep(0.005)
         self.proc.terminate()
         try:
-            out, _ = self.proc.communicate(timeout=5)
+            self.proc.wait(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
-            out, _ = self.proc.communicate()
+            self.proc.wait()
+        self.reader.join(timeout=5)
         sm, smax, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in out.splitlines():
+        for ts, line in list(self.lines):
+            if ts < self.t0 or ts > t1 + self.interval:
+                continue
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 9:
                 continue
