@@ -45,6 +45,19 @@ __device__ __forceinline__ uint16_t f32_to_bf16_rne(float value) {
     return static_cast<uint16_t>(bits >> 16);
 }
 
+// 2^x and 1/x with the hardware approximations (subnormal results flush to
+// zero), for values that are rounded to bf16 right after.
+__device__ __forceinline__ float fast_exp2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ float fast_rcp(float x) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 // ---- streaming loads (weights are read exactly once per step) ----
 __device__ __forceinline__ uint4 ldg_stream(const uint4 *ptr) {
     uint4 v;

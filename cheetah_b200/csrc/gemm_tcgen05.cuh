@@ -330,6 +330,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const int quad = warp % 4;
         const int row = m_tile * kGemmBM + quad * 32 + lane;
         const bool live = row < p.M;
+        // 64-column residual tiles: the row's residual slice is loaded while
+        // the MMAs run (it does not depend on them).
+        constexpr bool kPrefetch = EPI == kPgResidual && BN == 64;
+        float4 res_pre[kPrefetch ? 16 : 1];
+        if (kPrefetch && live && n_tile * BN < p.N) {
+            const float4 *s4 = reinterpret_cast<const float4 *>(p.out_f32 + (long long)row * p.ld_out + n_tile * BN);
+#pragma unroll
+            for (int i = 0; i < (kPrefetch ? 16 : 1); ++i) res_pre[i] = s4[i];
+        }
         const bool ok = mbar_wait(smem_u32(&done_bar), 0);
         tc_fence_after();
         const uint32_t acc_addr = tmem + ((uint32_t)(quad * 32) << 16);
@@ -340,7 +349,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const uint32_t lane_addr = tmem + ((uint32_t)(quad * 32) << 16);
             if (EPI == kPgResidual) {
                 // hidden[row][n] += acc (+ bias): 32 columns per step, float4 traffic.
-#pragma unroll 1
+#pragma unroll
                 for (int c0 = 0; c0 < BN; c0 += 32) {
                     float v[32];
                     tmem_ld32(lane_addr + c0, v);
@@ -348,8 +357,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     if (live && n0 < p.N) {
                         float4 *d4 = reinterpret_cast<float4 *>(p.out_f32 + (long long)row * p.ld_out + n0);
                         float4 r[8];
+                        if (kPrefetch) {
 #pragma unroll
-                        for (int i = 0; i < 8; ++i) r[i] = d4[i];
+                            for (int i = 0; i < 8; ++i) r[i] = res_pre[(c0 / 4 + i) % (kPrefetch ? 16 : 1)];
+                        } else {
+#pragma unroll
+                            for (int i = 0; i < 8; ++i) r[i] = d4[i];
+                        }
                         if (p.bias) {
                             const float4 *b4 = reinterpret_cast<const float4 *>(p.bias + n0);
 #pragma unroll
@@ -382,9 +396,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                         uint32_t packed[8];
 #pragma unroll
                         for (int i = 0; i < 8; ++i) {
-                            const float a0 = __fmul_rn(g[2 * i], __fdiv_rn(u[2 * i], __fadd_rn(1.0f, expf(-g[2 * i]))));
-                            const float a1 =
-                                __fmul_rn(g[2 * i + 1], __fdiv_rn(u[2 * i + 1], __fadd_rn(1.0f, expf(-g[2 * i + 1]))));
+                            // silu(g) * u = g * u / (1 + e^-g), rounded to bf16.
+                            const float a0 = g[2 * i] * u[2 * i] *
+                                             fast_rcp(1.0f + fast_exp2(g[2 * i] * -1.4426950408889634f));
+                            const float a1 = g[2 * i + 1] * u[2 * i + 1] *
+                                             fast_rcp(1.0f + fast_exp2(g[2 * i + 1] * -1.4426950408889634f));
                             packed[i] = (uint32_t)f32_to_bf16_rne(a0) | ((uint32_t)f32_to_bf16_rne(a1) << 16);
                         }
                         uint4 *dst = reinterpret_cast<uint4 *>(p.out_bf16 + (long long)row * p.ld_out + n0);

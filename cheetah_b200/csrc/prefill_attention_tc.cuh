@@ -70,14 +70,6 @@ __device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, float *v) {
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// 2^x with the hardware approximation (flushes subnormal results to zero);
-// the softmax weights are rounded to bf16 right after.
-__device__ __forceinline__ float fast_exp2(float x) {
-    float y;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-    return y;
-}
-
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 __global__ void __launch_bounds__(kTcThreads, 1)
