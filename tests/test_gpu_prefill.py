@@ -123,3 +123,24 @@ def test_prefill_attention_key_splits_match_oracle(tiny_prepared, chunk, monkeyp
     other = model.new_sequence()
     other.forward(toks[:1003], 0)
     assert np.abs(other.forward(toks[1003:], 1003) - got).max() < TOL
+
+
+def test_prefill_sliding_window_matches_oracle(tiny_prepared, monkeypatch):
+    """A 150-token sliding window (not a multiple of the 128-key tile) over a
+    cached prefix and two chunks: keys below the window are masked per row in
+    the tensor-core attention (`ops.rs:1366-1372`)."""
+    from cheetah_b200 import runtime as R
+    monkeypatch.setenv("CHEETAH_PREFILL_CHUNK", "256")
+    pm = PreparedModel(tiny_prepared)
+    cfg = dict(resolve_config(pm, 2048))
+    cfg["sliding_window"] = 150
+    ref = O.OracleModel(pm, cfg)
+    model = R.CudaModel(tiny_prepared, config=cfg)
+    toks = _toks(900, cfg["vocab_size"], 23)
+    seq = model.new_sequence()
+    seq.forward(toks[:300], 0)
+    ref.forward(toks[:300], 0)
+    got = seq.forward(toks[300:], 300)
+    want = ref.forward(toks[300:], 300)
+    assert np.abs(got - want).max() < TOL
+    model.close()
