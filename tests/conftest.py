@@ -2,7 +2,6 @@
 
 from __future__ import annotations
 
-import os
 import sys
 from pathlib import Path
 
@@ -58,7 +57,3 @@ def tinywide_prepared(tmp_path_factory):
     root = tmp_path_factory.mktemp("tiny_qwen2_widemlp")
     write_prepared(root, TINY_WIDE_MLP, seed=0)
     return root
-
-
-def reference_tree() -> Path:
-    return Path(os.environ.get("CHEETAH_REFERENCE", "/root/reference"))
