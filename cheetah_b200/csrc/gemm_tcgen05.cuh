@@ -15,7 +15,9 @@
 //   warps 2-5   epilogue: tcgen05.ld of the accumulator rows (warp w reads
 //               TMEM lanes 32*(w%4)..+31 = tile rows), fused epilogue, global
 //               stores.
-// All mbarrier waits are bounded (error flag + early exit, TMEM freed).
+// All mbarrier waits are bounded: on a timeout the CTA sets the error flag,
+// waits (bounded) for its own bulk copies and MMAs in flight, frees its TMEM
+// and exits.
 // Fused epilogues:
 //   kPgQkv      + bias, rotate-half RoPE (`ops.rs:693-715`, host rotary
 //               table), q rows -> bf16, K/V rows -> the paged cache
@@ -240,6 +242,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     __shared__ __align__(8) uint64_t full_bar[kGemmStages];
     __shared__ __align__(8) uint64_t empty_bar[kGemmStages];
     __shared__ __align__(8) uint64_t done_bar;
+    __shared__ __align__(8) uint64_t drain_bar;
     __shared__ uint32_t tmem_base_s;
     __shared__ int abort_s;
     __shared__ int split_last_s;
@@ -261,6 +264,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             mbar_init(smem_u32(&empty_bar[s]), 1);
         }
         mbar_init(smem_u32(&done_bar), 1);
+        mbar_init(smem_u32(&drain_bar), 1);
         abort_s = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -277,6 +281,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     pdl_wait();
     pdl_launch_dependents();
 
+    int issued = 0;  // k-blocks the producer has requested
     if (warp == 0) {
         if (lane == 0) {
             for (int kb = 0; kb < k_blocks; ++kb) {
@@ -302,6 +307,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                         tma_load_2d(smem_u32(b_dst + r * 64 * 128), &b_map, kx, n_tile * BN + r * 64, bar);
                     }
                 }
+                issued = kb + 1;
             }
         }
     } else if (warp == 1) {
@@ -345,6 +351,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const bool run = ok && (gridDim.z == 1 || split_k_reduce<BN>(p, acc_addr, quad * 32 + lane, &split_last_s));
         if (!ok) {
             if (p.error) *p.error = 4;
+            abort_s = 1;
         } else if (run) {
             const uint32_t lane_addr = tmem + ((uint32_t)(quad * 32) << 16);
             if (EPI == kPgResidual) {
@@ -518,7 +525,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     tc_fence_before();
     __syncthreads();
-    if (abort_s && threadIdx.x == 0 && p.error) *p.error = 5;
+    if (abort_s) {
+        // A wait gave up: let this CTA's copies and MMAs still in flight land
+        // before its shared memory and TMEM are released (bounded waits).
+        if (warp == 0 && lane == 0) {
+            for (int kb = max(0, issued - kGemmStages); kb < issued; ++kb) {
+                mbar_wait(smem_u32(&full_bar[kb % kGemmStages]), (kb / kGemmStages) & 1);
+            }
+        } else if (warp == 1 && lane == 0) {
+            umma_commit(smem_u32(&drain_bar));
+            mbar_wait(smem_u32(&drain_bar), 0);
+        }
+        tc_fence_before();
+        __syncthreads();
+        if (threadIdx.x == 0 && p.error && *p.error == 0) *p.error = 5;
+    }
     if (warp == 1) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)BN));

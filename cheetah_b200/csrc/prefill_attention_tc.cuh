@@ -21,8 +21,9 @@
 //               registers as each PV completes.
 // Key-range splits over blockIdx.z write unnormalised partials (O, m in log2
 // units, l) in prefill_attention_kernel's format, combined by
-// prefill_merge_kernel. All mbarrier waits are bounded (error flag, early
-// exit, TMEM freed).
+// prefill_merge_kernel. All mbarrier waits are bounded: on a timeout the CTA
+// sets the error flag, waits (bounded) for its own copies and MMAs in flight,
+// frees its TMEM and exits.
 #pragma once
 
 #include "gemm_tcgen05.cuh"
@@ -86,6 +87,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     __shared__ __align__(8) uint64_t s_empty[2];
     __shared__ __align__(8) uint64_t p_full;
     __shared__ __align__(8) uint64_t o_full;
+    __shared__ __align__(8) uint64_t drain_bar;
     __shared__ uint32_t tmem_base_s;
     __shared__ int abort_s;
 
@@ -124,6 +126,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         mbar_init(smem_u32(&p_full), kTcRows);
         mbar_init(smem_u32(&o_full), 1);
+        mbar_init(smem_u32(&drain_bar), 1);
         abort_s = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -140,6 +143,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     pdl_wait();
     pdl_launch_dependents();
 
+    int issued = 0;  // K/V tiles the producer has requested
     if (warp == 0) {
         if (lane == 0 && n_tiles > 0) {
             mbar_expect_tx(smem_u32(&q_full), kTcQBytes);
@@ -180,6 +184,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     tma_load_2d(smem_u32(ks + b * 64 * 128), &k_map, 0, rows[b], bar);
                     tma_load_2d(smem_u32(vs + b * 64 * 128), &v_map, 0, rows[b], bar);
                 }
+                issued = j + 1;
             }
         }
     } else if (warp == 1) {
@@ -355,7 +360,22 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     tc_fence_before();
     __syncthreads();
-    if (abort_s && threadIdx.x == 0 && p.error) *p.error = 8;
+    if (abort_s) {
+        // A wait gave up: let this CTA's copies and MMAs still in flight land
+        // before its shared memory and TMEM are released (bounded waits).
+        if (warp == 0 && lane == 0 && n_tiles > 0) {
+            mbar_wait(smem_u32(&q_full), 0);
+            for (int j = max(0, issued - kTcStages); j < issued; ++j) {
+                mbar_wait(smem_u32(&kv_full[j % kTcStages]), (j / kTcStages) & 1);
+            }
+        } else if (warp == 1 && lane == 0) {
+            umma_commit(smem_u32(&drain_bar));
+            mbar_wait(smem_u32(&drain_bar), 0);
+        }
+        tc_fence_before();
+        __syncthreads();
+        if (threadIdx.x == 0 && p.error) *p.error = 8;
+    }
     if (warp == 1) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)kTcTmemCols));
