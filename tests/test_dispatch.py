@@ -214,3 +214,14 @@ def test_world2_rank_that_never_reports_times_out_and_is_requeued():
     assert not store.check(["fail/1"]) and not store.check(["done/1"])
     assert out[0]["failed"] == [1]
     assert out[0]["merged"] == {str(i): work(i) for i in range(N_SEQ)}
+
+
+def test_requeue_respects_the_kv_budget():
+    reqs = [SeqRequest(i, 900, 100) for i in range(6)]   # 1000 KV tokens each
+    plan = plan_shards(reqs, 3, kv_budget=2000)           # two per rank
+    assert rank_load(plan, reqs) == [2000, 2000, 2000]
+    with pytest.raises(ValueError, match="budget"):
+        requeue(plan, reqs, [1], kv_budget=2000)         # survivors are full
+    plan2 = requeue(plan, reqs, [1], kv_budget=3000)
+    check_partition(plan2, reqs)
+    assert rank_load(plan2, reqs) == [3000, 0, 3000]
