@@ -1,26 +1,45 @@
 #!/usr/bin/env python
 """Benchmark of the Cheetah decoder hot path on B200 (driver contract).
 
-Default workload: Qwen2-0.5B-architecture decoder,
-seeded random-init bf16 weights in the prepared (`cheetah init`) layout,
-batch 1, a 512-token uniform-random prompt, then greedy decode. A timed
-"step" is one decode token through the whole model (embedding, 24 layers,
-final norm, lm_head, greedy argmax).
+One GPU (`--gpus 1`, the default). `value` is Qwen2-0.5B-architecture B=1
+greedy decode (config 1): seeded random-init bf16 weights in the prepared
+(`cheetah init`) layout, a 512-token uniform-random prompt, then greedy
+decode; a timed step is one token through the whole model (embedding, 24
+layers, final norm, lm_head, greedy argmax).
 
-  value  device-resident decode tok/s: K greedy steps chained on the device
-         (cheetah_cuda_generate_greedy), CUDA events on the sequence stream.
-  e2e    the same tokens through the public ModelForward call
-         (cheetah_cuda_forward_ex): host token in, host logits (vocab f32) +
-         greedy id out, every step, host wall clock.
-  roofline  the dominant kernel (bf16 weight-streaming GEMV) timed live with
-         CUDA events against MEASURED_PEAKS.json's copy bandwidth.
+  value      device-resident decode tok/s: K greedy steps chained on the
+             device (cheetah_cuda_generate_greedy), CUDA events on the
+             sequence stream.
+  e2e        the same tokens through the public ModelForward call
+             (cheetah_cuda_forward_ex): host token in, host logits (vocab
+             f32) + greedy id out, every step, host wall clock.
+  roofline   the persistent decode kernel per step against the measured copy
+             bandwidth (MEASURED_PEAKS.json).
   cpu_baseline  the C++ restatement of the reference AVX2 path (oracle/),
-         all host threads, on a bounded sample of the same workload.
+             all host threads, on a bounded sample of the same workload.
 
-`--impl reference` times that CPU restatement alone (the reference is Rust
-and cannot be built in this image). Under torchrun (N>1) each rank decodes
-its own sequence on its own GPU (sequence-sharded replicas, no collective on
-the data path); value = all ranks' tokens / max-over-ranks time.
+The other configurations of the path are sub-objects of the same line, each
+with its own roofline and CPU baseline:
+
+  attention  config 2: paged GQA decode attention, 14/2/64 and 28/4/128,
+             B in {1, 8, 32, 64}, L in {1k, 4k, 16k, 32k}.
+  prefill    config 3: 2048-token cached prefix + 4096-token prompt in
+             chunks of 512 (tensor-pipe roofline against the sustained bf16
+             figure).
+  serve      config 5 on one GPU: 64 sequences, prompts U[128, 8192],
+             outputs U[32, 512], half sharing a 1024-token prefix.
+  decode_7b  config 4: Qwen2-7B architecture, q8 / q4 / bf16 linears,
+             1024-token prompt, device-chained greedy steps.
+
+N GPUs (torchrun, N > 1): `value` is config 5, the 64 sequences sharded over
+the ranks by the KV-token planner (cheetah_b200.dispatch.plan_shards); each
+rank decodes its share with batched greedy steps, and value = generated
+tokens of all ranks / max-over-ranks device time (strong scaling of a fixed
+sequence set; no collective on the data path).
+
+`--impl reference` times the reference's CPU path for the same config (the
+reference is Rust and cannot be built in this image: its AVX2 path runs as
+the C++ restatement in oracle/).
 """
 
 from __future__ import annotations
@@ -40,14 +59,22 @@ sys.path.insert(0, str(ROOT))
 
 PROMPT_LEN = 512
 METRIC = "decode tok/s (B=1 & batched) + GQA attn HBM GB/s vs peak; prefill tok/s"
+SERVE_SEQS = 64
+SERVE_PREFIX = 1024
+# Kernels one chained batched step launches: embedding, 7 per layer (norm,
+# QKV GEMM, attention, o_proj GEMM, norm, gate/up GEMM, down GEMM), final
+# norm, lm_head GEMM + argmax, and the row-advance kernel.
+BATCH_STEP_FIXED_LAUNCHES = 4
+BATCH_STEP_LAUNCHES_PER_LAYER = 7
 
 
 def peaks():
     path = ROOT / "MEASURED_PEAKS.json"
     if path.exists():
         data = json.loads(path.read_text())
-        return float(data["hbm_gbs"]), float(data.get("bf16_tflops", 1634.5)), "measured"
-    return 6650.0, 1590.0, "fallback"
+        return (float(data["hbm_gbs"]), float(data.get("bf16_tflops", 1590.0)),
+                float(data.get("bf16_tflops_sustained", data.get("bf16_tflops", 1400.0))), "measured")
+    return 6650.0, 1590.0, 1400.0, "fallback"
 
 
 def dist_env():
@@ -72,6 +99,26 @@ def synthetic_model(name):
             raise RuntimeError(f"timed out waiting for {target}")
         time.sleep(1.0)
     return target
+
+
+def workload_config(world: int) -> dict:
+    """The `config` of the line: identical in both arms (ours and the
+    reference's) for the same number of GPUs."""
+    if world == 1:
+        return {"workload": "qwen2-0.5b decode B=1 (config 1: 512-token prompt, greedy decode)",
+                "model": "Qwen2-0.5B architecture", "global_batch": 1, "seq_len": PROMPT_LEN,
+                "parallelism": "single GPU", "kv_cache": "paged bf16, 64-token pages",
+                "l2": "inputs larger than L2 (988 MB of weights streamed per step > 126 MB L2)"}
+    return serve_config(world)
+
+
+def serve_config(world: int) -> dict:
+    return {"workload": f"config 5: qwen2-0.5b batched serving, {SERVE_SEQS} sequences sharded over {world} GPU(s)",
+            "model": "Qwen2-0.5B architecture", "global_batch": SERVE_SEQS,
+            "seq_len": "prompts U[128, 8192], outputs U[32, 512], half share a 1024-token prefix",
+            "parallelism": f"sequence-sharded x{world} (KV-token planner; no collective on the data path)",
+            "kv_cache": "paged bf16, 64-token pages",
+            "l2": "inputs larger than L2 (988 MB of weights + the batch's K/V per step)"}
 
 
 class ClockSampler:
@@ -145,22 +192,43 @@ class ClockSampler:
                 "samples": len(sm), "reasons": sorted(reasons)}
 
 
-def cpu_baseline(model_dir, cfg, decode_steps: int):
-    """Oracle (C++ restatement of the reference AVX2 path) decode tok/s on a
-    bounded sample: 512-token prompt (untimed prefill) + decode steps."""
-    import oracle as O
-    from cheetah_b200.prepared import PreparedModel
+# ---------------------------------------------------------------------------
+# CPU baselines: the C++ restatement of the reference AVX2 path (oracle/),
+# all host threads, bounded samples. The oracle is the timed baseline here,
+# never the thing measured as ours.
 
-    O.set_threads(os.cpu_count() or 1)
-    pm = PreparedModel(model_dir)
-    ref = O.OracleModel(pm, cfg, "bf16")
+def _oracle(threads: int = 0):
+    import oracle as O
+    O.set_threads(threads or os.cpu_count() or 1)
+    return O
+
+
+def _oracle_model(model_dir, cfg, quant="bf16"):
+    from cheetah_b200.prepared import PreparedModel
+    O = _oracle()
+    return O, O.OracleModel(PreparedModel(model_dir), cfg, quant)
+
+
+def _random_kv(ref, cfg, positions: int, seed: int) -> None:
+    """Fill the oracle's KV cache with `positions` seeded N(0, 1) rows (the
+    cost of a decode step does not depend on the cached values)."""
+    rng = np.random.default_rng(seed)
+    n = positions * cfg["kv_heads"] * cfg["head_dim"]
+    layers = [(rng.standard_normal(n, dtype=np.float32), rng.standard_normal(n, dtype=np.float32))
+              for _ in range(cfg["num_layers"])]
+    ref.clear_cache()
+    ref.restore_kv_prefix((positions, layers), positions)
+
+
+def cpu_decode_05b(model_dir, cfg, decode_steps: int):
+    """Config 1 on the CPU: 512-token prompt (untimed prefill), then timed
+    greedy decode steps."""
+    O, ref = _oracle_model(model_dir, cfg)
     prompt = np.random.default_rng(1).integers(0, cfg["vocab_size"], PROMPT_LEN).astype(np.uint32)
-    logits = ref.forward(prompt, 0)
-    tok = int(np.argmax(logits))
+    tok = int(np.argmax(ref.forward(prompt, 0)))
     t0 = time.perf_counter()
     for i in range(decode_steps):
-        logits = ref.forward([tok], PROMPT_LEN + i)
-        tok = int(np.argmax(logits))
+        tok = int(np.argmax(ref.forward([tok], PROMPT_LEN + i)))
     dt = time.perf_counter() - t0
     return {"value": decode_steps / dt, "unit": "tok/s", "cores": O.threads(), "kind": "port",
             "sample": f"Qwen2-0.5B B=1: {decode_steps} greedy decode steps after a {PROMPT_LEN}-token "
@@ -168,50 +236,106 @@ def cpu_baseline(model_dir, cfg, decode_steps: int):
             "ms_per_token": 1e3 * dt / decode_steps}
 
 
-def run_reference(args):
-    world, rank, _ = dist_env()
-    if rank != 0:
-        return 0
-    from cheetah_b200.prepared import PreparedModel, cached_synthetic, resolve_config
-    model_dir = synthetic_model("qwen2-0.5b")
-    cfg = resolve_config(PreparedModel(model_dir))
-    per_step = []
-    import oracle as O
-    O.set_threads(os.cpu_count() or 1)
-    ref = O.OracleModel(PreparedModel(model_dir), cfg, "bf16")
-    prompt = np.random.default_rng(1).integers(0, cfg["vocab_size"], PROMPT_LEN).astype(np.uint32)
-    tok = int(np.argmax(ref.forward(prompt, 0)))
-    pos = PROMPT_LEN
-    for i in range(args.warmup + args.steps):
+def cpu_attention(rows_gpu):
+    """Config 2 on the CPU: the restated `attention` (`ops.rs:1357-1467`,
+    parallel over heads) for one sequence at each shape and L, timed per call;
+    reported in the GPU rows' unit (algorithmic bytes of a B=1 call / time)."""
+    O = _oracle()
+    out = []
+    for qh, kvh, D in [(14, 2, 64), (28, 4, 128)]:
+        for L in (1024, 32768):
+            rng = np.random.default_rng(L + D)
+            k = rng.standard_normal(L * kvh * D, dtype=np.float32)
+            v = rng.standard_normal(L * kvh * D, dtype=np.float32)
+            q = rng.standard_normal(qh * D, dtype=np.float32)
+            O.attention(k, v, q, qh, kvh, D)
+            reps = 20 if L <= 4096 else 5
+            t0 = time.perf_counter()
+            for _ in range(reps):
+                O.attention(k, v, q, qh, kvh, D)
+            sec = (time.perf_counter() - t0) / reps
+            bytes_ = kvh * L * D * 2 * 2 + qh * D * 4 * 2
+            out.append({"shape": f"{qh}/{kvh}/{D}", "B": 1, "L": L, "us": round(sec * 1e6, 1),
+                        "GBps": round(bytes_ / sec / 1e9, 2)})
+    best = max(out, key=lambda r: r["GBps"])
+    return {"value": best["GBps"], "unit": "GB/s", "cores": O.threads(), "kind": "port",
+            "sample": "one sequence (B=1) per call at L=1k and 32k for both shapes, f32 cache; GB/s counts "
+                      "the GPU rows' algorithmic bytes (bf16 K/V) for the same work; value = best row",
+            "rows": out}
+
+
+def cpu_prefill(model_dir, cfg):
+    """Config 3 on the CPU: the restated chunked prefill (`forward_chunked`
+    with 512-row chunks) of the first and the last 512-token chunk of the
+    4096-token prompt (positions 2048-2559 and 5632-6143) over a 2048-token
+    cached prefix and the chunks before them (seeded KV); the 8 chunks are
+    interpolated linearly between the two (attention grows linearly with the
+    position, the GEMMs do not change)."""
+    O, ref = _oracle_model(model_dir, cfg)
+    toks = np.random.default_rng(3).integers(0, cfg["vocab_size"], 512).astype(np.uint32)
+    times = []
+    for start in (2048, 5632):
+        _random_kv(ref, cfg, start, seed=start)
         t0 = time.perf_counter()
-        tok = int(np.argmax(ref.forward([tok], pos)))
-        pos += 1
-        if i >= args.warmup:
-            per_step.append(time.perf_counter() - t0)
-    total = sum(per_step)
-    value = len(per_step) / total
-    line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / len(per_step),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic (seeded random-init bf16 weights, uniform-random prompt ids)",
-        "config": {"workload": "qwen2-0.5b decode B=1 (512-token prompt, greedy)", "batch": 1,
-                   "prompt": PROMPT_LEN, "parallelism": "single process (CPU)"},
-        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": O.threads(), "kind": "port",
-                         "sample": f"{args.steps} decode steps after a {PROMPT_LEN}-token prompt; the "
-                                   "reference is Rust (no toolchain here), so its AVX2 path runs as the "
-                                   "C++ restatement in oracle/"},
-        "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }
-    print(json.dumps(line), flush=True)
-    return 0
+        ref.forward(toks, start, chunk_rows=512)
+        times.append(time.perf_counter() - t0)
+    est = sum(times[0] + (times[1] - times[0]) * k / 7 for k in range(8))
+    return {"value": 4096 / est, "unit": "tok/s", "cores": O.threads(), "kind": "port",
+            "sample": "first and last 512-token chunk of the 4096-token prompt timed (seeded KV stands in for "
+                      "the cached positions), the 8 chunks interpolated linearly between them",
+            "chunk_s": [round(t, 3) for t in times]}
 
 
-# DRAM bytes (read + write) of one decode step of the persistent kernel,
-# Qwen2-0.5B, context ~600: ncu dram__bytes_read.sum + dram__bytes_write.sum
-# of a one-step launch (summary and command in profiles/).
-DECODE_STEP_DRAM_BYTES = 998049536
+def cpu_serve(model_dir, cfg, reqs):
+    """Config 5 on the CPU: the reference serves one sequence at a time on all
+    host cores (max-concurrent 1). A decode step is timed at a short and a
+    long context (seeded KV) and the per-token time, linear in the context,
+    is summed over every generated token of the 64 sequences (a tokens-only
+    projection of the whole run)."""
+    O, ref = _oracle_model(model_dir, cfg)
+    pts = []
+    for ctx in (256, 8192):
+        _random_kv(ref, cfg, ctx, seed=ctx)
+        tok = 17
+        ref.forward([tok], ctx)
+        t0 = time.perf_counter()
+        for i in range(4):
+            ref.forward([tok], ctx + 1 + i)
+        pts.append((ctx, (time.perf_counter() - t0) / 4))
+    (c0, t0_), (c1, t1_) = pts
+    slope = (t1_ - t0_) / (c1 - c0)
+    total_s = 0.0
+    tokens = 0
+    for r in reqs:
+        n = r.output_len - 1  # the first token comes from the prefill
+        mean_ctx = r.prompt_len + (n + 1) / 2
+        total_s += n * (t0_ + slope * (mean_ctx - c0))
+        tokens += n
+    return {"value": tokens / total_s, "unit": "tok/s", "cores": O.threads(), "kind": "port",
+            "sample": f"decode steps timed at contexts {c0} and {c1} (seeded KV); per-token time linear in the "
+                      f"context, summed over the {tokens} decode tokens of the {len(reqs)} sequences served one "
+                      "at a time (projection)",
+            "ms_per_token_at": {str(c0): round(1e3 * t0_, 3), str(c1): round(1e3 * t1_, 3)}}
 
+
+def cpu_decode_7b(model_dir, cfg, quant: str, steps: int = 3):
+    """Config 4 on the CPU: the restated 7B decoder with the reference's
+    per-row q8/q4 quantisation (or bf16) at load, decode steps at context
+    1024 (seeded KV stands in for the 1024-token prompt)."""
+    O, ref = _oracle_model(model_dir, cfg, quant)
+    _random_kv(ref, cfg, 1024, seed=7)
+    ref.forward([11], 1024)
+    t0 = time.perf_counter()
+    for i in range(steps):
+        ref.forward([11], 1025 + i)
+    dt = (time.perf_counter() - t0) / steps
+    return {"value": 1.0 / dt, "unit": "tok/s", "cores": O.threads(), "kind": "port",
+            "sample": f"Qwen2-7B {quant}: {steps} decode steps at context 1024 (seeded KV stands in for the "
+                      "1024-token prompt)", "ms_per_token": 1e3 * dt}
+
+
+# ---------------------------------------------------------------------------
+# GPU measurements
 
 def gemv_roofline(torch, R, hbm_peak, reps=20):
     """Time the lm_head-shaped bf16 GEMV (151936 x 896, 272 MB > L2) with CUDA
@@ -238,7 +362,8 @@ def gemv_roofline(torch, R, hbm_peak, reps=20):
 
 
 def attention_microbench(torch, R, hbm_peak, quick: bool):
-    """Config 2: paged GQA decode attention, bf16 K/V ~N(0,1), shuffled pages."""
+    """Config 2: paged GQA decode attention, bf16 K/V ~N(0,1), shuffled pages.
+    Launches are timed back to back with CUDA events on their stream."""
     rows = []
     shapes = [(14, 2, 64), (28, 4, 128)]
     batches = [1, 8, 32, 64]
@@ -281,7 +406,7 @@ def attention_microbench(torch, R, hbm_peak, quick: bool):
     return rows
 
 
-def prefill_bench(torch, R, model_dir, cfg, reps: int = 3):
+def prefill_bench(torch, R, model_dir, cfg, tensor_peak, reps: int = 3):
     """Config 3: 2048-token cached prefix, then a 4096-token prompt in chunks
     of 512 (CHEETAH_PREFILL_CHUNK=512); the prefix is restored from a device
     snapshot before every repetition. CUDA events on the sequence stream."""
@@ -315,224 +440,289 @@ def prefill_bench(torch, R, model_dir, cfg, reps: int = 3):
     del seq, snap
     model.close()
     os.environ.pop("CHEETAH_PREFILL_CHUNK", None)
+    tflops = total / sec / 1e12
     return {"workload": "config 3: 0.5B, 2048-token cached prefix + 4096-token prompt, chunks of 512",
-            "tok_per_s": prompt / sec, "ms": sec * 1e3, "tflops": total / sec / 1e12,
+            "value": prompt / sec, "unit": "tok/s", "tok_per_s": prompt / sec, "ms": sec * 1e3,
+            "tflops": tflops,
             "flops": {"linear": lin_flops, "attention": attn_flops, "lm_head": lm_flops},
+            "roofline": {"bound": "tensor", "kernel": "whole prefill (tcgen05 GEMMs + tcgen05 attention)",
+                         "achieved": tflops, "peak": tensor_peak, "unit": "TFLOP/s", "frac": tflops / tensor_peak,
+                         "peak_kind": "bf16_tflops_sustained (measured)", "traffic": None},
             "timing": f"min of {reps} repetitions, CUDA events on the sequence stream"}
 
 
-def decode_7b(args):
-    """Config 4: Qwen2-7B-architecture decode (B=1) with q8 / q4 / bf16 linears:
-    1024-token prompt, then device-chained greedy steps."""
-    import torch
-    from cheetah_b200 import runtime as R
-    from cheetah_b200.prepared import PreparedModel, cached_synthetic, resolve_config
-    quant = args.workload.split("-")[-1]
-    model_dir = synthetic_model("qwen2-7b")
-    cfg = resolve_config(PreparedModel(model_dir))
-    hbm_peak, _, peak_kind = peaks()
+def decode_7b_run(torch, R, model_dir, cfg, quant, steps, warmup, hbm_peak, prompt_len=1024):
+    """Config 4 on one GPU: 1024-token prompt, then device-chained greedy
+    steps; CUDA events on the sequence stream."""
     model = R.CudaModel(model_dir, quant=quant, max_positions=4096)
     seq = model.new_sequence()
-    prompt = np.random.default_rng(1).integers(0, cfg["vocab_size"], 1024).astype(np.uint32)
+    prompt = np.random.default_rng(1).integers(0, cfg["vocab_size"], prompt_len).astype(np.uint32)
     first = int(np.argmax(seq.forward(prompt, 0)))
-    warm = seq.generate_greedy(first, 1024, args.warmup)
+    warm = seq.generate_greedy(first, prompt_len, warmup)
     stream = torch.cuda.ExternalStream(seq.stream_handle())
     torch.cuda.synchronize()
-    clocks = ClockSampler(0)
+    clocks = ClockSampler(torch.cuda.current_device())
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s.record(stream)
-    seq.generate_greedy(int(warm[-1]), 1024 + args.warmup, args.steps, wait=False)
+    seq.generate_greedy(int(warm[-1]), prompt_len + warmup, steps, wait=False)
     e.record(stream)
     e.synchronize()
     clock_info = clocks.stop()
     sec = s.elapsed_time(e) / 1e3
     info = model.info()
-    ctx = 1024 + args.warmup + args.steps / 2
+    ctx = prompt_len + warmup + steps / 2
     kv = cfg["num_layers"] * cfg["kv_heads"] * cfg["head_dim"] * 2 * 2 * ctx
     # An untied embedding table is not streamed per token: one bf16 row is.
     embed = 0 if cfg["tie_word_embeddings"] else (cfg["vocab_size"] - 1) * cfg["hidden_size"] * 2
     step_bytes = info["weight_bytes"] - embed + kv
-    gbs = step_bytes / (sec / args.steps) / 1e9
-    line = {"metric": METRIC, "value": args.steps / sec, "unit": "tok/s", "n_gpus": 1, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": 1e3 * sec / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": quant,
-            "data": "synthetic (seeded random-init bf16 weights quantised per row at load)",
-            "config": {"workload": f"qwen2-7b decode B=1 {quant} (config 4: 1024-token prompt)",
-                       "model": "Qwen2-7B architecture", "global_batch": 1, "seq_len": 1024},
-            "clocks": clock_info,
-            "step_roofline": {"bytes_per_token": step_bytes, "achieved_GBps": gbs, "peak": hbm_peak,
-                              "peak_kind": peak_kind, "frac_measured": gbs / hbm_peak, "frac_8TBps": gbs / 8000.0}}
-    print(json.dumps(line), flush=True)
-    return 0
+    gbs = step_bytes / (sec / steps) / 1e9
+    del seq
+    model.close()
+    return {"value": steps / sec, "unit": "tok/s", "steps": steps, "warmup": warmup,
+            "ms_per_step": 1e3 * sec / steps, "dtype": quant, "clocks": clock_info,
+            "roofline": {"bound": "hbm", "kernel": "7B decode step (multi-kernel graph)", "achieved": gbs,
+                         "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak, "frac_8TBps": gbs / 8000.0,
+                         "algorithmic_bytes_per_step": step_bytes, "traffic": None}}
 
 
-def serve_bench(args):
-    """Config 5: 64 concurrent sequences, prompts ~U[128, 8192], outputs
-    ~U[32, 512] (seed 2); half share a 1024-token prefix (prefilled once per
-    rank, restored from a device snapshot like the engine's prefix cache). The
-    64 sequences are sharded across the ranks by the KV-token planner
-    (cheetah_b200.dispatch.plan_shards; strong scaling); each rank
-    prefills its share, then decodes it with batched greedy steps chained on
-    the device (cheetah_cuda_forward_batch_greedy, one call per change of the
-    batch) until every sequence has its output length.
-    value = generated tokens of all ranks / max-over-ranks decode time."""
+def serve_requests(cfg):
+    """Config 5's 64 sequences (seed 2): prompt and output lengths, which ones
+    share the 1024-token prefix, and every prompt's ids."""
+    from cheetah_b200.dispatch import SeqRequest
+    rng = np.random.default_rng(2)
+    prompt_len = rng.integers(128, 8193, SERVE_SEQS)
+    out_len = rng.integers(32, 513, SERVE_SEQS)
+    shared = set(rng.permutation(SERVE_SEQS)[: SERVE_SEQS // 2].tolist())
+    prefix = rng.integers(0, cfg["vocab_size"], SERVE_PREFIX).astype(np.uint32)
+    uses_prefix = [i in shared and prompt_len[i] > SERVE_PREFIX for i in range(SERVE_SEQS)]
+    reqs = [SeqRequest(i, int(prompt_len[i]), int(out_len[i]), 0 if uses_prefix[i] else None)
+            for i in range(SERVE_SEQS)]
+    prompts = {}
+    for i in range(SERVE_SEQS):
+        body = rng.integers(0, cfg["vocab_size"], int(prompt_len[i])).astype(np.uint32)
+        if uses_prefix[i]:
+            body[:SERVE_PREFIX] = prefix
+        prompts[i] = body
+    return reqs, prompts, prefix, uses_prefix
+
+
+def serve_run(torch, R, model_dir, cfg, world, rank, local, hbm_peak, reqs, prompts, prefix, uses_prefix):
+    """Config 5 on this rank: prefill its share of the sequences (the shared
+    prefix once, restored from a device snapshot like the engine's prefix
+    cache), then decode them twice from the same state:
+
+    value  batched greedy steps chained on the device
+           (cheetah_cuda_forward_batch_greedy, one call per change of the
+           batch); CUDA events on the model's batch stream.
+    e2e    one public batched call per step (cheetah_cuda_forward_batch):
+           host token ids in, greedy ids out, host wall clock.
+    Returns this rank's numbers (not yet reduced over ranks)."""
+    from cheetah_b200.dispatch import plan_shards, rank_load
+    plan = plan_shards(reqs, world)
+    mine = plan[rank]
+    kv_tokens = int(sum(reqs[i].kv_tokens for i in mine))
+    # Room for the sequences, their per-sequence snapshots and the prefix.
+    pool = 2 * int(sum(reqs[i].kv_tokens + 64 for i in mine)) + 2 * SERVE_PREFIX + 4096
+    model = R.CudaModel(model_dir, max_positions=8192 + 512 + 128, kv_pool_tokens=pool, device=local)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    snap = None
+    if any(uses_prefix[i] for i in mine):
+        pre = model.new_sequence()
+        pre.forward(prefix, 0)
+        snap = pre.kv_snapshot()
+    seqs, first, offs, left, snaps = [], [], [], [], []
+    for i in mine:
+        seq = model.new_sequence()
+        start = 0
+        if snap is not None and uses_prefix[i]:
+            seq.restore_kv_prefix(snap, SERVE_PREFIX)
+            start = SERVE_PREFIX
+        logits = seq.forward(prompts[i][start:], start)
+        seqs.append(seq)
+        first.append(int(np.argmax(logits)))
+        offs.append(reqs[i].prompt_len)
+        left.append(reqs[i].output_len - 1)
+    torch.cuda.synchronize()
+    prefill_s = time.perf_counter() - t0
+    prefill_tokens = int(sum(reqs[i].prompt_len for i in mine))
+    snaps = [s.kv_snapshot() for s in seqs]
+    kv_per_pos = cfg["num_layers"] * cfg["kv_heads"] * cfg["head_dim"] * 2 * 2
+    weight_bytes = model.info()["weight_bytes"]
+
+    def decode(chained: bool):
+        toks, o, lf = list(first), list(offs), list(left)
+        generated, steps, batch_sizes, algo_bytes = 0, 0, [], 0.0
+        active = [j for j in range(len(seqs)) if lf[j] > 0]
+        while active:
+            n = min(lf[j] for j in active) if chained else 1
+            for i in range(n):
+                algo_bytes += weight_bytes + kv_per_pos * sum(o[j] + i + 1 for j in active)
+            if chained:
+                out = model.forward_batch_greedy([seqs[j] for j in active], [toks[j] for j in active],
+                                                 [o[j] for j in active], n)
+                last = out[:, -1]
+            else:
+                last = model.forward_batch([seqs[j] for j in active], [toks[j] for j in active],
+                                           [o[j] for j in active])
+            batch_sizes.extend([len(active)] * n)
+            for k, j in enumerate(active):
+                toks[j] = int(last[k])
+                o[j] += n
+                lf[j] -= n
+                generated += n
+            active = [j for j in active if lf[j] > 0]
+            steps += n
+        return generated, steps, batch_sizes, algo_bytes
+
+    def rewind():
+        for s, sn, j in zip(seqs, snaps, range(len(seqs))):
+            s.restore_kv_prefix(sn, offs[j])
+        torch.cuda.synchronize()
+
+    # Warm-up: one short chained call captures the step graphs of the
+    # first batch size.
+    if seqs:
+        model.forward_batch_greedy(seqs, first, offs, 1)
+        rewind()
+    stream = torch.cuda.ExternalStream(model.batch_stream_handle()) if seqs else torch.cuda.current_stream()
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record(stream)
+    generated, steps, batch_sizes, algo_bytes = decode(True)
+    e.record(stream)
+    e.synchronize()
+    clock_info = clocks.stop()
+    decode_s = s.elapsed_time(e) / 1e3
+    rewind()
+    if world > 1:
+        torch.distributed.barrier()
+    t1 = time.perf_counter()
+    g2, steps2, _, _ = decode(False)
+    e2e_s = time.perf_counter() - t1
+    assert g2 == generated
+    del snaps, seqs, snap
+    model.close()
+    return {"generated": generated, "steps": steps, "decode_s": decode_s, "e2e_s": e2e_s, "e2e_steps": steps2,
+            "mean_batch": float(np.mean(batch_sizes)) if batch_sizes else 0.0, "algo_bytes": algo_bytes,
+            "kv_tokens": kv_tokens, "kv_share": kv_tokens / max(1, sum(rank_load(plan, reqs))),
+            "prefill_tokens": prefill_tokens, "prefill_s": prefill_s, "sequences": len(mine),
+            "clocks": clock_info}
+
+
+def serve_summary(per_rank, world, hbm_peak, cpu=None):
+    """Whole-job numbers from every rank's serve_run (max-over-ranks times)."""
+    decode_s = max(r["decode_s"] for r in per_rank)
+    e2e_s = max(r["e2e_s"] for r in per_rank)
+    generated = sum(r["generated"] for r in per_rank)
+    steps = max(r["steps"] for r in per_rank)
+    busiest = max(per_rank, key=lambda r: r["decode_s"])
+    gbs = busiest["algo_bytes"] / busiest["decode_s"] / 1e9 if busiest["decode_s"] else 0.0
+    out = {
+        "value": generated / decode_s, "unit": "tok/s", "n_gpus": world, "steps": steps,
+        "ms_per_step": 1e3 * decode_s / max(steps, 1), "scaling": "strong",
+        "decode": {"tokens": generated, "seconds": decode_s,
+                   "timing": "CUDA events on each rank's batch stream around the chained batched decode "
+                             "(cheetah_cuda_forward_batch_greedy, one call per change of the batch); max over ranks"},
+        "e2e": {"value": generated / e2e_s, "unit": "tok/s", "ms_per_step": 1e3 * e2e_s / max(steps, 1),
+                "h2d_bytes_per_step": int(round(np.mean([12 * r["mean_batch"] for r in per_rank]))),
+                "d2h_bytes_per_step": int(round(np.mean([4 * r["mean_batch"] for r in per_rank]))),
+                "api": "cheetah_cuda_forward_batch once per step (host token ids + offsets in, greedy ids out), "
+                       "host wall clock, max over ranks"},
+        "per_rank": [{"rank": k, "sequences": r["sequences"], "mean_batch": round(r["mean_batch"], 2),
+                      "kv_share": round(r["kv_share"], 4), "decode_s": round(r["decode_s"], 4),
+                      "steps": r["steps"], "tokens": r["generated"]} for k, r in enumerate(per_rank)],
+        "busiest_rank_kv_share": max(r["kv_share"] for r in per_rank),
+        "roofline": {"bound": "hbm", "kernel": "batched decode step (slowest rank)", "achieved": gbs,
+                     "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak, "traffic": None,
+                     "algorithmic_bytes": "per step: every weight byte once + the K/V rows of every active "
+                                          "sequence's context"},
+        "prefill": {"tokens": sum(r["prefill_tokens"] for r in per_rank),
+                    "seconds": max(r["prefill_s"] for r in per_rank)},
+        "clocks": busiest["clocks"],
+    }
+    if cpu is not None:
+        out["cpu_baseline"] = cpu
+    return out
+
+
+def _gather_dicts(torch, obj, world):
+    """Every rank's JSON-serialisable dict, on every rank (NCCL all_gather of
+    a fixed-size byte tensor; every rank takes this step)."""
+    if world == 1:
+        return [obj]
+    data = json.dumps(obj).encode()
+    buf = torch.zeros(8192, dtype=torch.uint8, device="cuda")
+    assert len(data) <= buf.numel()
+    buf[: len(data)] = torch.tensor(list(data), dtype=torch.uint8, device="cuda")
+    outs = [torch.zeros_like(buf) for _ in range(world)]
+    torch.distributed.all_gather(outs, buf)
+    return [json.loads(bytes(o.cpu().numpy().tolist()).rstrip(b"\0").decode()) for o in outs]
+
+
+def run_serve(args):
+    """`--gpus N` with N > 1 (or `--workload serve-0.5b`): config 5 is the value."""
     import torch
     from cheetah_b200 import runtime as R
-    from cheetah_b200.dispatch import SeqRequest, plan_shards
-    from cheetah_b200.prepared import PreparedModel, cached_synthetic, resolve_config
+    from cheetah_b200.prepared import PreparedModel, resolve_config
+    from datetime import timedelta
 
     world, rank, local = dist_env()
     torch.cuda.set_device(local)
     if world > 1:
-        import torch.distributed as dist
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300))
-    name = "qwen2-0.5b" if args.workload == "serve-0.5b" else "qwen2-7b"
-    model_dir = synthetic_model(name)
+        torch.distributed.init_process_group("nccl", timeout=timedelta(seconds=300))
+    hbm_peak, _, _, peak_kind = peaks()
+    model_dir = synthetic_model("qwen2-0.5b")
     cfg = resolve_config(PreparedModel(model_dir))
-    rng = np.random.default_rng(2)
-    n_seq = 64
-    prompt_len = rng.integers(128, 8193, n_seq)
-    out_len = rng.integers(32, 513, n_seq)
-    shared = rng.permutation(n_seq)[: n_seq // 2]
-    prefix = rng.integers(0, cfg["vocab_size"], 1024).astype(np.uint32)
-    reqs = [SeqRequest(i, int(prompt_len[i]), int(out_len[i]),
-                       0 if (i in shared and prompt_len[i] > 1024) else None) for i in range(n_seq)]
-    mine = plan_shards(reqs, world)[rank]
-    pool = int(sum(prompt_len[i] + out_len[i] + 64 for i in mine)) + 4096
-    model = R.CudaModel(model_dir, max_positions=8192 + 512 + 128, kv_pool_tokens=pool, device=local)
-    prompts = {}
-    for i in range(n_seq):
-        body = rng.integers(0, cfg["vocab_size"], int(prompt_len[i])).astype(np.uint32)
-        if i in shared and prompt_len[i] > 1024:
-            body[:1024] = prefix
-        prompts[i] = body
-    torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    snap = None
-    if any(i in shared and prompt_len[i] > 1024 for i in mine):
-        pre = model.new_sequence()
-        pre.forward(prefix, 0)
-        snap = pre.kv_snapshot()
-    seqs, toks, offs, left = [], [], [], []
-    for i in mine:
-        seq = model.new_sequence()
-        start = 0
-        if snap is not None and i in shared and prompt_len[i] > 1024:
-            seq.restore_kv_prefix(snap, 1024)
-            start = 1024
-        logits = seq.forward(prompts[i][start:], start)
-        seqs.append(seq)
-        toks.append(int(np.argmax(logits)))
-        offs.append(int(prompt_len[i]))
-        left.append(int(out_len[i]) - 1)
-    torch.cuda.synchronize()
-    prefill_s = time.perf_counter() - t0
-    prefill_tokens = int(sum(prompt_len[i] for i in mine))
-    if world > 1:
-        torch.distributed.barrier()
-    generated, steps, batch_sizes = len(mine), 0, []
-    t1 = time.perf_counter()
-    active = [j for j in range(len(seqs)) if left[j] > 0]
-    while active:
-        # Greedy ids stay on the device until the next sequence finishes.
-        n = min(left[j] for j in active)
-        out = model.forward_batch_greedy([seqs[j] for j in active], [toks[j] for j in active],
-                                         [offs[j] for j in active], n)
-        batch_sizes.extend([len(active)] * n)
-        for k, j in enumerate(active):
-            toks[j] = int(out[k, -1])
-            offs[j] += n
-            left[j] -= n
-            generated += n
-        active = [j for j in active if left[j] > 0]
-        steps += n
-    decode_s = time.perf_counter() - t1
-    totals = torch.tensor([decode_s, prefill_s], device="cuda", dtype=torch.float64)
-    counts = torch.tensor([generated, prefill_tokens], device="cuda", dtype=torch.float64)
-    if world > 1:
-        torch.distributed.all_reduce(totals, op=torch.distributed.ReduceOp.MAX)
-        torch.distributed.all_reduce(counts, op=torch.distributed.ReduceOp.SUM)
-    decode_s, prefill_s = float(totals[0]), float(totals[1])
-    generated, prefill_tokens = int(counts[0]), int(counts[1])
+    reqs, prompts, prefix, uses_prefix = serve_requests(cfg)
+    mine = serve_run(torch, R, model_dir, cfg, world, rank, local, hbm_peak, reqs, prompts, prefix, uses_prefix)
+    per_rank = _gather_dicts(torch, mine, world)
     if rank == 0:
-        line = {"metric": METRIC, "value": generated / decode_s, "unit": "tok/s", "n_gpus": world,
-                "steps": steps, "warmup": 0, "ms_per_step": 1e3 * decode_s / max(steps, 1),
+        summ = serve_summary(per_rank, world, hbm_peak)
+        launches = sum(r["steps"] for r in per_rank) * (BATCH_STEP_FIXED_LAUNCHES +
+                                                         BATCH_STEP_LAUNCHES_PER_LAYER * cfg["num_layers"])
+        line = {"metric": METRIC, "value": summ["value"], "unit": "tok/s", "n_gpus": world,
+                "steps": summ["steps"], "warmup": args.warmup, "ms_per_step": summ["ms_per_step"],
                 "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
                 "data": "synthetic (seeded random-init bf16 weights; seeded prompt/output lengths and ids)",
-                "config": {"workload": f"config 5: {name} batched serving, 64 sequences sharded over {world} GPU(s)",
-                           "model": name, "global_batch": n_seq, "parallelism": f"sequence-sharded x{world}"},
-                "decode": {"tokens": generated, "seconds": decode_s,
-                           "timing": "host wall clock around the batched decode loop (cheetah_cuda_forward_batch_greedy: "
-                                     "ids stay on the device between changes of the batch)",
-                           "mean_batch": float(np.mean(batch_sizes)) if batch_sizes else 0.0},
-                "prefill": {"tokens": prefill_tokens, "seconds": prefill_s, "tok_per_s": prefill_tokens / prefill_s}}
+                "config": workload_config(world) if world > 1 else serve_config(1),
+                "e2e": summ["e2e"], "gpu_launches": launches, "clocks": summ["clocks"],
+                "roofline": summ["roofline"] | {"peak_kind": peak_kind},
+                "serve": {k: v for k, v in summ.items() if k not in ("e2e", "roofline", "clocks")},
+                "warmup_note": "one chained step per rank captures the step graphs before the timed region"}
         print(json.dumps(line), flush=True)
-    del seqs
-    model.close()
     if world > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
     return 0
 
 
-def op_bench(args):
-    """Config 3 (chunked prefill) or config 2 (decode attention) alone, one GPU."""
+def run_ours(args):
+    """`--gpus 1`: config 1 is the value; configs 2-5 are sub-objects."""
     import torch
     from cheetah_b200 import runtime as R
     from cheetah_b200.prepared import PreparedModel, resolve_config
-    torch.cuda.set_device(dist_env()[2])
-    hbm_peak, _, peak_kind = peaks()
-    if args.workload == "attention":
-        rows = attention_microbench(torch, R, hbm_peak, quick=args.quick_attention)
-        best = max((r for r in rows if r["L"] == 32768), key=lambda r: r["GBps"])
-        line = {"metric": METRIC, "value": best["GBps"], "unit": "GB/s", "n_gpus": 1, "steps": 1,
-                "warmup": 3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-                "data": "synthetic (seeded N(0,1) Q/K/V, shuffled pages)",
-                "config": {"workload": "config 2: paged GQA decode attention microbench"},
-                "attention": rows, "peak_kind": peak_kind}
-    else:
-        model_dir = synthetic_model("qwen2-0.5b")
-        cfg = resolve_config(PreparedModel(model_dir))
-        pre = prefill_bench(torch, R, model_dir, cfg)
-        line = {"metric": METRIC, "value": pre["tok_per_s"], "unit": "tok/s", "n_gpus": 1, "steps": 1,
-                "warmup": 1, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-                "data": "synthetic (seeded random-init bf16 weights, uniform-random prompt ids)",
-                "config": {"workload": pre["workload"]}, "prefill": pre}
-    print(json.dumps(line), flush=True)
-    return 0
-
-
-def run_ours(args):
-    import torch
-    from cheetah_b200 import runtime as R
-    from cheetah_b200.prepared import PreparedModel, cached_synthetic, resolve_config
 
     world, rank, local = dist_env()
-    if world > 1:
-        import torch.distributed as dist
-        from datetime import timedelta
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120))
-    else:
-        torch.cuda.set_device(local)
-    hbm_peak, _, peak_kind = peaks()
+    torch.cuda.set_device(local)
+    hbm_peak, _, tensor_sustained, peak_kind = peaks()
 
     model_dir = synthetic_model("qwen2-0.5b")
     cfg = resolve_config(PreparedModel(model_dir))
     total_positions = PROMPT_LEN + args.warmup + args.steps + 8
     model = R.CudaModel(model_dir, device=local, max_positions=max(4096, total_positions + 64))
-    prompt = np.random.default_rng(1 + rank).integers(0, cfg["vocab_size"], PROMPT_LEN).astype(np.uint32)
+    prompt = np.random.default_rng(1).integers(0, cfg["vocab_size"], PROMPT_LEN).astype(np.uint32)
 
     # ---- value: device-resident greedy chain ----
     seq = model.new_sequence()
     first = int(np.argmax(seq.forward(prompt, 0)))
-    warm = seq.generate_greedy(first, PROMPT_LEN, max(args.warmup, 3))
+    warm = seq.generate_greedy(first, PROMPT_LEN, args.warmup)
     next_tok = int(warm[-1])
-    pos = PROMPT_LEN + max(args.warmup, 3)
+    pos = PROMPT_LEN + args.warmup
     stream = torch.cuda.ExternalStream(seq.stream_handle())
-    if world > 1:
-        torch.distributed.barrier()
     torch.cuda.synchronize()
     clocks = ClockSampler(local)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -543,11 +733,7 @@ def run_ours(args):
     torch.cuda.synchronize()
     clock_info = clocks.stop()
     elapsed = start.elapsed_time(end) / 1e3
-    if world > 1:
-        t = torch.tensor([elapsed], device="cuda", dtype=torch.float64)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        elapsed = float(t.item())
-    value = world * args.steps / elapsed
+    value = args.steps / elapsed
     ms_per_step = 1e3 * elapsed / args.steps
 
     # ---- e2e: public ModelForward call, host buffers, every step ----
@@ -556,21 +742,15 @@ def run_ours(args):
     logits = torch.empty(cfg["vocab_size"], dtype=torch.float32, pin_memory=True).numpy()
     tok = int(np.argmax(seq2.forward(prompt, 0, out=logits)))
     pos2 = PROMPT_LEN
-    for _ in range(max(args.warmup, 3)):
+    for _ in range(args.warmup):
         tok = seq2.forward_greedy([tok], pos2, logits_out=logits)
         pos2 += 1
-    if world > 1:
-        torch.distributed.barrier()
     t0 = time.perf_counter()
     for _ in range(args.steps):
         tok = seq2.forward_greedy([tok], pos2, logits_out=logits)
         pos2 += 1
     e2e_elapsed = time.perf_counter() - t0
-    if world > 1:
-        t = torch.tensor([e2e_elapsed], device="cuda", dtype=torch.float64)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        e2e_elapsed = float(t.item())
-    e2e = {"value": world * args.steps / e2e_elapsed, "unit": "tok/s",
+    e2e = {"value": args.steps / e2e_elapsed, "unit": "tok/s",
            "h2d_bytes_per_step": 4, "d2h_bytes_per_step": cfg["vocab_size"] * 4 + 4,
            "ms_per_step": 1e3 * e2e_elapsed / args.steps,
            "api": "cheetah_cuda_forward_ex (host token in, host logits in pinned memory + greedy id out)"}
@@ -585,6 +765,8 @@ def run_ours(args):
     step_bytes = weight_bytes + kv_bytes_per_pos * mean_ctx
     step_gbs = step_bytes / (elapsed / args.steps) / 1e9
     persistent = bool(info.get("persistent_decode", 0))
+    del seq
+    model.close()
 
     line = {
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
@@ -592,11 +774,7 @@ def run_ours(args):
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded random-init bf16 N(0,0.02) weights in the cheetah-init layout; "
                 "uniform-random prompt ids)",
-        "config": {"workload": "qwen2-0.5b decode B=1 (config 1: 512-token prompt, greedy decode)",
-                   "model": "Qwen2-0.5B architecture", "global_batch": world, "seq_len": PROMPT_LEN,
-                   "parallelism": f"sequence-sharded replicas x{world}" if world > 1 else "single GPU",
-                   "kv_cache": "paged bf16, 64-token pages", "l2": "inputs larger than L2 "
-                   f"(weights {weight_bytes / 1e6:.0f} MB per step > 126 MB L2)"},
+        "config": workload_config(1),
         "e2e": e2e,
         # The timed greedy run is one cooperative launch of the persistent
         # decode kernel (all steps); the multi-kernel path launches an
@@ -613,22 +791,192 @@ def run_ours(args):
                      "frac_8TBps": step_gbs / 8000.0, "peak_kind": peak_kind},
     }
 
-    if rank == 0:
-        line["lm_head_gemv"] = gemv_roofline(torch, R, hbm_peak)
-        # The op microbench and prefill figures are single-GPU measurements;
-        # a multi-rank run reports the scaled decode line only.
-        if not args.no_attention and world == 1:
-            line["attention"] = attention_microbench(torch, R, hbm_peak, quick=args.quick_attention)
-        if not args.no_prefill and world == 1:
-            line["prefill"] = prefill_bench(torch, R, model_dir, cfg)
-        if world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline(model_dir, cfg, args.cpu_steps)
-        print(json.dumps(line), flush=True)
-    del seq
-    model.close()
-    if world > 1:
-        torch.distributed.barrier()
-        torch.distributed.destroy_process_group()
+    line["lm_head_gemv"] = gemv_roofline(torch, R, hbm_peak)
+    if not args.no_attention:
+        rows = attention_microbench(torch, R, hbm_peak, quick=args.quick_attention)
+        best = max((r for r in rows if r["L"] == 32768), key=lambda r: r["GBps"])
+        line["attention"] = {"value": best["GBps"], "unit": "GB/s", "rows": rows,
+                             "roofline": {"bound": "hbm", "kernel": "decode_attention_mma_kernel (best row at 32k)",
+                                          "achieved": best["GBps"], "peak": hbm_peak, "unit": "GB/s",
+                                          "frac": best["GBps"] / hbm_peak, "traffic": None}}
+    if not args.no_prefill:
+        line["prefill"] = prefill_bench(torch, R, model_dir, cfg, tensor_sustained)
+    if not args.no_serve:
+        reqs, prompts, prefix, uses_prefix = serve_requests(cfg)
+        mine = serve_run(torch, R, model_dir, cfg, 1, 0, local, hbm_peak, reqs, prompts, prefix, uses_prefix)
+        line["serve"] = serve_summary([mine], 1, hbm_peak)
+        line["serve"]["gpu_launches"] = mine["steps"] * (BATCH_STEP_FIXED_LAUNCHES +
+                                                          BATCH_STEP_LAUNCHES_PER_LAYER * cfg["num_layers"])
+    if not args.no_7b:
+        dir7 = synthetic_model("qwen2-7b")
+        cfg7 = resolve_config(PreparedModel(dir7))
+        line["decode_7b"] = {}
+        for quant in args.quant_7b.split(","):
+            line["decode_7b"][quant] = decode_7b_run(torch, R, dir7, cfg7, quant, args.steps_7b, args.warmup,
+                                                     hbm_peak)
+    # CPU baselines last: the GPU work is done.
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_decode_05b(model_dir, cfg, args.cpu_steps)
+        if "attention" in line:
+            line["attention"]["cpu_baseline"] = cpu_attention(line["attention"]["rows"])
+        if "prefill" in line:
+            line["prefill"]["cpu_baseline"] = cpu_prefill(model_dir, cfg)
+        if "serve" in line:
+            line["serve"]["cpu_baseline"] = cpu_serve(model_dir, cfg, serve_requests(cfg)[0])
+        if "decode_7b" in line:
+            for quant, row in line["decode_7b"].items():
+                row["cpu_baseline"] = cpu_decode_7b(dir7, cfg7, quant)
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# DRAM bytes (read + write) of one decode step of the persistent kernel,
+# Qwen2-0.5B, context ~600: ncu dram__bytes_read.sum + dram__bytes_write.sum
+# of a one-step launch (summary and command in profiles/).
+DECODE_STEP_DRAM_BYTES = 998049536
+
+
+def run_reference(args):
+    """The reference arm: the reference's CPU path (C++ restatement of the
+    AVX2 backend, oracle/) on all host threads, on the same config as ours
+    for this number of GPUs. Under torchrun only rank 0 runs and prints."""
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return 0
+    from cheetah_b200.prepared import PreparedModel, resolve_config
+    model_dir = synthetic_model("qwen2-0.5b")
+    cfg = resolve_config(PreparedModel(model_dir))
+    O = _oracle()
+    if world == 1:
+        ref = O.OracleModel(PreparedModel(model_dir), cfg, "bf16")
+        prompt = np.random.default_rng(1).integers(0, cfg["vocab_size"], PROMPT_LEN).astype(np.uint32)
+        tok = int(np.argmax(ref.forward(prompt, 0)))
+        pos = PROMPT_LEN
+        per_step = []
+        for i in range(args.warmup + args.steps):
+            t0 = time.perf_counter()
+            tok = int(np.argmax(ref.forward([tok], pos)))
+            pos += 1
+            if i >= args.warmup:
+                per_step.append(time.perf_counter() - t0)
+        total = sum(per_step)
+        value = len(per_step) / total
+        sample = (f"{args.steps} greedy decode steps after a {PROMPT_LEN}-token prompt; the reference is Rust (no "
+                  "toolchain here), so its AVX2 path runs as the C++ restatement in oracle/")
+        ms = 1e3 * total / len(per_step)
+        scaling = "weak"
+    else:
+        cpu = cpu_serve(model_dir, cfg, serve_requests(cfg)[0])
+        value = cpu["value"]
+        sample = cpu["sample"] + "; the reference serves on one host, whatever the GPU count"
+        ms = 1e3 / value
+        scaling = "strong"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded random-init bf16 weights, uniform-random prompt ids)",
+        "config": workload_config(world),
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": O.threads(), "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# Single-kernel cases for ncu captures (small, seeded, end by themselves).
+
+def case_gemv(fmt: str, rows: int, cols: int) -> int:
+    """Device quantisation of a [rows, cols] bf16 matrix, then three quantised
+    GEMVs through the C-ABI op entry."""
+    import torch
+    from cheetah_b200 import runtime as R
+    g = torch.Generator(device="cuda").manual_seed(0)
+    w = (torch.randn(rows, cols, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    buf = R.quantize(w, fmt)
+    x = torch.randn(cols, device="cuda", generator=g)
+    for _ in range(3):
+        y = R.gemv_quant(buf, fmt, rows, cols, x)
+    torch.cuda.synchronize()
+    print(f"{fmt} gemv {rows}x{cols}: sum|y| = {float(y.abs().sum()):.6f}")
+    return 0
+
+
+def case_batch_decode(batch: int, context: int, steps: int) -> int:
+    """Qwen2-0.5B: `batch` sequences prefilled with `context` tokens each (one
+    chunk per prompt), then `steps` host-synchronous batched decode steps."""
+    os.environ.setdefault("CHEETAH_PREFILL_CHUNK", str(context))
+    from cheetah_b200 import runtime as R
+    from cheetah_b200.prepared import PreparedModel, resolve_config
+    root = synthetic_model("qwen2-0.5b")
+    cfg = resolve_config(PreparedModel(root))
+    model = R.CudaModel(root, max_positions=context + steps + 8,
+                        kv_pool_tokens=batch * (context + steps + 128))
+    rng = np.random.default_rng(3)
+    seqs, toks = [], []
+    for _ in range(batch):
+        seq = model.new_sequence()
+        prompt = rng.integers(0, cfg["vocab_size"], context).astype(np.uint32)
+        toks.append(int(np.argmax(seq.forward(prompt, 0))))
+        seqs.append(seq)
+    pos = context
+    for i in range(steps + 2):
+        if i == 2:
+            t0 = time.perf_counter()
+        toks = model.forward_batch(seqs, toks, [pos] * batch).tolist()
+        pos += 1
+    ms = (time.perf_counter() - t0) * 1e3 / steps
+    print(f"batch-decode B={batch} L={context}: {ms:.4f} ms/step (host-synchronous calls)")
+    return 0
+
+
+def run_decode_7b(args):
+    """`--workload decode-7b-<quant>`: config 4 alone, one line."""
+    import torch
+    from cheetah_b200 import runtime as R
+    from cheetah_b200.prepared import PreparedModel, resolve_config
+    torch.cuda.set_device(dist_env()[2])
+    hbm_peak, _, _, peak_kind = peaks()
+    quant = args.workload.split("-")[-1]
+    dir7 = synthetic_model("qwen2-7b")
+    cfg7 = resolve_config(PreparedModel(dir7))
+    row = decode_7b_run(torch, R, dir7, cfg7, quant, args.steps, args.warmup, hbm_peak, args.prompt_7b)
+    line = {"metric": METRIC, "value": row["value"], "unit": "tok/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": row["ms_per_step"], "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": quant,
+            "data": "synthetic (seeded random-init bf16 weights quantised per row at load)",
+            "config": {"workload": f"qwen2-7b decode B=1 {quant} (config 4: {args.prompt_7b}-token prompt)",
+                       "model": "Qwen2-7B architecture", "global_batch": 1, "seq_len": args.prompt_7b},
+            "clocks": row["clocks"], "roofline": row["roofline"] | {"peak_kind": peak_kind}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_op(args):
+    """`--workload prefill-0.5b | attention`: config 3 or config 2 alone."""
+    import torch
+    from cheetah_b200 import runtime as R
+    from cheetah_b200.prepared import PreparedModel, resolve_config
+    torch.cuda.set_device(dist_env()[2])
+    hbm_peak, _, tensor_sustained, peak_kind = peaks()
+    if args.workload == "attention":
+        rows = attention_microbench(torch, R, hbm_peak, quick=args.quick_attention)
+        best = max((r for r in rows if r["L"] == 32768), key=lambda r: r["GBps"])
+        line = {"metric": METRIC, "value": best["GBps"], "unit": "GB/s", "n_gpus": 1, "steps": 1,
+                "warmup": 3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic (seeded N(0,1) Q/K/V, shuffled pages)",
+                "config": {"workload": "config 2: paged GQA decode attention microbench"},
+                "attention": rows, "peak_kind": peak_kind}
+    else:
+        model_dir = synthetic_model("qwen2-0.5b")
+        cfg = resolve_config(PreparedModel(model_dir))
+        pre = prefill_bench(torch, R, model_dir, cfg, tensor_sustained)
+        line = {"metric": METRIC, "value": pre["tok_per_s"], "unit": "tok/s", "n_gpus": 1, "steps": 1,
+                "warmup": 1, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic (seeded random-init bf16 weights, uniform-random prompt ids)",
+                "config": {"workload": pre["workload"]}, "prefill": pre}
+    print(json.dumps(line), flush=True)
     return 0
 
 
@@ -643,20 +991,34 @@ def main():
     ap.add_argument("--no-attention", action="store_true")
     ap.add_argument("--quick-attention", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
-    ap.add_argument("--workload", default="decode-0.5b",
-                    choices=["decode-0.5b", "decode-7b-q8", "decode-7b-q4", "decode-7b-bf16",
-                             "serve-0.5b", "serve-7b", "prefill-0.5b", "attention"])
+    ap.add_argument("--no-serve", action="store_true")
+    ap.add_argument("--no-7b", action="store_true")
+    ap.add_argument("--quant-7b", default="q8,q4,bf16")
+    ap.add_argument("--steps-7b", type=int, default=64)
+    ap.add_argument("--prompt-7b", type=int, default=1024, help="decode-7b-* workloads: prompt tokens")
+    ap.add_argument("--workload", default="default",
+                    choices=["default", "decode-7b-q8", "decode-7b-q4", "decode-7b-bf16", "serve-0.5b",
+                             "prefill-0.5b", "attention", "gemv-q8", "gemv-q4", "batch-decode"])
+    ap.add_argument("--rows", type=int, default=18944, help="gemv-q8/q4 case")
+    ap.add_argument("--cols", type=int, default=3584, help="gemv-q8/q4 case")
+    ap.add_argument("--batch", type=int, default=32, help="batch-decode case")
+    ap.add_argument("--context", type=int, default=4096, help="batch-decode case")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    world, _, _ = dist_env()
     if args.impl == "reference":
         return run_reference(args)
     if args.workload.startswith("decode-7b"):
-        return decode_7b(args)
-    if args.workload.startswith("serve"):
-        return serve_bench(args)
+        return run_decode_7b(args)
     if args.workload in ("prefill-0.5b", "attention"):
-        return op_bench(args)
+        return run_op(args)
+    if args.workload in ("gemv-q8", "gemv-q4"):
+        return case_gemv(args.workload.split("-")[1], args.rows, args.cols)
+    if args.workload == "batch-decode":
+        return case_batch_decode(args.batch, args.context, args.steps)
+    if world > 1 or args.workload == "serve-0.5b":
+        return run_serve(args)
     return run_ours(args)
 
 

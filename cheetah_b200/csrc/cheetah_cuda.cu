@@ -440,7 +440,7 @@ struct Model {
     int *b_error = nullptr;
     // Chained greedy steps: [0] live rows, [1] step index within the chunk;
     // token log [kChainSteps][cap] and its pinned host copy.
-    int32_t *b_chain = nullptr, *h_chain = nullptr;
+    int32_t *b_chain = nullptr, *h_chain = nullptr;  // h_chain: [0..1] chain state, [2] error word read-back
     int32_t *b_log = nullptr, *h_log = nullptr;
     CUtensorMap map_bxb{}, map_bab{}, map_bact{};
     std::map<uint64_t, cudaGraphExec_t> batch_graphs;  // (rows, table stride, logits, chained) -> captured step
@@ -1775,7 +1775,7 @@ int ensure_batch_workspace(Model &m, int cap, int table_cap) {
               cudaMalloc(&m.b_tickets, R * c.kv_heads * 4) == cudaSuccess && cudaMalloc(&m.b_error, 4) == cudaSuccess &&
               cudaMalloc(&m.b_split_ws, (size_t)m.sms * kGemmBM * 128 * 4) == cudaSuccess &&
               cudaMalloc(&m.b_split_tickets, (size_t)m.sms * 4) == cudaSuccess &&
-              cudaMalloc(&m.b_chain, 2 * 4) == cudaSuccess && cudaMallocHost(&m.h_chain, 2 * 4) == cudaSuccess &&
+              cudaMalloc(&m.b_chain, 2 * 4) == cudaSuccess && cudaMallocHost(&m.h_chain, 4 * 4) == cudaSuccess &&
               cudaMalloc(&m.b_log, (size_t)kChainSteps * R * 4) == cudaSuccess &&
               cudaMallocHost(&m.h_log, (size_t)kChainSteps * R * 4) == cudaSuccess;
     if (!ok) {
@@ -2098,7 +2098,14 @@ int forward_batch_greedy(Model *mp, Seq *const *seqs, const uint32_t *tokens, co
             }
         }
         CH_CUDA_TRY(cudaMemcpyAsync(m.h_log, m.b_log, n * (size_t)cap * 4, cudaMemcpyDeviceToHost, st));
+        // The error word travels with the chunk's token log: a chunk that
+        // tripped a device guard is reported before any of its ids are used.
+        CH_CUDA_TRY(cudaMemcpyAsync(&m.h_chain[2], m.b_error, 4, cudaMemcpyDeviceToHost, st));
         CH_CUDA_TRY(cudaStreamSynchronize(st));
+        if (m.h_chain[2] != 0) {
+            check_batch_error(m);  // sets the message, resets the word and the tickets
+            return -1;
+        }
         for (size_t i = 0; i < n; ++i)
             for (size_t b = 0; b < B; ++b) tokens_out[b * steps + done + i] = (uint32_t)m.h_log[i * cap + b];
         done += n;
@@ -2310,6 +2317,12 @@ int cheetah_cuda_generate_greedy(CheetahCudaSeq *seq, uint32_t first_token, size
 int cheetah_cuda_seq_stream(const CheetahCudaSeq *seq, void **stream) {
     CH_REQUIRE(seq != nullptr && stream != nullptr, "cheetah_cuda_seq_stream: null argument");
     *stream = reinterpret_cast<const Seq *>(seq)->stream;
+    return 0;
+}
+
+int cheetah_cuda_model_batch_stream(const CheetahCudaModel *model, void **stream) {
+    CH_REQUIRE(model != nullptr && stream != nullptr, "cheetah_cuda_model_batch_stream: null argument");
+    *stream = reinterpret_cast<const Model *>(model)->batch_stream;
     return 0;
 }
 

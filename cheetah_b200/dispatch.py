@@ -23,9 +23,12 @@ what happens when a rank fails:
                 (torch.distributed TCPStore): `done/<rank>` with its results,
                 or `fail/<rank>` when its work raised. A rank that has neither
                 reported nor failed by the deadline counts as failed too (it
-                never joined, or died). Survivors requeue the failed ranks'
-                sequences, serve their share, publish `requeued/<rank>`, and
-                every survivor returns the merged results of all sequences.
+                never joined, died, or is too slow). The deadline runs from
+                one start time shared by all ranks, and the first rank to
+                decide writes the failed set once (compare_set): every rank
+                uses that set. Survivors requeue the failed ranks' sequences,
+                serve their share, publish `requeued/<rank>`, and every rank
+                still running returns the merged results of all sequences.
                 Failure is learned on the host between steps: no device wait
                 depends on another rank.
 """
@@ -144,9 +147,20 @@ def run_with_failover(store, rank: int, world: int, requests: Sequence[SeqReques
                       ) -> Tuple[Dict[int, object], List[int]]:
     """Serve this rank's shard of `plan_shards(requests, world)` with
     `process(seq_id)` (JSON-serialisable results) and return (results of all
-    sequences, failed ranks) on a surviving rank. If this rank's own work
-    raises, `fail/<rank>` is published and the exception propagates."""
+    sequences, failed ranks). If this rank's own work raises, `fail/<rank>`
+    is published and the exception propagates.
+
+    Every rank measures the deadline from one common start: the wall-clock
+    time of the first rank to enter (`t0`, written once with compare_set).
+    Every rank agrees on one failed set: the first rank to decide (all ranks
+    reported, or the deadline passed) writes `failed` with compare_set and
+    every rank reads that value back, so survivors never requeue different
+    sets. A rank that was slow but alive and finds itself in the agreed set
+    discards its own results (the survivors serve its sequences again) and
+    returns the survivors' merged results."""
     plan = plan_shards(requests, world, kv_budget)
+    t0 = float(store.compare_set("t0", "", repr(time.time())).decode())
+    deadline = t0 + deadline_s
     results: Dict[int, object] = {}
     try:
         for sid in plan[rank]:
@@ -156,9 +170,12 @@ def run_with_failover(store, rank: int, world: int, requests: Sequence[SeqReques
         raise
     store.set(f"done/{rank}", json.dumps({str(k): v for k, v in results.items()}))
 
-    deadline = time.monotonic() + deadline_s
+    agreed = None
     status: Dict[int, str] = {}
-    while True:
+    while agreed is None:
+        if store.check(["failed"]):
+            agreed = store.get("failed").decode()
+            break
         for r in range(world):
             if r in status:
                 continue
@@ -166,10 +183,12 @@ def run_with_failover(store, rank: int, world: int, requests: Sequence[SeqReques
                 status[r] = "done"
             elif store.check([f"fail/{r}"]):
                 status[r] = "fail"
-        if len(status) == world or time.monotonic() > deadline:
+        if len(status) == world or time.time() > deadline:
+            mine = sorted(r for r in range(world) if status.get(r) != "done")
+            agreed = store.compare_set("failed", "", json.dumps(mine)).decode()
             break
         time.sleep(poll_s)
-    failed = sorted(r for r in range(world) if status.get(r) != "done")
+    failed = sorted(int(r) for r in json.loads(agreed))
     survivors = [r for r in range(world) if r not in failed]
 
     merged: Dict[int, object] = {}
@@ -177,12 +196,13 @@ def run_with_failover(store, rank: int, world: int, requests: Sequence[SeqReques
         merged.update({int(k): v for k, v in json.loads(store.get(f"done/{r}")).items()})
     if failed:
         plan2 = requeue(plan, requests, failed, kv_budget)
-        extra = {sid: process(sid) for sid in plan2[rank] if sid not in plan[rank]}
-        store.set(f"requeued/{rank}", json.dumps({str(k): v for k, v in extra.items()}))
+        if rank in survivors:
+            extra = {sid: process(sid) for sid in plan2[rank] if sid not in plan[rank]}
+            store.set(f"requeued/{rank}", json.dumps({str(k): v for k, v in extra.items()}))
         for r in survivors:
             key = f"requeued/{r}"
             while not store.check([key]):
-                if time.monotonic() > deadline + deadline_s:
+                if time.time() > deadline + deadline_s:
                     raise TimeoutError(f"rank {r} did not publish its requeued results")
                 time.sleep(poll_s)
             merged.update({int(k): v for k, v in json.loads(store.get(key)).items()})

@@ -17,9 +17,9 @@ Layout (written by the reference's `cheetah_init.c:1331-1452` and read by
 * ``<dir>/config.json`` copied from the source checkpoint.
 
 This module also generates the seeded synthetic Qwen2 checkpoints the
-benchmarks and parity tests run on (random-init bf16 N(0, 0.02), seed 0,
-tensors drawn in name order), either directly in the prepared layout or in
-the Hugging Face single-file layout that `cheetah init` converts.
+benchmarks and parity tests run on (random-init bf16 N(0, 0.02) from seed 0,
+one child seed per tensor chunk), either directly in the prepared layout or
+in the Hugging Face single-file layout that `cheetah init` converts.
 """
 
 from __future__ import annotations
@@ -144,18 +144,36 @@ def bf16_bits_to_f32(bits: np.ndarray) -> np.ndarray:
 
 
 def generate_tensors(shape: Qwen2Shape, seed: int = 0, std: float = 0.02,
-                     chunk: int = 1 << 24) -> Iterator[Tuple[str, Tuple[int, ...], np.ndarray]]:
+                     chunk: int = 1 << 24, threads: Optional[int] = None
+                     ) -> Iterator[Tuple[str, Tuple[int, ...], np.ndarray]]:
     """Seeded random-init weights: N(0, std) bf16 for every tensor (norms and
-    biases included), drawn in sorted-name order from one generator."""
-    rng = np.random.default_rng(seed)
-    for name, dims in tensor_specs(shape):
-        count = int(np.prod(dims))
-        out = np.empty(count, dtype=np.uint16)
-        for start in range(0, count, chunk):
-            n = min(chunk, count - start)
-            draw = rng.standard_normal(n, dtype=np.float32)
-            draw *= np.float32(std)
-            out[start:start + n] = f32_to_bf16_bits(draw)
+    biases included), yielded in sorted-name order. Tensor i's chunk j of
+    `chunk` values is drawn from its own generator, seeded by child (i, j) of
+    `SeedSequence(seed)`, so the values do not depend on how many threads
+    draw them; the chunks are drawn on a thread pool (numpy releases the GIL
+    while it fills large arrays)."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    specs = tensor_specs(shape)
+    root = np.random.SeedSequence(seed)
+    per_tensor = root.spawn(len(specs))
+    outs = [np.empty(int(np.prod(dims)), dtype=np.uint16) for _, dims in specs]
+    jobs = []
+    for i, (_, dims) in enumerate(specs):
+        count = outs[i].size
+        seeds = per_tensor[i].spawn(max(1, -(-count // chunk)))
+        for j, start in enumerate(range(0, count, chunk)):
+            jobs.append((i, start, min(chunk, count - start), seeds[j]))
+
+    def draw(job):
+        i, start, n, ss = job
+        values = np.random.default_rng(ss).standard_normal(n, dtype=np.float32)
+        values *= np.float32(std)
+        outs[i][start:start + n] = f32_to_bf16_bits(values)
+
+    with ThreadPoolExecutor(max_workers=threads or min(32, os.cpu_count() or 1)) as pool:
+        list(pool.map(draw, jobs))
+    for (name, dims), out in zip(specs, outs):
         yield name, dims, out
 
 

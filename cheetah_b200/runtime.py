@@ -84,6 +84,7 @@ SIGNATURES = {
     "cheetah_cuda_forward_batch_greedy": (_I, [_P, _P, _P, _P, _S, _S, _P]),
     "cheetah_cuda_generate_greedy": (_I, [_P, C.c_uint32, _S, _S, _P]),
     "cheetah_cuda_seq_stream": (_I, [_P, C.POINTER(_P)]),
+    "cheetah_cuda_model_batch_stream": (_I, [_P, C.POINTER(_P)]),
     "cheetah_cuda_seq_snapshot": (_I, [_P, C.POINTER(_P)]),
     "cheetah_cuda_snapshot_positions": (_I, [_P, C.POINTER(_S)]),
     "cheetah_cuda_seq_restore_prefix": (_I, [_P, _P, _S]),
@@ -192,6 +193,12 @@ class CudaModel:
         _check(lib().cheetah_cuda_forward_batch(self._h, handles, _ptr(t), _ptr(o), B,
                                                 _ptr(logits) if want_logits else None, _ptr(am)))
         return (am, logits) if want_logits else am
+
+    def batch_stream_handle(self) -> int:
+        """The stream batched calls run on (0 before the first batched call)."""
+        s = C.c_void_p()
+        _check(lib().cheetah_cuda_model_batch_stream(self._h, C.byref(s)))
+        return s.value or 0
 
     def forward_batch_greedy(self, seqs, tokens, offsets, steps: int) -> np.ndarray:
         """`steps` greedy tokens for each sequence with no host round trip

@@ -151,6 +151,11 @@ CHEETAH_CUDA_API int cheetah_cuda_generate_greedy(CheetahCudaSeq *seq, uint32_t 
                                                   size_t steps, uint32_t *tokens_out);
 /* The sequence's CUDA stream (cudaStream_t) for event timing / synchronisation. */
 CHEETAH_CUDA_API int cheetah_cuda_seq_stream(const CheetahCudaSeq *seq, void **stream);
+/* The model's batch stream (cudaStream_t), on which cheetah_cuda_forward_batch
+ * and cheetah_cuda_forward_batch_greedy run, for event timing. Created by the
+ * first batched call; *stream is NULL before it. A harness accessor: the
+ * reference times `forward` on the host (no counterpart in `registry.rs`). */
+CHEETAH_CUDA_API int cheetah_cuda_model_batch_stream(const CheetahCudaModel *model, void **stream);
 
 /* `ModelForward::kv_snapshot` / `restore_kv_prefix` (`registry.rs:68-79`,
  * `ops.rs:1575-1607`): a device-resident copy of the sequence's KV pages. */

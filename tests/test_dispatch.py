@@ -1,8 +1,9 @@
 """Sequence dispatch over ranks: placement by KV-token load, prefix-group
 co-location, requeue after a rank failure, and the store-based failover run
 as world-size-2 CPU processes (gloo process group, TCPStore on 127.0.0.1).
-Failures are made on the host: a rank whose work raises, and a rank that exits
-without reporting. No GPU is involved."""
+Failures are made on the host: a rank whose work raises, a rank that exits
+without reporting, and a rank that is alive but finishes after the deadline.
+No GPU is involved."""
 
 from __future__ import annotations
 
@@ -10,6 +11,7 @@ import json
 import multiprocessing as mp
 import os
 import socket
+import time
 from datetime import timedelta
 
 import numpy as np
@@ -140,6 +142,8 @@ def _rank_main(rank: int, world: int, port: int, mode: str, deadline_s: float) -
         calls.append(sid)
         if mode == "raise" and rank == 1 and len(calls) == 2:
             raise RuntimeError("injected failure on the host")
+        if mode == "slow" and rank == world - 1 and len(calls) == 1:
+            time.sleep(deadline_s + 2.0)  # alive, but past every other rank's deadline
         return work(sid)
 
     merged, failed = run_with_failover(store, rank, world, small_requests(), process,
@@ -160,13 +164,13 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def run_world2(mode: str, deadline_s: float = 20.0):
+def run_world(mode: str, world: int = 2, deadline_s: float = 20.0):
     import torch.distributed as dist
     port = _free_port()
-    store = dist.TCPStore("127.0.0.1", port, 3, is_master=True, timeout=timedelta(seconds=60),
+    store = dist.TCPStore("127.0.0.1", port, world + 1, is_master=True, timeout=timedelta(seconds=60),
                           wait_for_workers=False)
     ctx = mp.get_context("spawn")
-    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, mode, deadline_s)) for r in range(2)]
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, mode, deadline_s)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
@@ -177,10 +181,14 @@ def run_world2(mode: str, deadline_s: float = 20.0):
             p.join()
     codes = [p.exitcode for p in procs]
     out = {}
-    for r in range(2):
+    for r in range(world):
         if store.check([f"result/{r}"]):
             out[r] = json.loads(store.get(f"result/{r}"))
     return store, codes, out
+
+
+def run_world2(mode: str, deadline_s: float = 20.0):
+    return run_world(mode, 2, deadline_s)
 
 
 def test_world2_all_ranks_succeed():
@@ -225,3 +233,24 @@ def test_requeue_respects_the_kv_budget():
     plan2 = requeue(plan, reqs, [1], kv_budget=3000)
     check_partition(plan2, reqs)
     assert rank_load(plan2, reqs) == [3000, 0, 3000]
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_slow_rank_past_the_deadline_every_rank_agrees(world):
+    """The last rank sleeps past the common deadline and still finishes: every
+    rank (the slow one included) uses the one agreed failed set, the slow
+    rank's sequences are served again by the survivors, and nobody times
+    out waiting for a requeue that was never published."""
+    store, codes, out = run_world("slow", world, deadline_s=3.0)
+    assert codes == [0] * world
+    slow = world - 1
+    expect = {str(i): work(i) for i in range(N_SEQ)}
+    assert json.loads(store.get("failed")) == [slow]
+    plan = plan_shards(small_requests(), world)
+    plan2 = requeue(plan, small_requests(), [slow])
+    for r in range(world):
+        assert out[r]["failed"] == [slow]
+        assert out[r]["merged"] == expect
+    for r in range(slow):
+        assert out[r]["calls"] == plan[r] + [s for s in plan2[r] if s not in plan[r]]
+    assert out[slow]["calls"] == plan[slow]
