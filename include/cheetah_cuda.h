@@ -225,9 +225,9 @@ typedef struct CheetahCudaDecodeAttention {
 CHEETAH_CUDA_API int cheetah_cuda_op_decode_attention(const CheetahCudaDecodeAttention *args, void *stream);
 
 /* Decode attention for callers that cannot let the library allocate device
- * memory — e.g. code recording into a CUDA graph (no allocation while a stream
- * is being captured), a host that runs a fixed device-memory budget, or a
- * latency-critical path that cannot absorb cudaMalloc's synchronisation.
+ * memory — e.g. a host that runs a fixed device-memory budget of its own and
+ * hands the library only inputs and outputs, or a latency-critical path that
+ * cannot absorb the device-wide synchronisation of cudaMalloc / cudaFree.
  * Same arguments and result as cheetah_cuda_op_decode_attention; the
  * split-merge scratch is a fixed ~4.1 MiB array compiled into the library,
  * held by every GPU that loads it until the process exits. Limits:
