@@ -418,7 +418,7 @@ struct Model {
     // attention key chunks per head, dynamic shared memory, layer table.
     bool mk_enabled = false;
     int mk_slots = 0;
-    int mk_att_splits = 1;
+    int mk_group_units = 1;  // attention units of a query head (CTAs per head, rounded up)
     size_t mk_smem = 0;
     size_t mk_copy_bytes = 0;  // arena bytes of the decode-kernel weight copies
     MkLayer *mk_layers = nullptr;
@@ -559,7 +559,7 @@ struct Seq {
     cudaGraphExec_t graph = nullptr;
     cudaGraphExec_t chain_graph = nullptr;
     // Persistent decode kernel scratch (allocated on first use).
-    float *mk_opart = nullptr, *mk_att_part = nullptr, *mk_hnew = nullptr;
+    float *mk_opart = nullptr, *mk_att_part = nullptr;
     unsigned *mk_ctrl = nullptr;
     unsigned long long *mk_argmax = nullptr;
 
@@ -581,7 +581,6 @@ struct Seq {
         cudaFree(psplit_tickets);
         cudaFree(mk_opart);
         cudaFree(mk_att_part);
-        cudaFree(mk_hnew);
         cudaFree(mk_ctrl);
         cudaFree(mk_argmax);
         if (stream) cudaStreamDestroy(stream);
@@ -621,7 +620,7 @@ namespace {
 // Enqueue one decode step (B = 1) on the sequence stream.
 // The persistent decode kernel instance for a model shape: head dim, and
 // per-thread hidden-width slices in registers when hidden <= 1024.
-using MkKernel = void (*)(MkParams);
+using MkKernel = void (*)(const CUtensorMap, const CUtensorMap, const MkParams);
 MkKernel mk_kernel_for(const CheetahCudaConfig &c) {
     const bool small = c.hidden_size <= 1024;
     if (c.head_dim == 64) return small ? decode_megakernel<64, true> : decode_megakernel<64, false>;
@@ -632,10 +631,9 @@ int ensure_mk_buffers(Seq &s) {
     if (s.mk_ctrl != nullptr) return 0;
     const Model &m = *s.m;
     const CheetahCudaConfig &c = m.cfg;
-    const size_t parts = (size_t)c.q_heads * m.mk_att_splits * (2 + c.head_dim);
+    const size_t parts = (size_t)c.q_heads * m.mk_group_units * (2 + c.head_dim);
     bool ok = cudaMalloc(&s.mk_opart, (size_t)c.q_heads * c.hidden_size * 4) == cudaSuccess &&
               cudaMalloc(&s.mk_att_part, parts * 4) == cudaSuccess &&
-              cudaMalloc(&s.mk_hnew, (size_t)c.hidden_size * 4) == cudaSuccess &&
               cudaMalloc(&s.mk_ctrl, kMkCtrlWords * 4) == cudaSuccess &&
               cudaMalloc(&s.mk_argmax, 2 * 8) == cudaSuccess;
     if (!ok) {
@@ -667,9 +665,8 @@ int launch_megakernel(Seq &s, int steps, float *logits, int32_t *token_log) {
     p.hd = (int)c.head_dim;
     p.vocab = (int)c.vocab_size;
     p.window = (int)c.sliding_window;
-    p.att_splits = m.mk_att_splits;
     p.slots = m.mk_slots;
-    p.xcap = (int)std::max(c.hidden_size, c.intermediate_size);
+    p.xcap = mk_xcap((int)c.hidden_size, (int)c.intermediate_size, (int)c.head_dim);
     p.inflight_layers = std::min(m.mk_slots, env_int("CHEETAH_MK_INFLIGHT", 1));
     p.inflight_lm = std::min(m.mk_slots, env_int("CHEETAH_MK_INFLIGHT_LM", 3));
     p.eps = c.rms_eps;
@@ -682,6 +679,7 @@ int launch_megakernel(Seq &s, int steps, float *logits, int32_t *token_log) {
     p.k_pool = m.k_pool;
     p.v_pool = m.v_pool;
     p.layer_stride_bytes = m.layer_stride_bytes;
+    p.layer_rows = (long long)m.num_pages * c.kv_heads * m.page_tokens;
     p.num_pages = m.num_pages;
     p.page_tokens = m.page_tokens;
     p.max_pages = s.max_pages;
@@ -691,7 +689,7 @@ int launch_megakernel(Seq &s, int steps, float *logits, int32_t *token_log) {
     p.hidden = s.hidden;
     p.q = s.q;
     p.opart = s.mk_opart;
-    p.hnew = s.mk_hnew;
+    p.att_part_units = m.mk_group_units;
     p.act = s.act;
     p.att_part = s.mk_att_part;
     p.ctrl = s.mk_ctrl;
@@ -700,6 +698,11 @@ int launch_megakernel(Seq &s, int steps, float *logits, int32_t *token_log) {
     p.token_log = token_log;
     p.logits = logits;
     p.error = s.d_error;
+    // Every wait is bounded (2 s). CHEETAH_CUDA_TEST_STALL_WAIT=1 is a test
+    // hook: the run's first attention wait targets a count nothing reaches,
+    // with a 20 ms bound, to exercise the timeout path.
+    p.stall_test = env_flag("CHEETAH_CUDA_TEST_STALL_WAIT", false) ? 1 : 0;
+    p.timeout_ns = p.stall_test ? 20000000ull : 2000000000ull;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(m.sms);
     cfg.blockDim = dim3(kMkThreads);
@@ -710,7 +713,7 @@ int launch_megakernel(Seq &s, int steps, float *logits, int32_t *token_log) {
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    CH_CUDA_TRY(cudaLaunchKernelEx(&cfg, mk_kernel_for(c), p));
+    CH_CUDA_TRY(cudaLaunchKernelEx(&cfg, mk_kernel_for(c), m.k_map, m.v_map, p));
     return 0;
 }
 
@@ -1051,17 +1054,21 @@ int open_model(const char *prepared_dir, const CheetahCudaConfig *config, const 
         int coop = 0, optin = 0;
         cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, device);
         cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
-        const int xcap = (int)std::max(H, I);
+        const int xcap = mk_xcap((int)H, (int)I, (int)c.head_dim);
         const size_t fixed = mk_smem_bytes(0, xcap, (int)H, (int)c.head_dim);
         const size_t budget = optin > 4096 ? (size_t)optin - 4096 : 0;  // static shared state
         const int slots = budget > fixed ? (int)std::min<size_t>(kMkMaxSlots, (budget - fixed) / kMkSlotBytes) : 0;
+        // The K/V tiles arrive by 128-byte-swizzled tensor-map loads (the bf16
+        // cache's maps): pages a whole number of tiles; every query head
+        // gets at least one attention unit.
         m->mk_enabled = env_flag("CHEETAH_CUDA_MEGAKERNEL", true) && coop != 0 && wfmt == kWBf16 && !m->kv_f32 &&
                         4 * H <= (size_t)kMkSlotBytes && 2 * I <= (size_t)kMkSlotBytes &&
-                        c.q_heads <= (uint32_t)kMkMaxHeads && slots >= 3;
+                        c.q_heads <= (uint32_t)kMkMaxHeads && c.q_heads <= (uint32_t)m->sms &&
+                        mma_attention_eligible((int)c.head_dim, m->page_tokens) && slots >= 3;
         if (m->mk_enabled) {
             m->mk_slots = slots;
             m->mk_smem = mk_smem_bytes(slots, xcap, (int)H, (int)c.head_dim);
-            m->mk_att_splits = std::max(1, m->sms / (int)c.q_heads);
+            m->mk_group_units = (m->sms + (int)c.q_heads - 1) / (int)c.q_heads;
         }
     }
     size_t per_layer = linear_bytes(QD + 2 * KD, H) + linear_bytes(H, QD) + 2 * linear_bytes(I, H) +
@@ -1454,7 +1461,12 @@ int forward(Seq *s, const uint32_t *tokens, size_t n, size_t offset, float *logi
     }
     CH_CUDA_TRY(cudaMemcpyAsync(s->h_error, s->d_error, 4, cudaMemcpyDeviceToHost, s->stream));
     CH_CUDA_TRY(cudaStreamSynchronize(s->stream));
-    if (*s->h_error != 0 && check_device_error(*s) != 0) return -1;
+    if (*s->h_error != 0 && check_device_error(*s) != 0) {
+        // The call's K/V rows are not trusted: the sequence keeps the
+        // positions it had, so the same call can be repeated.
+        s->positions = offset;
+        return -1;
+    }
     if (logits_out && !direct) memcpy(logits_out, s->h_logits, (size_t)c.vocab_size * 4);
     if (argmax_out) *argmax_out = (uint32_t)(*s->h_argmax & 0xFFFFFFFFull);
     return 0;
@@ -2165,7 +2177,10 @@ int generate_greedy(Seq *s, uint32_t first_token, size_t offset, size_t steps, u
         std::vector<int32_t> log(steps);
         CH_CUDA_TRY(cudaMemcpyAsync(log.data(), s->token_log, steps * 4, cudaMemcpyDeviceToHost, s->stream));
         CH_CUDA_TRY(cudaStreamSynchronize(s->stream));
-        if (check_device_error(*s) != 0) return -1;
+        if (check_device_error(*s) != 0) {
+            s->positions = offset;  // the run's K/V rows are not trusted
+            return -1;
+        }
         for (size_t i = 0; i < steps; ++i) tokens_out[i] = (uint32_t)log[i];
         return 0;
     }
@@ -2190,6 +2205,10 @@ int generate_greedy(Seq *s, uint32_t first_token, size_t offset, size_t steps, u
     CH_CUDA_TRY(cudaMemcpyAsync(log.data(), s->token_log, steps * 4, cudaMemcpyDeviceToHost, s->stream));
     CH_CUDA_TRY(cudaMemcpyAsync(s->h_argmax, s->argmax, 8, cudaMemcpyDeviceToHost, s->stream));
     CH_CUDA_TRY(cudaStreamSynchronize(s->stream));
+    if (check_device_error(*s) != 0) {
+        s->positions = offset;  // the run's K/V rows are not trusted
+        return -1;
+    }
     for (size_t i = 0; i + 1 < steps; ++i) tokens_out[i] = (uint32_t)log[i + 1];
     tokens_out[steps - 1] = (uint32_t)(*s->h_argmax & 0xFFFFFFFFull);
     return 0;
@@ -2216,6 +2235,10 @@ __attribute__((visibility("default"))) int cheetah_cuda_debug_mk_trace(unsigned 
 }
 __attribute__((visibility("default"))) int cheetah_cuda_debug_mk_cycles(long long *out) {
     CH_CUDA_TRY(cudaMemcpyFromSymbol(out, cheetah::g_mk_cycles, sizeof(cheetah::g_mk_cycles)));
+    return 0;
+}
+__attribute__((visibility("default"))) int cheetah_cuda_debug_mk_ptrace(unsigned long long *out) {
+    CH_CUDA_TRY(cudaMemcpyFromSymbol(out, cheetah::g_mk_ptrace, sizeof(cheetah::g_mk_ptrace)));
     return 0;
 }
 #endif

@@ -185,3 +185,34 @@ def test_logits_into_pinned_and_pageable_host_buffers_agree(tiny_prepared, monke
         np.testing.assert_array_equal(pinned, pageable)
         assert ta == tb == int(np.nonzero(pageable == pageable.max())[0][-1])
         tok = ta
+
+
+def test_persistent_decode_wait_timeout_reports_error_and_recovers(tiny_prepared, monkeypatch):
+    """The kernel's bounded waits, exercised without a fault: the test hook
+    CHEETAH_CUDA_TEST_STALL_WAIT=1 makes the run's first attention wait target
+    a count nothing reaches, with a 20 ms bound (no copy is left waiting: the
+    weight copies already issued land and are drained). The call returns the
+    device guard's error with the kernel's code (0x4D4B01), the sequence keeps
+    its positions, the error word and counters are reset, and the same
+    sequence then decodes exactly as a sequence that never failed."""
+    from cheetah_b200 import runtime as R
+    model = _model(tiny_prepared, monkeypatch, True)
+    cfg = model.cfg
+    prompt = _tokens(40, cfg["vocab_size"], 13)
+    seq, clean = model.new_sequence(), model.new_sequence()
+    tok = int(np.argmax(seq.forward(prompt, 0)))
+    clean.forward(prompt, 0)
+    monkeypatch.setenv("CHEETAH_CUDA_TEST_STALL_WAIT", "1")
+    with pytest.raises(R.CheetahCudaError, match=f"code {0x4D4B01}"):
+        seq.forward_greedy([tok], 40)
+    assert seq.positions() == 40
+    with pytest.raises(R.CheetahCudaError, match=f"code {0x4D4B01}"):
+        seq.generate_greedy(tok, 40, 4)
+    assert seq.positions() == 40
+    monkeypatch.delenv("CHEETAH_CUDA_TEST_STALL_WAIT")
+    got, want = np.empty(cfg["vocab_size"], np.float32), np.empty(cfg["vocab_size"], np.float32)
+    ta = seq.forward_greedy([tok], 40, logits_out=got)
+    tb = clean.forward_greedy([tok], 40, logits_out=want)
+    np.testing.assert_array_equal(got, want)
+    assert ta == tb
+    np.testing.assert_array_equal(seq.generate_greedy(ta, 41, 8), clean.generate_greedy(tb, 41, 8))
