@@ -32,6 +32,7 @@
 #include "kernels_misc.cuh"
 #include "quant.cuh"
 #include "gemv_qmma.cuh"
+#include "gemv_mma.cuh"
 #include "gemm_tcgen05.cuh"
 #include "prefill_attention.cuh"
 #include "prefill_attention_tc.cuh"
@@ -48,6 +49,7 @@ const char *last_error() { return g_last_error.c_str(); }
 // Chained batched greedy steps run in chunks of at most this many steps
 // between host reads of the token log.
 constexpr int kChainSteps = 256;
+constexpr int kBatchGemvRows = 8;  // padded batch rows up to which a batched step streams weights through GEMVs
 
 namespace {
 
@@ -124,6 +126,36 @@ int launch_gemv_wt(const GemvParams &p, cudaStream_t stream, bool pdl, int sms) 
     case 4: return launch_gemv_ks<NB, EPI, 4, WT>(p, stream, pdl, sms);
     default: return launch_gemv_ks<NB, EPI, 8, WT>(p, stream, pdl, sms);
     }
+}
+
+// Small-batch decode GEMV (<= 8 rows) on the tensor cores. Enough tiles for
+// every warp of the GPU: a warp per tile. Otherwise a CTA per tile, its K
+// range split over up to `max_tickets` CTAs (at least 16 steps of 32
+// columns per split) until about two items per SM.
+template <int EPI>
+int launch_gemv_mma(GemvParams p, cudaStream_t stream, bool pdl, int sms, int max_tickets) {
+    const int steps = p.cols / 32, tiles = gm_num_tiles(EPI, p.rows);
+    const size_t smem = gemv_mma_smem(p.cols);
+    const bool per_warp = tiles >= sms * kGmWarps / 2;
+    auto kernel = per_warp ? gemv_mma_kernel<EPI, 1> : gemv_mma_kernel<EPI, kGmWarps>;
+    if (smem > 48 * 1024) CH_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    int per_sm = 0;
+    CH_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kGmThreads, smem));
+    per_sm = std::max(1, std::min(per_sm, 4));
+    int items;
+    if (per_warp) {
+        p.splits = 1;
+        items = (tiles + kGmWarps - 1) / kGmWarps;
+    } else {
+        int splits = 1;
+        if (tiles <= max_tickets && p.split_ws != nullptr && p.split_tickets != nullptr)
+            splits = std::max(1, std::min((2 * sms + tiles - 1) / tiles, steps / 16));
+        p.splits = splits;
+        items = tiles * splits;
+    }
+    const int grid = std::max(1, std::min(items, sms * per_sm));
+    CH_CUDA_TRY(launch_ex(kernel, dim3(grid), dim3(kGmThreads), smem, stream, pdl, p));
+    return 0;
 }
 
 template <int NB, int EPI>
@@ -413,6 +445,7 @@ struct Model {
     bool use_mma_attention = false;
     bool qkv_interleaved = false;  // QKV rows stored pair-interleaved (bulk-prefetch GEMV)
     bool gemm_prefill = false;     // bf16 weights with tensor maps: tensor-core chunked prefill
+    bool batch_gemv = false;       // batched steps of <= kBatchGemvRows rows run as weight-streaming GEMVs
     CUtensorMap map_lm_head{};
     // Persistent B=1 decode kernel (bf16 weights, bf16 KV): ring slots,
     // attention key chunks per head, dynamic shared memory, layer table.
@@ -431,6 +464,8 @@ struct Model {
     int32_t *h_meta = nullptr;        // pinned staging of b_meta
     float *b_hid = nullptr, *b_q = nullptr, *b_logits = nullptr;
     uint16_t *b_xb = nullptr, *b_ab = nullptr, *b_act = nullptr;
+    // f32 attention output and SwiGLU activations of the small-batch GEMV step.
+    float *b_attn_f32 = nullptr, *b_act_f32 = nullptr;
     unsigned long long *b_argmax = nullptr, *h_argmax = nullptr;
     float *b_part_o = nullptr, *b_part_ml = nullptr;
     unsigned int *b_tickets = nullptr;
@@ -461,6 +496,9 @@ struct Model {
         cudaFree(b_xb);
         cudaFree(b_ab);
         cudaFree(b_act);
+        cudaFree(b_attn_f32);
+        cudaFree(b_act_f32);
+        b_attn_f32 = b_act_f32 = nullptr;
         cudaFree(b_argmax);
         cudaFreeHost(h_argmax);
         cudaFree(b_part_o);
@@ -1352,6 +1390,10 @@ int open_model(const char *prepared_dir, const CheetahCudaConfig *config, const 
     // Vectorised epilogues: residual widths in 32-column groups, SwiGLU in 16.
     m->gemm_prefill = weight_maps_ok && m->use_mma_attention && (c.head_dim == 64 || c.head_dim == 128) &&
                       c.hidden_size % 32 == 0 && c.intermediate_size % 16 == 0;
+    // Small batches: every weight byte streamed once per step by GEMVs over
+    // all SMs (tensor-core tiles would put a few dozen CTAs on the weights).
+    m->batch_gemv = m->gemm_prefill && !m->qkv_interleaved && env_flag("CHEETAH_CUDA_BATCH_GEMV", true) &&
+                    H % 32 == 0 && I % 32 == 0 && QD % 32 == 0 && ((QD + 2 * KD) / 2) % 8 == 0;
     m->free_pages.reserve(m->num_pages);
     for (int i = m->num_pages - 1; i >= 0; --i) m->free_pages.push_back(i);
     err = cudaDeviceSynchronize();
@@ -1781,6 +1823,7 @@ int ensure_batch_workspace(Model &m, int cap, int table_cap) {
               cudaMalloc(&m.b_hid, R * H * 4) == cudaSuccess && cudaMalloc(&m.b_q, R * QD * 4) == cudaSuccess &&
               cudaMalloc(&m.b_logits, R * V * 4) == cudaSuccess && cudaMalloc(&m.b_xb, R * H * 2) == cudaSuccess &&
               cudaMalloc(&m.b_ab, R * QD * 2) == cudaSuccess && cudaMalloc(&m.b_act, R * I * 2) == cudaSuccess &&
+              cudaMalloc(&m.b_attn_f32, R * QD * 4) == cudaSuccess && cudaMalloc(&m.b_act_f32, R * I * 4) == cudaSuccess &&
               cudaMalloc(&m.b_argmax, R * 8) == cudaSuccess && cudaMallocHost(&m.h_argmax, R * 8) == cudaSuccess &&
               cudaMalloc(&m.b_part_o, parts * kMaxGroup * c.head_dim * 4) == cudaSuccess &&
               cudaMalloc(&m.b_part_ml, parts * kMaxGroup * 2 * 4) == cudaSuccess &&
@@ -1834,7 +1877,159 @@ __global__ void batch_advance_kernel(const unsigned long long *__restrict__ argm
 // argmax. A chained step skips the upload (the metadata is already on the
 // device) and ends with batch_advance_kernel, so the next step consumes this
 // step's greedy ids.
+// The same step for M <= kBatchGemvRows padded rows as weight-streaming
+// tensor-core GEMVs over all M rows at once (gemv_mma.cuh: every weight byte
+// streamed once, the rows as the MMA columns): RMSNorm prologues, QKV with
+// RoPE and the paged K/V append of each row's position, batched tensor-core
+// attention (f32 output), o_proj / down with residual epilogues, gate/up
+// with SwiGLU, lm_head with per-row argmax. f32 activations between the
+// kernels, rounded to bf16 as MMA operands (as the GEMM step's are).
+int enqueue_batch_step_gemv(Model &m, int M, int table_stride, bool want_logits, bool chained) {
+    cudaStream_t st = m.batch_stream;
+    const bool pdl = m.pdl;
+    const int cap = m.batch_cap;
+    const CheetahCudaConfig &c = m.cfg;
+    const int H = c.hidden_size, I = c.intermediate_size, QD = c.q_heads * c.head_dim, KD = c.kv_heads * c.head_dim;
+    if (!chained) {
+        CH_CUDA_TRY(cudaMemcpyAsync(m.b_meta, m.h_meta, (size_t)(3 * cap + M * table_stride) * 4,
+                                    cudaMemcpyHostToDevice, st));
+    }
+    const int32_t *d_tok = m.b_meta, *d_pos = m.b_meta + cap, *d_len = m.b_meta + 2 * cap;
+    const int32_t *d_tab = m.b_meta + 3 * cap;
+    CH_CUDA_TRY(cudaMemsetAsync(m.b_argmax, 0, (size_t)M * 8, st));
+    CH_CUDA_TRY(launch_ex(embed_rows_kernel, dim3(M), dim3(256), 0, st, pdl, m.embed, H, d_tok, M, m.b_hid));
+    const int splits = mma_attention_splits(M, c.kv_heads, m.sms);
+    for (uint32_t layer = 0; layer < c.num_layers; ++layer) {
+        const LayerWeights &w = m.layers[layer];
+        GemvParams q = {};
+        q.w0 = w.wqkv;
+        q.wt = kWBf16;
+        q.rows = QD + 2 * KD;
+        q.cols = H;
+        q.batch = M;
+        q.x = m.b_hid;
+        q.x_stride = H;
+        q.norm_w = w.ln1;
+        q.eps = c.rms_eps;
+        q.bias = w.bqkv;
+        q.y = m.b_q;
+        q.y_stride = QD;
+        q.q_heads = c.q_heads;
+        q.kv_heads = c.kv_heads;
+        q.head_dim = c.head_dim;
+        q.rope_cos = m.rope_cos;
+        q.rope_sin = m.rope_sin;
+        q.positions = d_pos;
+        q.page_table = d_tab;
+        q.max_pages = table_stride;
+        q.num_pages = m.num_pages;
+        q.page_tokens = m.page_tokens;
+        q.k_cache = m.k_pool + layer * m.layer_stride_bytes;
+        q.v_cache = m.v_pool + layer * m.layer_stride_bytes;
+        q.kv_f32 = m.kv_f32;
+        q.error = m.b_error;
+        q.split_ws = m.b_split_ws;
+        q.split_tickets = m.b_split_tickets;
+        if (launch_gemv_mma<kEpiQkv>(q, st, pdl, m.sms, m.sms) != 0) return -1;
+
+        MmaAttnParams ap = {};
+        ap.a.q = m.b_q;
+        ap.a.page_table = d_tab;
+        ap.a.seq_lens = d_len;
+        ap.a.max_pages = table_stride;
+        ap.a.num_pages = m.num_pages;
+        ap.a.page_tokens = m.page_tokens;
+        ap.a.batch = M;
+        ap.a.q_heads = c.q_heads;
+        ap.a.kv_heads = c.kv_heads;
+        ap.a.window = c.sliding_window;
+        ap.a.splits = splits;
+        ap.a.scale = 1.0f / sqrtf((float)c.head_dim);
+        ap.a.out = m.b_attn_f32;
+        ap.a.part_o = m.b_part_o;
+        ap.a.part_ml = m.b_part_ml;
+        ap.a.tickets = m.b_tickets;
+        ap.a.error = m.b_error;
+        ap.layer_row_offset = (long long)layer * m.num_pages * c.kv_heads * m.page_tokens;
+        ap.page_tokens = m.page_tokens;
+        if (launch_attention_mma(m.k_map, m.v_map, ap, c.head_dim, st, pdl) != 0) return -1;
+
+        GemvParams o = {};
+        o.w0 = w.wo;
+        o.wt = kWBf16;
+        o.rows = H;
+        o.cols = QD;
+        o.batch = M;
+        o.x = m.b_attn_f32;
+        o.x_stride = QD;
+        o.bias = w.bo;
+        o.y = m.b_hid;
+        o.y_stride = H;
+        o.error = m.b_error;
+        o.split_ws = m.b_split_ws;
+        o.split_tickets = m.b_split_tickets;
+        if (launch_gemv_mma<kEpiResidual>(o, st, pdl, m.sms, m.sms) != 0) return -1;
+
+        GemvParams gu = {};
+        gu.w0 = w.wgate;
+        gu.w1 = w.wup;
+        gu.wt = kWBf16;
+        gu.rows = I;
+        gu.cols = H;
+        gu.batch = M;
+        gu.x = m.b_hid;
+        gu.x_stride = H;
+        gu.norm_w = w.ln2;
+        gu.eps = c.rms_eps;
+        gu.y = m.b_act_f32;
+        gu.y_stride = I;
+        gu.error = m.b_error;
+        gu.split_ws = m.b_split_ws;
+        gu.split_tickets = m.b_split_tickets;
+        if (launch_gemv_mma<kEpiSwiglu>(gu, st, pdl, m.sms, m.sms) != 0) return -1;
+
+        GemvParams dn = {};
+        dn.w0 = w.wdown;
+        dn.wt = kWBf16;
+        dn.rows = H;
+        dn.cols = I;
+        dn.batch = M;
+        dn.x = m.b_act_f32;
+        dn.x_stride = I;
+        dn.y = m.b_hid;
+        dn.y_stride = H;
+        dn.error = m.b_error;
+        dn.split_ws = m.b_split_ws;
+        dn.split_tickets = m.b_split_tickets;
+        if (launch_gemv_mma<kEpiResidual>(dn, st, pdl, m.sms, m.sms) != 0) return -1;
+    }
+    GemvParams lm = {};
+    lm.w0 = m.lm_head;
+    lm.wt = kWBf16;
+    lm.rows = c.vocab_size;
+    lm.cols = H;
+    lm.batch = M;
+    lm.x = m.b_hid;
+    lm.x_stride = H;
+    lm.norm_w = m.final_norm;
+    lm.eps = c.rms_eps;
+    lm.y = m.b_logits;  // always written (the rows' argmax reads the same pass)
+    lm.y_stride = c.vocab_size;
+    lm.argmax = m.b_argmax;
+    lm.error = m.b_error;
+    lm.split_ws = m.b_split_ws;
+        lm.split_tickets = m.b_split_tickets;
+        if (launch_gemv_mma<kEpiLogits>(lm, st, pdl, m.sms, m.sms) != 0) return -1;
+    (void)want_logits;
+    if (chained) {
+        batch_advance_kernel<<<1, 128, 0, st>>>(m.b_argmax, m.b_meta, cap, M, m.b_chain, m.b_log, kChainSteps);
+        CH_CUDA_TRY(cudaGetLastError());
+    }
+    return 0;
+}
+
 int enqueue_batch_step(Model &m, int M, int table_stride, bool want_logits, bool chained = false) {
+    if (m.batch_gemv && M <= kBatchGemvRows) return enqueue_batch_step_gemv(m, M, table_stride, want_logits, chained);
     cudaStream_t st = m.batch_stream;
     const bool pdl = m.pdl;
     const int cap = m.batch_cap;

@@ -59,6 +59,11 @@ struct GemvParams {
     // kEpiLogits
     unsigned long long *argmax;  // [batch] packed (order key << 32 | index), nullable
     int *error;                  // nullable: set when a bounded wait gives up
+    // Cross-CTA K splits of the small-batch tensor-core GEMV (gemv_mma.cuh):
+    // per-(tile, split) partials and per-tile tickets (zero between launches).
+    int splits;
+    float *split_ws;
+    unsigned *split_tickets;
 };
 
 template <int NB>

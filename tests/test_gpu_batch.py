@@ -18,9 +18,13 @@ def _cuda():
         pytest.skip("needs a CUDA device")
 
 
+@pytest.mark.parametrize("step", ["gemv", "gemm"])
 @pytest.mark.parametrize("fixture", ["tiny_prepared", "tiny7b_prepared"])
-def test_batched_decode_matches_per_sequence_oracle(fixture, request):
+def test_batched_decode_matches_per_sequence_oracle(fixture, step, request, monkeypatch):
+    """Five sequences: the small-batch weight-streaming GEMV step, and the
+    tensor-core GEMM step (CHEETAH_CUDA_BATCH_GEMV=0)."""
     from cheetah_b200 import runtime as R
+    monkeypatch.setenv("CHEETAH_CUDA_BATCH_GEMV", "1" if step == "gemv" else "0")
     root = request.getfixturevalue(fixture)
     pm = PreparedModel(root)
     cfg = resolve_config(pm)

@@ -116,16 +116,20 @@ def test_config2_attention_28_4_128_long_context_batch32():
         assert err < 1e-2, f"b={b} max err {err}"
 
 
-def test_config5_batched_step_mixed_long_contexts_matches_oracle():
-    """16 sequences of the 0.5B shape at contexts from 1 to 8192 tokens:
+@pytest.mark.parametrize("lengths", [
+    [8192, 1, 4097, 63, 64, 65, 7000, 129, 2048, 3001, 511, 6144, 17, 1000, 5555, 300],  # tensor-core GEMM step
+    [6000, 1, 700, 64, 8192, 129],                                                      # weight-streaming GEMV step
+])
+def test_config5_batched_step_mixed_long_contexts_matches_oracle(lengths):
+    """Sequences of the 0.5B shape at contexts from 1 to 8192 tokens:
     prefilled on the GPU, their cached K/V copied into per-sequence oracle
     models, then three batched greedy steps compared step by step with the
-    oracle's single-sequence steps (logits 2e-2, greedy ids identical)."""
+    oracle's single-sequence steps (logits 2e-2, greedy ids identical). 16
+    rows take the tensor-core GEMM step, 6 rows (padded to 8) the GEMV step."""
     from cheetah_b200 import runtime as R
     root = cached_synthetic("qwen2-0.5b")
     pm = PreparedModel(root)
     cfg = resolve_config(pm)
-    lengths = [8192, 1, 4097, 63, 64, 65, 7000, 129, 2048, 3001, 511, 6144, 17, 1000, 5555, 300]
     pool = sum(lengths) + 64 * (len(lengths) + 4) + 4096
     model = R.CudaModel(root, max_positions=8192 + 64, kv_pool_tokens=pool)
     rng = np.random.default_rng(31)
