@@ -663,6 +663,66 @@ def _gather_dicts(torch, obj, world):
     return [json.loads(bytes(o.cpu().numpy().tolist()).rstrip(b"\0").decode()) for o in outs]
 
 
+def clones_bench(torch, R, model_dir, cfg, single_e2e, clones=16, steps=32, warmup=4, prompt_len=128):
+    """`ModelForward` clones driven concurrently: one host thread per clone
+    calls the plain per-sequence forward (`cheetah_cuda_forward_ex`, host
+    token in, pinned host logits and greedy id out) every step, the way the
+    reference's serve loop drives one clone per generation. The backend's
+    batcher folds calls that meet into batched steps. Aggregate tok/s over
+    the timed steps, wall clock (host-visible end to end)."""
+    import threading
+    model = R.CudaModel(model_dir, max_positions=1024, kv_pool_tokens=clones * 512 + 4096)
+    rng = np.random.default_rng(5)
+    seqs = [model.new_sequence() for _ in range(clones)]
+    toks = [int(np.argmax(s.forward(rng.integers(0, cfg["vocab_size"], prompt_len).astype(np.uint32), 0)))
+            for s in seqs]
+    pos = [prompt_len] * clones
+    bufs = [torch.empty(cfg["vocab_size"], dtype=torch.float32, pin_memory=True).numpy() for _ in range(clones)]
+
+    def drive(n):
+        barrier = threading.Barrier(clones + 1)
+        errors = []
+
+        def worker(i):
+            try:
+                barrier.wait()
+                for _ in range(n):
+                    toks[i] = seqs[i].forward_greedy([toks[i]], pos[i], logits_out=bufs[i])
+                    pos[i] += 1
+            except Exception as e:  # noqa: BLE001 - reported below
+                errors.append(e)
+
+        threads = [threading.Thread(target=worker, args=(i,)) for i in range(clones)]
+        for t in threads:
+            t.start()
+        barrier.wait()
+        t0 = time.perf_counter()
+        for t in threads:
+            t.join()
+        if errors:
+            raise errors[0]
+        return time.perf_counter() - t0
+
+    drive(warmup)
+    before = model.coalesce_stats()
+    elapsed = drive(steps)
+    after = model.coalesce_stats()
+    calls = after["calls"] - before["calls"]
+    batched = after["batched_calls"] - before["batched_calls"]
+    batches = after["batches"] - before["batches"]
+    del seqs
+    model.close()
+    value = clones * steps / elapsed
+    return {"value": value, "unit": "tok/s", "clones": clones, "steps_per_clone": steps,
+            "prompt_len": prompt_len, "ms_per_round": 1e3 * elapsed / steps,
+            "batched_share": batched / max(1, calls), "mean_batch": batched / max(1, batches),
+            "api": "cheetah_cuda_forward_ex, one host thread per clone (host token in, pinned host logits "
+                   "+ greedy id out)",
+            "vs_single_sequence_e2e": value / single_e2e,
+            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 4 * clones,
+                    "d2h_bytes_per_step": (cfg["vocab_size"] * 4 + 4) * clones}}
+
+
 def run_serve(args):
     """`--gpus N` with N > 1 (or `--workload serve-0.5b`): config 5 is the value."""
     import torch
@@ -807,6 +867,8 @@ def run_ours(args):
         line["serve"] = serve_summary([mine], 1, hbm_peak)
         line["serve"]["gpu_launches"] = mine["steps"] * (BATCH_STEP_FIXED_LAUNCHES +
                                                           BATCH_STEP_LAUNCHES_PER_LAYER * cfg["num_layers"])
+    if not args.no_serve:
+        line["clones"] = clones_bench(torch, R, model_dir, cfg, e2e["value"])
     if not args.no_7b:
         dir7 = synthetic_model("qwen2-7b")
         cfg7 = resolve_config(PreparedModel(dir7))

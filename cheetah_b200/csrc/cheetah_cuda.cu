@@ -16,6 +16,8 @@
 
 #include <algorithm>
 #include <atomic>
+#include <chrono>
+#include <condition_variable>
 #include <cstdlib>
 #include <map>
 #include <mutex>
@@ -410,6 +412,9 @@ struct LayerWeights {
     const float *ln2 = nullptr;
     const float *bqkv = nullptr;
     const float *bo = nullptr;
+    // Per-head q/k RMSNorm weights (qwen3's `self_attn.{q,k}_norm`), f32 [head_dim].
+    const float *q_norm = nullptr;
+    const float *k_norm = nullptr;
     // Persistent decode kernel copies: QKV rows as all first rows of the
     // rotate-half pairs, then all partner rows (a tile of pairs is two
     // contiguous bulk copies); W_o as head-major [q_heads][hidden][head_dim]
@@ -419,6 +424,20 @@ struct LayerWeights {
 };
 
 }  // namespace
+
+struct Seq;
+
+// One single-token forward waiting to be folded into a batched step.
+struct CoalescedCall {
+    Seq *s = nullptr;
+    uint32_t token = 0;
+    size_t offset = 0;
+    float *logits = nullptr;
+    uint32_t *argmax = nullptr;
+    int status = 0;
+    std::string error;
+    bool done = false;
+};
 
 struct Model {
     CheetahCudaConfig cfg{};
@@ -450,6 +469,9 @@ struct Model {
     // Persistent B=1 decode kernel (bf16 weights, bf16 KV): ring slots,
     // attention key chunks per head, dynamic shared memory, layer table.
     bool mk_enabled = false;
+    // Per-head q/k RMSNorm units present (qwen3): the QKV epilogues normalise
+    // each q and k head before RoPE; the persistent decode kernel is off.
+    bool qk_norm = false;
     int mk_slots = 0;
     int mk_group_units = 1;  // attention units of a query head (CTAs per head, rounded up)
     size_t mk_smem = 0;
@@ -466,6 +488,7 @@ struct Model {
     uint16_t *b_xb = nullptr, *b_ab = nullptr, *b_act = nullptr;
     // f32 attention output and SwiGLU activations of the small-batch GEMV step.
     float *b_attn_f32 = nullptr, *b_act_f32 = nullptr;
+    float *b_qk_raw = nullptr;  // [cap][q + 2 kv dims] biased QKV rows (per-head q/k norm families)
     unsigned long long *b_argmax = nullptr, *h_argmax = nullptr;
     float *b_part_o = nullptr, *b_part_ml = nullptr;
     unsigned int *b_tickets = nullptr;
@@ -483,7 +506,19 @@ struct Model {
     CUtensorMap v_map{};
     std::mutex pool_mutex;
     std::vector<int> free_pages;
+    // Holders of each KV page (sequences and snapshots); 0 = free. A page
+    // with more than one holder is never written: a sequence about to append
+    // into one first takes a private copy (make_tail_page_private).
+    std::vector<int> page_refs;
     std::atomic<int> refs{1};
+    // Continuous batching behind the per-sequence forward: single-token
+    // calls that arrive while a step runs are folded into the next one.
+    std::mutex co_mutex;
+    std::condition_variable co_cv;
+    std::vector<CoalescedCall *> co_pending;
+    bool co_running = false;
+    size_t co_last_group = 0;  // calls in the previous group (how many callers are active)
+    std::atomic<unsigned long long> co_calls{0}, co_batched_calls{0}, co_batches{0};
 
     void free_batch() {
         for (auto &kv : batch_graphs) cudaGraphExecDestroy(kv.second);
@@ -498,7 +533,8 @@ struct Model {
         cudaFree(b_act);
         cudaFree(b_attn_f32);
         cudaFree(b_act_f32);
-        b_attn_f32 = b_act_f32 = nullptr;
+        cudaFree(b_qk_raw);
+        b_attn_f32 = b_act_f32 = b_qk_raw = nullptr;
         cudaFree(b_argmax);
         cudaFreeHost(h_argmax);
         cudaFree(b_part_o);
@@ -536,13 +572,27 @@ struct Model {
         if (free_pages.empty()) return -1;
         int page = free_pages.back();
         free_pages.pop_back();
+        page_refs[page] = 1;
         return page;
     }
 
+    // Drops one hold on each page; a page nobody holds returns to the pool.
     void release_pages(std::vector<int> &pages) {
         std::lock_guard<std::mutex> lock(pool_mutex);
-        for (int page : pages) free_pages.push_back(page);
+        for (int page : pages) {
+            if (--page_refs[page] == 0) free_pages.push_back(page);
+        }
         pages.clear();
+    }
+
+    void retain_pages(const std::vector<int> &pages) {
+        std::lock_guard<std::mutex> lock(pool_mutex);
+        for (int page : pages) ++page_refs[page];
+    }
+
+    int page_holders(int page) {
+        std::lock_guard<std::mutex> lock(pool_mutex);
+        return page_refs[page];
     }
 
     ~Model() {
@@ -570,6 +620,7 @@ struct Seq {
     int max_pages = 0;
     int32_t *page_table = nullptr;
     float *hidden = nullptr, *q = nullptr, *attn_out = nullptr, *act = nullptr, *logits = nullptr;
+    float *qk_raw = nullptr;  // [q + 2 kv dims] biased QKV (per-head q/k norm families)
     unsigned long long *argmax = nullptr;
     StepState *d_step = nullptr;
     StepState *h_step = nullptr;
@@ -625,6 +676,7 @@ struct Seq {
         cudaFree(page_table);
         cudaFree(hidden);
         cudaFree(q);
+        cudaFree(qk_raw);
         cudaFree(attn_out);
         cudaFree(act);
         cudaFree(logits);
@@ -805,7 +857,12 @@ int enqueue_decode_step(Seq &s, bool chain) {
         qkv.k_cache = k_layer;
         qkv.v_cache = v_layer;
         qkv.kv_f32 = m.kv_f32;
+        if (m.qk_norm) qkv.qk_raw = s.qk_raw;
         if (run_gemv<kEpiQkv>(qkv, st, pdl, m.sms) != 0) return -1;
+        if (m.qk_norm) {
+            CH_CUDA_TRY(launch_ex(qk_norm_rope_kernel, dim3(c.q_heads + 2 * c.kv_heads, 1), dim3(32), 0, st, pdl,
+                                  qkv, w.q_norm, w.k_norm));
+        }
 
         AttnParams at = {};
         at.q = s.q;
@@ -1099,7 +1156,10 @@ int open_model(const char *prepared_dir, const CheetahCudaConfig *config, const 
         // The K/V tiles arrive by 128-byte-swizzled tensor-map loads (the bf16
         // cache's maps): pages a whole number of tiles; every query head
         // gets at least one attention unit.
+        m->qk_norm = store.contains("model.layers.0.self_attn.q_norm.weight") ||
+                     store.contains("model.layers.0.self_attn.k_norm.weight");
         m->mk_enabled = env_flag("CHEETAH_CUDA_MEGAKERNEL", true) && coop != 0 && wfmt == kWBf16 && !m->kv_f32 &&
+                        !m->qk_norm &&
                         4 * H <= (size_t)kMkSlotBytes && 2 * I <= (size_t)kMkSlotBytes &&
                         c.q_heads <= (uint32_t)kMkMaxHeads && c.q_heads <= (uint32_t)m->sms &&
                         mma_attention_eligible((int)c.head_dim, m->page_tokens) && slots >= 3;
@@ -1311,6 +1371,17 @@ int open_model(const char *prepared_dir, const CheetahCudaConfig *config, const 
             if (!upload_f32_from_bf16(bo, bytes, H)) return fail(error);
             w.bo = bo;
         }
+        // Per-head q/k norms are unit-optional as well (`ops.rs:1130-1152`).
+        const char *norm_names[2] = {"self_attn.q_norm.weight", "self_attn.k_norm.weight"};
+        const float **norm_dst[2] = {&w.q_norm, &w.k_norm};
+        for (int k = 0; k < 2; ++k) {
+            if (!store.contains(p + norm_names[k])) continue;
+            if (!m->qk_norm) return fail("CUDA backend: per-head q/k norms must start at layer 0");
+            if (!check_unit(p + norm_names[k], {(size_t)c.head_dim}, &bytes)) return fail(error);
+            float *nw = (float *)m->take((size_t)c.head_dim * 4);
+            if (!upload_f32_from_bf16(nw, bytes, c.head_dim)) return fail(error);
+            *norm_dst[k] = nw;
+        }
     }
 
     cudaFree(staging);
@@ -1396,6 +1467,7 @@ int open_model(const char *prepared_dir, const CheetahCudaConfig *config, const 
                     H % 32 == 0 && I % 32 == 0 && QD % 32 == 0 && ((QD + 2 * KD) / 2) % 8 == 0;
     m->free_pages.reserve(m->num_pages);
     for (int i = m->num_pages - 1; i >= 0; --i) m->free_pages.push_back(i);
+    m->page_refs.assign(m->num_pages, 0);
     err = cudaDeviceSynchronize();
     if (err != cudaSuccess) return fail(std::string("CUDA backend: ") + cudaGetErrorString(err));
     *out = m;
@@ -1418,6 +1490,7 @@ int new_seq(Model *m, Seq **out) {
               cudaMalloc(&s->page_table, s->max_pages * sizeof(int32_t)) == cudaSuccess &&
               cudaMalloc(&s->hidden, c.hidden_size * 4) == cudaSuccess &&
               cudaMalloc(&s->q, QD * 4) == cudaSuccess &&
+              cudaMalloc(&s->qk_raw, (QD + 2 * (size_t)c.kv_heads * c.head_dim) * 4) == cudaSuccess &&
               cudaMalloc(&s->attn_out, QD * 4) == cudaSuccess &&
               cudaMalloc(&s->act, c.intermediate_size * 4) == cudaSuccess &&
               cudaMalloc(&s->logits, (size_t)c.vocab_size * 4) == cudaSuccess &&
@@ -1455,6 +1528,8 @@ int prefill_chunk_rows();
 int run_prefill_chunk(Seq &s, const uint32_t *tokens, int M, size_t offset, bool last);
 int check_device_error(Seq &s);
 
+int make_tail_page_private(Seq &s);
+
 int forward(Seq *s, const uint32_t *tokens, size_t n, size_t offset, float *logits_out,
             uint32_t *argmax_out) {
     CH_REQUIRE(s != nullptr, "cheetah_cuda_forward: null sequence");
@@ -1474,6 +1549,7 @@ int forward(Seq *s, const uint32_t *tokens, size_t n, size_t offset, float *logi
                "CUDA backend: position " + std::to_string(offset + n - 1) +
                    " exceeds the sequence capacity " + std::to_string(c.max_positions) + ".");
     CH_CUDA_TRY(cudaSetDevice(s->m->device));
+    if (make_tail_page_private(*s) != 0) return -1;
     const bool chunked = n > 1 && s->m->gemm_prefill && std::getenv("CHEETAH_CUDA_STEPWISE_PREFILL") == nullptr;
     if (chunked) {
         const size_t chunk = (size_t)prefill_chunk_rows();
@@ -1511,6 +1587,51 @@ int forward(Seq *s, const uint32_t *tokens, size_t n, size_t offset, float *logi
     }
     if (logits_out && !direct) memcpy(logits_out, s->h_logits, (size_t)c.vocab_size * 4);
     if (argmax_out) *argmax_out = (uint32_t)(*s->h_argmax & 0xFFFFFFFFull);
+    return 0;
+}
+
+int copy_pages(Model *m, const std::vector<int> &src, const std::vector<int> &dst, cudaStream_t stream) {
+    if (src.empty()) return 0;
+    int32_t *d_ids = nullptr;
+    CH_CUDA_TRY(cudaMalloc(&d_ids, src.size() * 2 * sizeof(int32_t)));
+    std::vector<int32_t> ids(src.begin(), src.end());
+    ids.insert(ids.end(), dst.begin(), dst.end());
+    cudaError_t err = cudaMemcpyAsync(d_ids, ids.data(), ids.size() * 4, cudaMemcpyHostToDevice, stream);
+    if (err == cudaSuccess) {
+        copy_pages_kernel<<<4 * m->sms, 256, 0, stream>>>(
+            d_ids, d_ids + src.size(), (int)src.size(), m->k_pool, m->v_pool, m->layer_stride_bytes,
+            (int)m->cfg.num_layers, m->page_bytes);
+        err = cudaGetLastError();
+    }
+    if (err == cudaSuccess) err = cudaStreamSynchronize(stream);
+    cudaFree(d_ids);
+    CH_CUDA_TRY(err);
+    return 0;
+}
+
+// Copy-on-write of the page a sequence appends into next: the page holding
+// position `positions` when a snapshot or another sequence also holds it
+// (the pages before it are full and never written again).
+int make_tail_page_private(Seq &s) {
+    const size_t index = s.positions / s.m->page_tokens;
+    if (index >= s.pages.size()) return 0;
+    const int shared = s.pages[index];
+    if (s.m->page_holders(shared) <= 1) return 0;
+    const int page = s.m->alloc_page();
+    if (page < 0) {
+        set_error("CUDA backend: KV page pool exhausted (raise kv_pool_tokens).");
+        return -1;
+    }
+    std::vector<int> dst{page};
+    if (copy_pages(s.m, {shared}, dst, s.stream) != 0) {
+        s.m->release_pages(dst);
+        return -1;
+    }
+    std::vector<int> old{shared};
+    s.m->release_pages(old);
+    s.pages[index] = page;
+    const int32_t id = page;
+    CH_CUDA_TRY(cudaMemcpy(s.page_table + index, &id, 4, cudaMemcpyHostToDevice));
     return 0;
 }
 
@@ -1630,6 +1751,59 @@ int launch_prefill_gemm(const CUtensorMap &a, const CUtensorMap &b, const CUtens
     return launch_prefill_gemm_bn<EPI, 128>(a, b, b2, p, st, pdl, splits);
 }
 
+// Causal prefill attention over the paged bf16 cache (`ops.rs:1357-1421`
+// for each query row; the rows' own K/V are already appended): tensor-core
+// (tcgen05) kernel for head_dim 64, tensor-core mma kernel for 128. Key-range
+// splits fill the SMs when the query rows alone do not; a merge kernel then
+// combines the partials (ap.part_o / ap.part_ml sized for kPrefillMaxSplits).
+int launch_prefill_attention(PrefillAttnParams ap, const CUtensorMap &q_map, const CUtensorMap &k_map,
+                             const CUtensorMap &v_map, int head_dim, size_t offset, int sms, cudaStream_t st,
+                             bool pdl) {
+    const int M = ap.T;
+    if (head_dim == 64 && env_flag("CHEETAH_PREFILL_TC", true)) {
+        // Tensor-core attention: one CTA per SM (512 TMEM columns each);
+        // key-range splits fill the SMs, each split >= 2 key tiles.
+        const int blocks = ((M + kTcRows - 1) / kTcRows) * ap.q_heads;
+        const int key_tiles = (int)((offset + M + kTcKeys - 1) / kTcKeys);
+        ap.splits = std::max(1, std::min(std::min(kPrefillMaxSplits, sms / blocks), key_tiles / 2));
+        const size_t tsmem = prefill_attention_tc_smem();
+        CH_CUDA_TRY(cudaFuncSetAttribute(prefill_attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)tsmem));
+        dim3 tgrid((M + kTcRows - 1) / kTcRows, ap.q_heads, ap.splits);
+        CH_CUDA_TRY(launch_ex(prefill_attention_tc_kernel, tgrid, dim3(kTcThreads), tsmem, st, pdl, q_map, k_map,
+                              v_map, ap));
+        if (ap.splits > 1) {
+            CH_CUDA_TRY(launch_ex(prefill_merge_kernel<64>, dim3(2 * sms), dim3(256), 0, st, pdl, ap));
+        }
+        return 0;
+    }
+    const size_t asmem = prefill_attention_smem();
+    // Key-range splits: about two CTAs per SM (each CTA covers >= 4 key tiles).
+    const int blocks = ((M + 15) / 16) * ap.kv_heads;
+    const int key_tiles = (int)((offset + M + 63) / 64);
+    ap.splits = std::max(1, std::min(std::min(kPrefillMaxSplits, (2 * sms + blocks - 1) / blocks),
+                                     std::max(1, key_tiles / 4)));
+    dim3 agrid((M + 15) / 16, ap.kv_heads, ap.splits);
+    if (head_dim == 64) {
+        CH_CUDA_TRY(cudaFuncSetAttribute(prefill_attention_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)asmem));
+        CH_CUDA_TRY(launch_ex(prefill_attention_kernel<64>, agrid, dim3(kPrefillWarps * kWarp), asmem, st, pdl,
+                              k_map, v_map, ap));
+        if (ap.splits > 1) {
+            CH_CUDA_TRY(launch_ex(prefill_merge_kernel<64>, dim3(2 * sms), dim3(256), 0, st, pdl, ap));
+        }
+    } else {
+        CH_CUDA_TRY(cudaFuncSetAttribute(prefill_attention_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)asmem));
+        CH_CUDA_TRY(launch_ex(prefill_attention_kernel<128>, agrid, dim3(kPrefillWarps * kWarp), asmem, st, pdl,
+                              k_map, v_map, ap));
+        if (ap.splits > 1) {
+            CH_CUDA_TRY(launch_ex(prefill_merge_kernel<128>, dim3(2 * sms), dim3(256), 0, st, pdl, ap));
+        }
+    }
+    return 0;
+}
+
 // One prompt chunk through every layer on the tensor cores
 // (`Qwen2Native::forward_chunk`, `qwen2.rs:208-233`): embeddings, then per
 // layer norm -> QKV GEMM (+bias, RoPE, KV append) -> causal attention ->
@@ -1658,6 +1832,9 @@ int run_prefill_chunk(Seq &s, const uint32_t *tokens, int M, size_t offset, bool
         g.N = QD + 2 * KD;
         g.K = H;
         g.bias = w.bqkv;
+        g.q_norm = w.q_norm;
+        g.k_norm = w.k_norm;
+        g.eps = c.rms_eps;
         g.out_bf16 = s.pqb;
         g.ld_out = QD;
         g.q_heads = c.q_heads;
@@ -1693,47 +1870,8 @@ int run_prefill_chunk(Seq &s, const uint32_t *tokens, int M, size_t offset, bool
         ap.error = s.d_error;
         ap.part_o = s.ppart_o;
         ap.part_ml = s.ppart_ml;
-        if (c.head_dim == 64 && env_flag("CHEETAH_PREFILL_TC", true)) {
-            // Tensor-core attention: one CTA per SM (512 TMEM columns each);
-            // key-range splits fill the SMs, each split >= 2 key tiles.
-            const int blocks = ((M + kTcRows - 1) / kTcRows) * (int)c.q_heads;
-            const int key_tiles = (int)((offset + M + kTcKeys - 1) / kTcKeys);
-            ap.splits = std::max(1, std::min(std::min(kPrefillMaxSplits, m.sms / blocks), key_tiles / 2));
-            const size_t tsmem = prefill_attention_tc_smem();
-            CH_CUDA_TRY(cudaFuncSetAttribute(prefill_attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)tsmem));
-            dim3 tgrid((M + kTcRows - 1) / kTcRows, c.q_heads, ap.splits);
-            CH_CUDA_TRY(launch_ex(prefill_attention_tc_kernel, tgrid, dim3(kTcThreads), tsmem, st, pdl, s.map_qb,
-                                  m.k_map, m.v_map, ap));
-            if (ap.splits > 1) {
-                CH_CUDA_TRY(launch_ex(prefill_merge_kernel<64>, dim3(2 * m.sms), dim3(256), 0, st, pdl, ap));
-            }
-        } else {
-            const size_t asmem = prefill_attention_smem();
-            // Key-range splits: about two CTAs per SM (each CTA covers >= 4 key tiles).
-            const int blocks = ((M + 15) / 16) * (int)c.kv_heads;
-            const int key_tiles = (int)((offset + M + 63) / 64);
-            ap.splits = std::max(1, std::min(std::min(kPrefillMaxSplits, (2 * m.sms + blocks - 1) / blocks),
-                                             std::max(1, key_tiles / 4)));
-            dim3 agrid((M + 15) / 16, c.kv_heads, ap.splits);
-            if (c.head_dim == 64) {
-                CH_CUDA_TRY(cudaFuncSetAttribute(prefill_attention_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 (int)asmem));
-                CH_CUDA_TRY(launch_ex(prefill_attention_kernel<64>, agrid, dim3(kPrefillWarps * kWarp), asmem, st, pdl,
-                                      m.k_map, m.v_map, ap));
-                if (ap.splits > 1) {
-                    CH_CUDA_TRY(launch_ex(prefill_merge_kernel<64>, dim3(2 * m.sms), dim3(256), 0, st, pdl, ap));
-                }
-            } else {
-                CH_CUDA_TRY(cudaFuncSetAttribute(prefill_attention_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 (int)asmem));
-                CH_CUDA_TRY(launch_ex(prefill_attention_kernel<128>, agrid, dim3(kPrefillWarps * kWarp), asmem, st, pdl,
-                                      m.k_map, m.v_map, ap));
-                if (ap.splits > 1) {
-                    CH_CUDA_TRY(launch_ex(prefill_merge_kernel<128>, dim3(2 * m.sms), dim3(256), 0, st, pdl, ap));
-                }
-            }
-        }
+        if (launch_prefill_attention(ap, s.map_qb, m.k_map, m.v_map, (int)c.head_dim, offset, m.sms, st, pdl) != 0)
+            return -1;
 
         PrefillGemmParams o = {};
         o.M = M;
@@ -1824,6 +1962,7 @@ int ensure_batch_workspace(Model &m, int cap, int table_cap) {
               cudaMalloc(&m.b_logits, R * V * 4) == cudaSuccess && cudaMalloc(&m.b_xb, R * H * 2) == cudaSuccess &&
               cudaMalloc(&m.b_ab, R * QD * 2) == cudaSuccess && cudaMalloc(&m.b_act, R * I * 2) == cudaSuccess &&
               cudaMalloc(&m.b_attn_f32, R * QD * 4) == cudaSuccess && cudaMalloc(&m.b_act_f32, R * I * 4) == cudaSuccess &&
+              cudaMalloc(&m.b_qk_raw, R * (QD + 2 * (size_t)c.kv_heads * c.head_dim) * 4) == cudaSuccess &&
               cudaMalloc(&m.b_argmax, R * 8) == cudaSuccess && cudaMallocHost(&m.h_argmax, R * 8) == cudaSuccess &&
               cudaMalloc(&m.b_part_o, parts * kMaxGroup * c.head_dim * 4) == cudaSuccess &&
               cudaMalloc(&m.b_part_ml, parts * kMaxGroup * 2 * 4) == cudaSuccess &&
@@ -1930,7 +2069,12 @@ int enqueue_batch_step_gemv(Model &m, int M, int table_stride, bool want_logits,
         q.error = m.b_error;
         q.split_ws = m.b_split_ws;
         q.split_tickets = m.b_split_tickets;
+        if (m.qk_norm) q.qk_raw = m.b_qk_raw;
         if (launch_gemv_mma<kEpiQkv>(q, st, pdl, m.sms, m.sms) != 0) return -1;
+        if (m.qk_norm) {
+            CH_CUDA_TRY(launch_ex(qk_norm_rope_kernel, dim3(c.q_heads + 2 * c.kv_heads, M), dim3(32), 0, st, pdl,
+                                  q, w.q_norm, w.k_norm));
+        }
 
         MmaAttnParams ap = {};
         ap.a.q = m.b_q;
@@ -2053,6 +2197,9 @@ int enqueue_batch_step(Model &m, int M, int table_stride, bool want_logits, bool
         g.N = QD + 2 * KD;
         g.K = H;
         g.bias = w.bqkv;
+        g.q_norm = w.q_norm;
+        g.k_norm = w.k_norm;
+        g.eps = c.rms_eps;
         g.out_q_f32 = m.b_q;
         g.ld_out = QD;
         g.q_heads = c.q_heads;
@@ -2172,7 +2319,7 @@ int prepare_batch(Model &m, Seq *const *seqs, const uint32_t *tokens, const size
                    "CUDA backend: position " + std::to_string(offsets[b] + steps - 1) +
                        " exceeds the sequence capacity " + std::to_string(c.max_positions) + ".");
         CH_CUDA_TRY(cudaStreamSynchronize(s->stream));
-        if (ensure_pages_upto(*s, offsets[b] + steps) != 0) return -1;
+        if (make_tail_page_private(*s) != 0 || ensure_pages_upto(*s, offsets[b] + steps) != 0) return -1;
         max_pages_used = std::max(max_pages_used, s->pages.size());
     }
     const int table_stride = (int)((max_pages_used + 15) / 16 * 16);
@@ -2240,8 +2387,10 @@ int check_batch_error(Model &m) {
 // stream is shared by the batch; attention reads each sequence's own pages.
 // The step is replayed from a CUDA graph cached per (padded rows, page-table
 // stride, logits wanted).
-int forward_batch(Model *mp, Seq *const *seqs, const uint32_t *tokens, const size_t *offsets, size_t B,
-                  float *logits_out, uint32_t *argmax_out) {
+// row_logits: nullptr, or one host destination per row (nullptr rows get no
+// copy); each row is copied straight into its destination.
+int forward_batch_rows(Model *mp, Seq *const *seqs, const uint32_t *tokens, const size_t *offsets, size_t B,
+                       float *const *row_logits, uint32_t *argmax_out) {
     CH_REQUIRE(mp != nullptr && seqs != nullptr && tokens != nullptr && offsets != nullptr,
                "cheetah_cuda_forward_batch: null argument");
     Model &m = *mp;
@@ -2249,7 +2398,8 @@ int forward_batch(Model *mp, Seq *const *seqs, const uint32_t *tokens, const siz
     std::lock_guard<std::mutex> lock(m.batch_mutex);
     int M = 0, table_stride = 0;
     if (prepare_batch(m, seqs, tokens, offsets, B, 1, "cheetah_cuda_forward_batch", &M, &table_stride) != 0) return -1;
-    const bool want_logits = logits_out != nullptr;
+    bool want_logits = false;
+    for (size_t b = 0; row_logits != nullptr && b < B; ++b) want_logits |= row_logits[b] != nullptr;
     cudaGraphExec_t exec = nullptr;
     if (batch_graph(m, M, table_stride, want_logits, false, &exec) != 0) return -1;
     cudaStream_t st = m.batch_stream;
@@ -2258,8 +2408,10 @@ int forward_batch(Model *mp, Seq *const *seqs, const uint32_t *tokens, const siz
     } else if (enqueue_batch_step(m, M, table_stride, want_logits) != 0) {
         return -1;
     }
-    if (logits_out) {
-        CH_CUDA_TRY(cudaMemcpyAsync(logits_out, m.b_logits, (size_t)B * c.vocab_size * 4, cudaMemcpyDeviceToHost, st));
+    for (size_t b = 0; want_logits && b < B; ++b) {
+        if (row_logits[b] == nullptr) continue;
+        CH_CUDA_TRY(cudaMemcpyAsync(row_logits[b], m.b_logits + b * c.vocab_size, (size_t)c.vocab_size * 4,
+                                    cudaMemcpyDeviceToHost, st));
     }
     CH_CUDA_TRY(cudaMemcpyAsync(m.h_argmax, m.b_argmax, (size_t)B * 8, cudaMemcpyDeviceToHost, st));
     CH_CUDA_TRY(cudaStreamSynchronize(st));
@@ -2269,6 +2421,151 @@ int forward_batch(Model *mp, Seq *const *seqs, const uint32_t *tokens, const siz
         if (argmax_out) argmax_out[b] = (uint32_t)(m.h_argmax[b] & 0xFFFFFFFFull);
     }
     return 0;
+}
+
+int forward_batch(Model *mp, Seq *const *seqs, const uint32_t *tokens, const size_t *offsets, size_t B,
+                  float *logits_out, uint32_t *argmax_out) {
+    CH_REQUIRE(mp != nullptr, "cheetah_cuda_forward_batch: null argument");
+    if (logits_out == nullptr) return forward_batch_rows(mp, seqs, tokens, offsets, B, nullptr, argmax_out);
+    CH_REQUIRE(B > 0 && B <= 128, "cheetah_cuda_forward_batch: batch must be 1..128");
+    float *rows[128];
+    for (size_t b = 0; b < B; ++b) rows[b] = logits_out + b * mp->cfg.vocab_size;
+    return forward_batch_rows(mp, seqs, tokens, offsets, B, rows, argmax_out);
+}
+
+// ---- Continuous batching behind the per-sequence forward -----------------
+// The reference serves concurrent generations by giving each one a clone of
+// the model (`engine.rs:1872-1876`, `ModelForwardClone`) whose `forward`
+// runs on its own thread. Here every clone is a sequence of one shared model,
+// and single-token forwards that reach the model while a step is running
+// queue up and run together as the next batched step (tensor-core GEMMs or
+// weight-streaming GEMVs shared by the batch): the first waiting caller runs
+// everything queued, the others sleep until their results are in. One caller
+// alone runs at once, without waiting for company. Groups smaller than
+// CHEETAH_CUDA_COALESCE_MIN (default 3) run one by one on the single-sequence
+// path, which beats a batched step that small.
+
+// Validates one call alone (the checks `forward` makes), so a bad call fails
+// by itself instead of failing the calls batched with it.
+bool coalesced_call_valid(CoalescedCall &call) {
+    const CheetahCudaConfig &c = call.s->m->cfg;
+    if (call.token >= c.vocab_size) {
+        call.error = "Native backend: token id " + std::to_string(call.token) + " exceeds the vocabulary size " +
+                     std::to_string(c.vocab_size) + ".";
+    } else if (call.offset != call.s->positions) {
+        call.error = "CUDA backend: offset " + std::to_string(call.offset) + " does not match the " +
+                     std::to_string(call.s->positions) + " cached positions.";
+    } else if (call.offset + 1 > c.max_positions) {
+        call.error = "CUDA backend: position " + std::to_string(call.offset) + " exceeds the sequence capacity " +
+                     std::to_string(c.max_positions) + ".";
+    } else {
+        return true;
+    }
+    call.status = -1;
+    return false;
+}
+
+void run_coalesced(Model &m, const std::vector<CoalescedCall *> &calls) {
+    std::vector<CoalescedCall *> ok;
+    for (CoalescedCall *call : calls) {
+        if (coalesced_call_valid(*call)) ok.push_back(call);
+    }
+    const size_t min_batch = (size_t)std::max(2, env_int("CHEETAH_CUDA_COALESCE_MIN", 3));
+    if (ok.size() < min_batch) {
+        for (CoalescedCall *call : ok) {
+            call->status = forward(call->s, &call->token, 1, call->offset, call->logits, call->argmax);
+            if (call->status != 0) call->error = last_error();
+        }
+        return;
+    }
+    constexpr size_t kMaxRows = 128;  // forward_batch's limit
+    for (size_t b0 = 0; b0 < ok.size(); b0 += kMaxRows) {
+        const size_t B = std::min(kMaxRows, ok.size() - b0);
+        std::vector<Seq *> seqs(B);
+        std::vector<uint32_t> tokens(B), argmax(B);
+        std::vector<size_t> offsets(B);
+        std::vector<float *> rows(B);
+        for (size_t b = 0; b < B; ++b) {
+            CoalescedCall *call = ok[b0 + b];
+            seqs[b] = call->s;
+            tokens[b] = call->token;
+            offsets[b] = call->offset;
+            rows[b] = call->logits;  // each caller's buffer, written by the device
+        }
+        const int rc = forward_batch_rows(&m, seqs.data(), tokens.data(), offsets.data(), B, rows.data(),
+                                          argmax.data());
+        const std::string err = rc != 0 ? std::string(last_error()) : std::string();
+        for (size_t b = 0; b < B; ++b) {
+            CoalescedCall *call = ok[b0 + b];
+            call->status = rc;
+            if (rc != 0) {
+                call->error = err;
+                continue;
+            }
+            if (call->argmax) *call->argmax = argmax[b];
+        }
+        if (rc == 0) {
+            m.co_batches.fetch_add(1);
+            m.co_batched_calls.fetch_add(B);
+        }
+    }
+}
+
+int coalesced_forward(Seq *s, uint32_t token, size_t offset, float *logits_out, uint32_t *argmax_out) {
+    Model &m = *s->m;
+    m.co_calls.fetch_add(1);
+    CoalescedCall me;
+    me.s = s;
+    me.token = token;
+    me.offset = offset;
+    me.logits = logits_out;
+    me.argmax = argmax_out;
+    std::unique_lock<std::mutex> lock(m.co_mutex);
+    m.co_pending.push_back(&me);
+    if (m.co_pending.size() >= m.co_last_group) m.co_cv.notify_all();  // a leader may be gathering
+    while (!me.done) {
+        if (m.co_running) {
+            m.co_cv.wait(lock);
+            continue;
+        }
+        // Lead: run everything queued (this call included). When the last
+        // group was larger, its callers are likely on their way back: give
+        // them a short window (CHEETAH_CUDA_COALESCE_WAIT_US, default 200)
+        // to join, ending as soon as they all have.
+        m.co_running = true;
+        if (m.co_pending.size() < m.co_last_group) {
+            const auto until = std::chrono::steady_clock::now() +
+                               std::chrono::microseconds(std::max(0, env_int("CHEETAH_CUDA_COALESCE_WAIT_US", 200)));
+            while (m.co_pending.size() < m.co_last_group &&
+                   m.co_cv.wait_until(lock, until) != std::cv_status::timeout) {
+            }
+        }
+        std::vector<CoalescedCall *> take;
+        take.swap(m.co_pending);
+        m.co_last_group = take.size();
+        lock.unlock();
+        run_coalesced(m, take);
+        lock.lock();
+        for (CoalescedCall *call : take) call->done = true;
+        m.co_running = false;
+        m.co_cv.notify_all();
+    }
+    lock.unlock();
+    if (me.status != 0) {
+        set_error(me.error);
+        return -1;
+    }
+    return 0;
+}
+
+// Single-token forwards go through the batcher when the model can run
+// batched steps (bf16 weights and KV cache) and CHEETAH_CUDA_COALESCE is on.
+int forward_entry(Seq *s, const uint32_t *tokens, size_t n, size_t offset, float *logits_out, uint32_t *argmax_out) {
+    if (s != nullptr && n == 1 && tokens != nullptr && s->m->gemm_prefill && env_flag("CHEETAH_CUDA_COALESCE", true)) {
+        CH_CUDA_TRY(cudaSetDevice(s->m->device));
+        return coalesced_forward(s, tokens[0], offset, logits_out, argmax_out);
+    }
+    return forward(s, tokens, n, offset, logits_out, argmax_out);
 }
 
 // `steps` greedy tokens for each of B sequences with no host round trip
@@ -2340,6 +2637,7 @@ int generate_greedy(Seq *s, uint32_t first_token, size_t offset, size_t steps, u
                    " exceeds the sequence capacity " + std::to_string(c.max_positions) + ".");
     CH_CUDA_TRY(cudaSetDevice(s->m->device));
     CH_CUDA_TRY(cudaStreamSynchronize(s->stream));
+    if (make_tail_page_private(*s) != 0) return -1;
     // Pages for every position of the run.
     const size_t first_page = s->pages.size();
     const size_t last_page = (offset + steps - 1) / s->m->page_tokens;
@@ -2507,12 +2805,23 @@ int cheetah_cuda_seq_positions(const CheetahCudaSeq *seq, size_t *positions) {
 
 int cheetah_cuda_forward(CheetahCudaSeq *seq, const uint32_t *tokens, size_t n, size_t offset,
                          float *logits_out) {
-    return cheetah::forward(reinterpret_cast<Seq *>(seq), tokens, n, offset, logits_out, nullptr);
+    return cheetah::forward_entry(reinterpret_cast<Seq *>(seq), tokens, n, offset, logits_out, nullptr);
 }
 
 int cheetah_cuda_forward_ex(CheetahCudaSeq *seq, const uint32_t *tokens, size_t n, size_t offset,
                             float *logits_out, uint32_t *argmax_out) {
-    return cheetah::forward(reinterpret_cast<Seq *>(seq), tokens, n, offset, logits_out, argmax_out);
+    return cheetah::forward_entry(reinterpret_cast<Seq *>(seq), tokens, n, offset, logits_out, argmax_out);
+}
+
+int cheetah_cuda_model_coalesce_stats(const CheetahCudaModel *model, uint64_t *calls, uint64_t *batched_calls,
+                                      uint64_t *batches) {
+    CH_REQUIRE(model != nullptr && calls != nullptr && batched_calls != nullptr && batches != nullptr,
+               "cheetah_cuda_model_coalesce_stats: null argument");
+    const Model *m = reinterpret_cast<const Model *>(model);
+    *calls = m->co_calls.load();
+    *batched_calls = m->co_batched_calls.load();
+    *batches = m->co_batches.load();
+    return 0;
 }
 
 int cheetah_cuda_forward_batch(CheetahCudaModel *model, CheetahCudaSeq *const *seqs, const uint32_t *tokens,
@@ -2544,46 +2853,20 @@ int cheetah_cuda_model_batch_stream(const CheetahCudaModel *model, void **stream
     return 0;
 }
 
-static int copy_pages(Model *m, const std::vector<int> &src, const std::vector<int> &dst, cudaStream_t stream) {
-    if (src.empty()) return 0;
-    int32_t *d_ids = nullptr;
-    CH_CUDA_TRY(cudaMalloc(&d_ids, src.size() * 2 * sizeof(int32_t)));
-    std::vector<int32_t> ids(src.begin(), src.end());
-    ids.insert(ids.end(), dst.begin(), dst.end());
-    cudaError_t err = cudaMemcpyAsync(d_ids, ids.data(), ids.size() * 4, cudaMemcpyHostToDevice, stream);
-    if (err == cudaSuccess) {
-        cheetah::copy_pages_kernel<<<4 * m->sms, 256, 0, stream>>>(
-            d_ids, d_ids + src.size(), (int)src.size(), m->k_pool, m->v_pool, m->layer_stride_bytes,
-            (int)m->cfg.num_layers, m->page_bytes);
-        err = cudaGetLastError();
-    }
-    if (err == cudaSuccess) err = cudaStreamSynchronize(stream);
-    cudaFree(d_ids);
-    CH_CUDA_TRY(err);
-    return 0;
-}
-
 int cheetah_cuda_seq_snapshot(const CheetahCudaSeq *seq, CheetahCudaSnapshot **out) {
     CH_REQUIRE(seq != nullptr && out != nullptr, "cheetah_cuda_seq_snapshot: null argument");
     Seq *s = const_cast<Seq *>(reinterpret_cast<const Seq *>(seq));
     CH_CUDA_TRY(cudaSetDevice(s->m->device));
+    CH_CUDA_TRY(cudaStreamSynchronize(s->stream));  // the captured rows are written
+    // The snapshot holds the pages of the cached positions: no copy. Whoever
+    // appends into the last (partial) page later copies it first.
     Snapshot *snap = new Snapshot();
     snap->m = s->m;
     s->m->refs.fetch_add(1);
     snap->positions = s->positions;
-    for (size_t i = 0; i < s->pages.size(); ++i) {
-        int page = s->m->alloc_page();
-        if (page < 0) {
-            delete snap;
-            cheetah::set_error("CUDA backend: KV page pool exhausted while snapshotting.");
-            return -1;
-        }
-        snap->pages.push_back(page);
-    }
-    if (copy_pages(s->m, s->pages, snap->pages, s->stream) != 0) {
-        delete snap;
-        return -1;
-    }
+    const size_t n = (s->positions + s->m->page_tokens - 1) / s->m->page_tokens;
+    snap->pages.assign(s->pages.begin(), s->pages.begin() + n);
+    s->m->retain_pages(snap->pages);
     *out = reinterpret_cast<CheetahCudaSnapshot *>(snap);
     return 0;
 }
@@ -2603,19 +2886,11 @@ int cheetah_cuda_seq_restore_prefix(CheetahCudaSeq *seq, const CheetahCudaSnapsh
     CH_CUDA_TRY(cudaStreamSynchronize(s->stream));
     s->m->release_pages(s->pages);
     s->positions = 0;
+    // The sequence shares the snapshot's pages of the kept positions.
     const size_t keep = std::min(positions, snap->positions);
     const size_t pages = (keep + s->m->page_tokens - 1) / s->m->page_tokens;
-    std::vector<int> src(snap->pages.begin(), snap->pages.begin() + pages);
-    for (size_t i = 0; i < pages; ++i) {
-        int page = s->m->alloc_page();
-        if (page < 0) {
-            s->m->release_pages(s->pages);
-            cheetah::set_error("CUDA backend: KV page pool exhausted while restoring.");
-            return -1;
-        }
-        s->pages.push_back(page);
-    }
-    if (copy_pages(s->m, src, s->pages, s->stream) != 0) return -1;
+    s->pages.assign(snap->pages.begin(), snap->pages.begin() + pages);
+    s->m->retain_pages(s->pages);
     std::vector<int32_t> table(s->pages.begin(), s->pages.end());
     if (!table.empty()) {
         CH_CUDA_TRY(cudaMemcpy(s->page_table, table.data(), table.size() * 4, cudaMemcpyHostToDevice));
@@ -2860,12 +3135,63 @@ int cheetah_cuda_op_decode_attention(const CheetahCudaDecodeAttention *a, void *
     return cheetah::launch_attention_mma(k_map, v_map, mp, (int)a->head_dim, st, false);
 }
 
+int cheetah_cuda_op_prefill_attention(const CheetahCudaPrefillAttention *a, void *stream) {
+    CH_REQUIRE(a != nullptr && a->q && a->k_pool && a->v_pool && a->page_table && a->out,
+               "cheetah_cuda_op_prefill_attention: null argument");
+    CH_REQUIRE(a->head_dim == 64 || a->head_dim == 128, "cheetah_cuda_op_prefill_attention: head_dim must be 64 or 128");
+    CH_REQUIRE(a->kv_heads > 0 && a->q_heads % a->kv_heads == 0 && a->q_heads / a->kv_heads <= (uint32_t)cheetah::kMaxGroup,
+               "cheetah_cuda_op_prefill_attention: q_heads must be a multiple of kv_heads (group <= 8)");
+    CH_REQUIRE(a->tokens > 0 && a->num_pages > 0 && a->max_pages > 0,
+               "cheetah_cuda_op_prefill_attention: empty shape");
+    CH_REQUIRE(a->page_tokens > 0 && a->page_tokens % 64 == 0,
+               "cheetah_cuda_op_prefill_attention: page_tokens must be a multiple of 64");
+    CH_REQUIRE((uint64_t)a->offset + a->tokens <= (uint64_t)a->max_pages * a->page_tokens,
+               "cheetah_cuda_op_prefill_attention: query rows past the page table");
+    CH_REQUIRE(((uintptr_t)a->q & 15) == 0 && ((uintptr_t)a->out & 15) == 0 && ((uintptr_t)a->k_pool & 15) == 0 &&
+                   ((uintptr_t)a->v_pool & 15) == 0,
+               "cheetah_cuda_op_prefill_attention: q, out and the pools must be 16-byte aligned");
+    int device = 0;
+    CH_CUDA_TRY(cudaGetDevice(&device));
+    const int sms = cheetah::sm_count(device);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const size_t T = a->tokens, QD = (size_t)a->q_heads * a->head_dim;
+    const size_t o_bytes = ((size_t)cheetah::kPrefillMaxSplits * T * QD * 4 + 255) & ~size_t(255);
+    const size_t ml_bytes = ((size_t)cheetah::kPrefillMaxSplits * T * a->q_heads * 2 * 4 + 255) & ~size_t(255);
+    uint8_t *scratch = nullptr;
+    unsigned int *tickets = nullptr;
+    if (op_scratch(device, st, o_bytes + ml_bytes, 1, &scratch, &tickets) != 0) return -1;
+    CUtensorMap q_map, k_map, v_map;
+    const unsigned long long rows = (unsigned long long)a->num_pages * a->kv_heads * a->page_tokens;
+    if (cheetah::make_bf16_tensor_map(&q_map, a->q, T, QD, cheetah::kTcRows) != 0 ||
+        cheetah::make_kv_tensor_map(&k_map, a->k_pool, rows, (int)a->head_dim) != 0 ||
+        cheetah::make_kv_tensor_map(&v_map, a->v_pool, rows, (int)a->head_dim) != 0) {
+        return -1;
+    }
+    cheetah::PrefillAttnParams ap = {};
+    ap.q = static_cast<const uint16_t *>(a->q);
+    ap.out = static_cast<uint16_t *>(a->out);
+    ap.T = (int)T;
+    ap.offset = (int)a->offset;
+    ap.q_heads = (int)a->q_heads;
+    ap.kv_heads = (int)a->kv_heads;
+    ap.page_table = a->page_table;
+    ap.max_pages = (int)a->max_pages;
+    ap.num_pages = (int)a->num_pages;
+    ap.page_tokens = (int)a->page_tokens;
+    ap.layer_row_offset = 0;
+    ap.window = (int)a->sliding_window;
+    ap.scale = 1.0f / sqrtf((float)a->head_dim);
+    ap.error = nullptr;
+    ap.part_o = reinterpret_cast<float *>(scratch);
+    ap.part_ml = reinterpret_cast<float *>(scratch + o_bytes);
+    return cheetah::launch_prefill_attention(ap, q_map, k_map, v_map, (int)a->head_dim, a->offset, sms, st, false);
+}
+
 // ---- Decode attention without allocation ----------------------------------
 // Some callers cannot let the library allocate device memory: a caller that
-// records its work into a CUDA graph (allocation is not allowed while a stream
-// is being captured), a caller that manages a fixed device-memory budget
-// itself, or a latency-critical caller that cannot absorb the device-wide
-// synchronisation cudaMalloc / cudaFree may cause. This entry point computes
+// manages a fixed device-memory budget itself, or a latency-critical caller
+// that cannot absorb the device-wide synchronisation cudaMalloc / cudaFree
+// may cause. This entry point computes
 // the same attention as cheetah_cuda_op_decode_attention, but its split-merge
 // scratch is a fixed array compiled into the library (held by every GPU that
 // loads it, until exit) instead of memory allocated on first use.

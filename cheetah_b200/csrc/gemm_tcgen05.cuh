@@ -69,6 +69,10 @@ struct PrefillGemmParams {
     const int32_t *row_pos;   // nullptr: position = offset + row (prefill)
     int table_stride;
     float *out_q_f32;         // kPgQkv: q [M][q_dim] f32 instead of bf16
+    // kPgQkv per-head RMSNorm of q / k before RoPE (qwen3, `ops.rs:1130`):
+    // f32 [head_dim] weights, nullptr = none.
+    const float *q_norm, *k_norm;
+    float eps;
     // kPgLogits: logits [M][ld_out] f32 + per-row packed argmax
     unsigned long long *argmax;
     // Split-K (gridDim.z > 1): [splits][tiles][128][BN] f32 partial tiles
@@ -458,6 +462,25 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 for (int hb = 0; hb < BN; hb += hd) {
                     const int col0 = n_tile * BN + hb;  // first output feature of this head
                     const int head = col0 / hd;
+                    // Per-head q/k norm: a first pass over the head's
+                    // accumulators (bias included) for the sum of squares.
+                    const float *nw = head < p.q_heads ? p.q_norm
+                                                       : (head < p.q_heads + p.kv_heads ? p.k_norm : nullptr);
+                    float inv = 1.0f;
+                    if (nw) {
+                        float ss = 0.0f;
+#pragma unroll 1
+                        for (int j = 0; j < hd; j += 16) {
+                            float a[16];
+                            tmem_ld16(lane_addr + hb + j, a);
+#pragma unroll
+                            for (int e = 0; e < 16; ++e) {
+                                const float v = p.bias ? __fadd_rn(a[e], p.bias[col0 + j + e]) : a[e];
+                                ss = fmaf(v, v, ss);
+                            }
+                        }
+                        inv = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(ss, (float)hd), p.eps));
+                    }
 #pragma unroll 1
                     for (int j = 0; j < half; j += 16) {
                         float a[16], b[16];
@@ -474,6 +497,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                                 a[4 * i + 2] = __fadd_rn(a[4 * i + 2], x.z); a[4 * i + 3] = __fadd_rn(a[4 * i + 3], x.w);
                                 b[4 * i] = __fadd_rn(b[4 * i], y.x); b[4 * i + 1] = __fadd_rn(b[4 * i + 1], y.y);
                                 b[4 * i + 2] = __fadd_rn(b[4 * i + 2], y.z); b[4 * i + 3] = __fadd_rn(b[4 * i + 3], y.w);
+                            }
+                        }
+                        if (nw) {
+#pragma unroll
+                            for (int e = 0; e < 16; ++e) {
+                                a[e] = __fmul_rn(a[e], __fmul_rn(inv, nw[j + e]));
+                                b[e] = __fmul_rn(b[e], __fmul_rn(inv, nw[half + j + e]));
                             }
                         }
                         if (head < p.q_heads + p.kv_heads) {

@@ -64,6 +64,9 @@ struct GemvParams {
     int splits;
     float *split_ws;
     unsigned *split_tickets;
+    // kEpiQkv for families with per-head q/k norms: the biased projections
+    // go to qk_raw [batch][rows] and `qk_norm_rope_kernel` finishes them.
+    float *qk_raw;
 };
 
 template <int NB>
@@ -169,6 +172,12 @@ __device__ __forceinline__ void epilogue_rows(const GemvParams &p, int b, int ro
         const int i = row_a - head * hd;
         float va = __fadd_rn(acc_a, p.bias ? p.bias[row_a] : 0.0f);
         float vb = __fadd_rn(acc_b, p.bias ? p.bias[row_b] : 0.0f);
+        if (p.qk_raw) {
+            float *raw = p.qk_raw + (long long)b * p.rows;
+            raw[row_a] = va;
+            raw[row_b] = vb;
+            return;
+        }
         if (head < p.q_heads + p.kv_heads) {
             // ops.rs:693-715: a' = a*cos - b*sin, b' = b*cos + a*sin
             const int pos = p.positions[b];
@@ -454,6 +463,57 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_bf16_kernel(const GemvParam
 #pragma unroll
             for (int w = 0; w < kGemvWarps; ++w) m = best_s[w][threadIdx.x] > m ? best_s[w][threadIdx.x] : m;
             atomicMax(p.argmax + threadIdx.x, m);
+        }
+    }
+}
+
+// Per-head RMSNorm of q and k (`ops.rs:1130-1152`, the qwen3 family), then
+// RoPE and the q store / paged K,V append of the kEpiQkv epilogue, over the
+// biased projections a kEpiQkv GEMV left in p.qk_raw. One warp per (head,
+// batch row): grid (q_heads + 2 kv_heads, batch), 32 threads. A null norm
+// weight leaves that head un-normalised (the reference's absent unit).
+__global__ void __launch_bounds__(32) qk_norm_rope_kernel(const GemvParams p, const float *q_norm,
+                                                          const float *k_norm) {
+    const int head = blockIdx.x, b = blockIdx.y, lane = threadIdx.x;
+    const int hd = p.head_dim, half = hd >> 1;
+    pdl_wait();  // the QKV GEMV's rows
+    pdl_launch_dependents();
+    const float *raw = p.qk_raw + (long long)b * p.rows + (long long)head * hd;
+    const bool is_q = head < p.q_heads;
+    const bool is_k = !is_q && head < p.q_heads + p.kv_heads;
+    const float *nw = is_q ? q_norm : (is_k ? k_norm : nullptr);
+    float inv = 1.0f;
+    if (nw) {
+        // rmsnorm (`ops.rs:646-652`): x * (1/sqrt(mean(x^2) + eps) * w)
+        float ss = 0.0f;
+        for (int d = lane; d < hd; d += 32) ss = fmaf(raw[d], raw[d], ss);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        inv = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(ss, (float)hd), p.eps));
+    }
+    const int pos = p.positions[b];
+    float *y = p.y + (long long)b * p.y_stride;
+    for (int i = lane; i < half; i += 32) {
+        float va = raw[i], vb = raw[i + half];
+        if (nw) {
+            va = __fmul_rn(va, __fmul_rn(inv, nw[i]));
+            vb = __fmul_rn(vb, __fmul_rn(inv, nw[i + half]));
+        }
+        if (is_q || is_k) {
+            const float c = p.rope_cos[(long long)pos * half + i];
+            const float s = p.rope_sin[(long long)pos * half + i];
+            const float ra = __fsub_rn(__fmul_rn(va, c), __fmul_rn(vb, s));
+            const float rb = __fadd_rn(__fmul_rn(vb, c), __fmul_rn(va, s));
+            va = ra;
+            vb = rb;
+        }
+        if (is_q) {
+            y[head * hd + i] = va;
+            y[head * hd + i + half] = vb;
+        } else {
+            const int kvh = is_k ? head - p.q_heads : head - p.q_heads - p.kv_heads;
+            store_kv<1>(p, b, kvh, i, va, is_k);
+            store_kv<1>(p, b, kvh, i + half, vb, is_k);
         }
     }
 }

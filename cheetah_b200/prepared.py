@@ -40,8 +40,12 @@ DTYPE_BYTES = {"BF16": 2, "F16": 2, "F32": 4, "U8": 1, "I8": 1}
 
 
 @dataclasses.dataclass(frozen=True)
-class Qwen2Shape:
-    """Qwen2-family decoder hyper-parameters (`qwen2.rs:66-82` profiles)."""
+class DecoderShape:
+    """Hyper-parameters of a dense llama-shaped decoder: Qwen2 (`qwen2.rs:66-82`
+    profiles) and the families that differ from it only by composition:
+    llama (no attention biases, `llama.rs:66-82`), mistral (a decode-time
+    sliding window, `mistral.rs:63-77`) and qwen3 (per-head q/k RMSNorm units,
+    `qwen3.rs:62-77`)."""
 
     hidden_size: int
     num_layers: int
@@ -55,6 +59,9 @@ class Qwen2Shape:
     tie_word_embeddings: bool = True
     max_position_embeddings: int = 32768
     attention_bias: bool = True
+    family: str = "qwen2"
+    sliding_window: int = 0     # written to config.json for the non-qwen2 families
+    qk_norm: bool = False       # qwen3: self_attn.{q,k}_norm.weight [head_dim] units
 
     @property
     def q_dim(self) -> int:
@@ -65,9 +72,9 @@ class Qwen2Shape:
         return self.kv_heads * self.head_dim
 
     def config_json(self) -> dict:
-        return {
-            "architectures": ["Qwen2ForCausalLM"],
-            "model_type": "qwen2",
+        cfg = {
+            "architectures": [FAMILIES[self.family]["architectures"][0]],
+            "model_type": self.family,
             "hidden_size": self.hidden_size,
             "intermediate_size": self.intermediate_size,
             "num_hidden_layers": self.num_layers,
@@ -78,28 +85,50 @@ class Qwen2Shape:
             "rope_theta": self.rope_theta,
             "rms_norm_eps": self.rms_eps,
             "tie_word_embeddings": self.tie_word_embeddings,
-            "use_sliding_window": False,
-            "sliding_window": 32768,
             "max_position_embeddings": self.max_position_embeddings,
             "hidden_act": "silu",
             "torch_dtype": "bfloat16",
         }
+        if self.family == "qwen2":
+            # Qwen2 configs carry a window the modeling never engages.
+            cfg.update(use_sliding_window=False, sliding_window=32768)
+        elif self.sliding_window:
+            cfg["sliding_window"] = self.sliding_window  # `use_sliding_window` absent = on
+        return cfg
+
+
+Qwen2Shape = DecoderShape
 
 
 # Qwen2-0.5B and Qwen2-7B architectures (qwen2.rs:72-74 profiles).
-QWEN2_0_5B = Qwen2Shape(896, 24, 14, 2, 64, 4864, 151936)
-QWEN2_7B = Qwen2Shape(3584, 28, 28, 4, 128, 18944, 152064, tie_word_embeddings=False)
+QWEN2_0_5B = DecoderShape(896, 24, 14, 2, 64, 4864, 151936)
+QWEN2_7B = DecoderShape(3584, 28, 28, 4, 128, 18944, 152064, tie_word_embeddings=False)
 # Small shapes with the real head geometry (7:1 GQA, head_dim 64 / 128) for
 # parity tests the CPU oracle finishes in seconds.
-TINY = Qwen2Shape(256, 2, 14, 2, 64, 512, 1000, max_position_embeddings=4096)
-TINY_7B_HEADS = Qwen2Shape(512, 2, 28, 4, 128, 768, 1024, tie_word_embeddings=False,
-                           max_position_embeddings=4096)
-TINY_WIDE_MLP = Qwen2Shape(256, 2, 14, 2, 64, 16384, 1000, max_position_embeddings=4096)
-TINY_15B_HEADS = Qwen2Shape(1536, 2, 12, 2, 128, 2048, 1024, tie_word_embeddings=False,
-                            max_position_embeddings=4096)
+TINY = DecoderShape(256, 2, 14, 2, 64, 512, 1000, max_position_embeddings=4096)
+TINY_7B_HEADS = DecoderShape(512, 2, 28, 4, 128, 768, 1024, tie_word_embeddings=False,
+                             max_position_embeddings=4096)
+TINY_WIDE_MLP = DecoderShape(256, 2, 14, 2, 64, 16384, 1000, max_position_embeddings=4096)
+TINY_15B_HEADS = DecoderShape(1536, 2, 12, 2, 128, 2048, 1024, tie_word_embeddings=False,
+                              max_position_embeddings=4096)
+# The other dense families at small sizes: llama (multi-head, no biases, rope
+# theta 1e4, eps 1e-5, untied), mistral (4:1 GQA, a 48-token window so short
+# prompts engage it), qwen3 (head_dim 128 > hidden / heads, q/k norms, tied).
+TINY_LLAMA = DecoderShape(256, 2, 4, 4, 64, 512, 1000, rope_theta=10_000.0, rms_eps=1e-5,
+                          tie_word_embeddings=False, max_position_embeddings=4096,
+                          attention_bias=False, family="llama")
+TINY_MISTRAL = DecoderShape(256, 2, 8, 2, 64, 512, 1000, rope_theta=10_000.0, rms_eps=1e-5,
+                            tie_word_embeddings=False, max_position_embeddings=4096,
+                            attention_bias=False, family="mistral", sliding_window=48)
+TINY_QWEN3 = DecoderShape(256, 2, 8, 4, 128, 512, 1000, max_position_embeddings=4096,
+                          attention_bias=False, family="qwen3", qk_norm=True)
+# Llama-3.2-1B's architecture (`llama.rs:72` profile; tied head as published).
+LLAMA_1B = DecoderShape(2048, 16, 32, 8, 64, 8192, 128256, rope_theta=500_000.0, rms_eps=1e-5,
+                        tie_word_embeddings=True, max_position_embeddings=4096,
+                        attention_bias=False, family="llama")
 
 
-def tensor_specs(shape: Qwen2Shape) -> List[Tuple[str, Tuple[int, ...]]]:
+def tensor_specs(shape: DecoderShape) -> List[Tuple[str, Tuple[int, ...]]]:
     """Every HF-layout tensor of a Qwen2 checkpoint, sorted by name."""
     specs: List[Tuple[str, Tuple[int, ...]]] = [
         ("model.embed_tokens.weight", (shape.vocab_size, shape.hidden_size)),
@@ -127,6 +156,11 @@ def tensor_specs(shape: Qwen2Shape) -> List[Tuple[str, Tuple[int, ...]]]:
                 (p + "self_attn.k_proj.bias", (kv,)),
                 (p + "self_attn.v_proj.bias", (kv,)),
             ]
+        if shape.qk_norm:
+            specs += [
+                (p + "self_attn.q_norm.weight", (shape.head_dim,)),
+                (p + "self_attn.k_norm.weight", (shape.head_dim,)),
+            ]
     specs.sort(key=lambda item: item[0])
     return specs
 
@@ -143,11 +177,19 @@ def bf16_bits_to_f32(bits: np.ndarray) -> np.ndarray:
     return (np.asarray(bits, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
 
 
-def generate_tensors(shape: Qwen2Shape, seed: int = 0, std: float = 0.02,
+# qwen3's per-head q/k norm weights are drawn N(0, 1): with N(0, 0.02) the
+# normalised q and k would be ~0.02 per element and every attention softmax
+# near-uniform, so the norms (and RoPE after them) would barely reach the
+# logits a parity test compares.
+QK_NORM_SUFFIXES = ("self_attn.q_norm.weight", "self_attn.k_norm.weight")
+QK_NORM_STD = 1.0
+
+
+def generate_tensors(shape: DecoderShape, seed: int = 0, std: float = 0.02,
                      chunk: int = 1 << 24, threads: Optional[int] = None
                      ) -> Iterator[Tuple[str, Tuple[int, ...], np.ndarray]]:
     """Seeded random-init weights: N(0, std) bf16 for every tensor (norms and
-    biases included), yielded in sorted-name order. Tensor i's chunk j of
+    biases included; q/k norms N(0, QK_NORM_STD)), yielded in sorted-name order. Tensor i's chunk j of
     `chunk` values is drawn from its own generator, seeded by child (i, j) of
     `SeedSequence(seed)`, so the values do not depend on how many threads
     draw them; the chunks are drawn on a thread pool (numpy releases the GIL
@@ -168,7 +210,7 @@ def generate_tensors(shape: Qwen2Shape, seed: int = 0, std: float = 0.02,
     def draw(job):
         i, start, n, ss = job
         values = np.random.default_rng(ss).standard_normal(n, dtype=np.float32)
-        values *= np.float32(std)
+        values *= np.float32(std if not specs[i][0].endswith(QK_NORM_SUFFIXES) else QK_NORM_STD)
         outs[i][start:start + n] = f32_to_bf16_bits(values)
 
     with ThreadPoolExecutor(max_workers=threads or min(32, os.cpu_count() or 1)) as pool:
@@ -244,7 +286,7 @@ def write_safetensors(path: Path, tensors: Sequence[Tuple[str, str, Tuple[int, .
     return offsets
 
 
-def write_prepared(dst: os.PathLike, shape: Qwen2Shape, seed: int = 0,
+def write_prepared(dst: os.PathLike, shape: DecoderShape, seed: int = 0,
                    tensors: Optional[Iterator[Tuple[str, Tuple[int, ...], np.ndarray]]] = None) -> Path:
     """Write a seeded synthetic Qwen2 model directly in the prepared layout."""
     dst = Path(dst)
@@ -274,7 +316,7 @@ def write_prepared(dst: os.PathLike, shape: Qwen2Shape, seed: int = 0,
     return dst
 
 
-def write_hf_source(dst: os.PathLike, shape: Qwen2Shape, seed: int = 0) -> Path:
+def write_hf_source(dst: os.PathLike, shape: DecoderShape, seed: int = 0) -> Path:
     """Seeded synthetic checkpoint in the Hugging Face layout (one
     model.safetensors + config.json + a minimal tokenizer.json), the input
     `cheetah init` converts into the prepared layout."""
@@ -369,51 +411,152 @@ class PreparedModel:
         return max((u.layer_id for u in self.units.values()), default=0)
 
 
-# Qwen2 family constants (qwen2.rs:66-82).
-QWEN2_FAMILY = {
-    "rope_theta": 1_000_000.0,
-    "rms_norm_eps": 1e-6,
-    "tie_word_embeddings": True,
-    "profiles": [(896, 151936, 14, 2, 64), (1536, 151936, 12, 2, 128), (3584, 152064, 28, 4, 128)],
+# Family constants of the dense registrations this backend serves
+# (`registrations/qwen2.rs:63-82`, `qwen3.rs:62-77`, `llama.rs:66-82`,
+# `mistral.rs:63-77`): the architecture names that select them
+# (`registry.rs:328`), rope theta, RMSNorm epsilon, tied head,
+# (hidden, vocab, q heads, kv heads, head_dim) profiles, context cap.
+FAMILIES = {
+    "qwen2": {
+        "architectures": ("Qwen2ForCausalLM", "qwen2"),
+        "rope_theta": 1_000_000.0, "rms_norm_eps": 1e-6, "tie_word_embeddings": True,
+        "profiles": [(896, 151936, 14, 2, 64), (1536, 151936, 12, 2, 128), (3584, 152064, 28, 4, 128)],
+        "max_position_embeddings": None,
+    },
+    "qwen3": {
+        "architectures": ("Qwen3ForCausalLM", "qwen3"),
+        "rope_theta": 1_000_000.0, "rms_norm_eps": 1e-6, "tie_word_embeddings": True,
+        "profiles": [(8192, 32768, 64, 8, 128)],
+        "max_position_embeddings": None,
+    },
+    "llama": {
+        "architectures": ("LlamaForCausalLM", "llama"),
+        "rope_theta": 10_000.0, "rms_norm_eps": 1e-5, "tie_word_embeddings": False,
+        "profiles": [(2048, 128256, 32, 8, 64), (3072, 128256, 24, 8, 128),
+                     (4096, 128256, 32, 8, 128), (4096, 32000, 32, 32, 128)],
+        "max_position_embeddings": 4096,
+    },
+    "mistral": {
+        "architectures": ("MistralForCausalLM", "mistral"),
+        "rope_theta": 10_000.0, "rms_norm_eps": 1e-5, "tie_word_embeddings": False,
+        "profiles": [(4096, 32000, 32, 8, 128), (4096, 32768, 32, 8, 128)],
+        "max_position_embeddings": 32768,
+    },
+}
+QWEN2_FAMILY = FAMILIES["qwen2"]
+# A config that names no architecture resolves against llama-shaped defaults
+# (`decoder.rs:283-296`).
+DEFAULT_FAMILY = {
+    "architectures": (), "rope_theta": 1_000_000.0, "rms_norm_eps": 1e-6,
+    "tie_word_embeddings": False, "profiles": [], "max_position_embeddings": None,
 }
 
 
+def config_architecture(raw: dict) -> Optional[str]:
+    """First `architectures` entry, else `model_type` (`chat/mod.rs:62-67`)."""
+    archs = raw.get("architectures")
+    if isinstance(archs, list) and archs and isinstance(archs[0], str):
+        return archs[0]
+    mt = raw.get("model_type")
+    return mt if isinstance(mt, str) else None
+
+
+def family_for(raw: dict) -> Tuple[Optional[str], dict]:
+    """(family name, constants) for a config.json; raises for an
+    architecture outside the dense families this backend serves (gemma's
+    offset norms, phi's fused QKV / LayerNorm / parallel residual, mixtral's
+    experts are other compositions)."""
+    arch = config_architecture(raw)
+    if arch is None:
+        return None, DEFAULT_FAMILY
+    for name, fam in FAMILIES.items():
+        if arch in fam["architectures"]:
+            return name, fam
+    raise ValueError(f"CUDA backend: architecture '{arch}' is not served "
+                     f"(dense families: {', '.join(sorted(FAMILIES))}).")
+
+
+def _field_u(raw: dict, name: str) -> Optional[int]:
+    """`Value::as_u64`: a non-negative JSON integer, else None."""
+    v = raw.get(name)
+    return v if isinstance(v, int) and not isinstance(v, bool) and v >= 0 else None
+
+
+def _field_f(raw: dict, name: str) -> Optional[float]:
+    """`Value::as_f64`: any JSON number, else None."""
+    v = raw.get(name)
+    return float(v) if isinstance(v, (int, float)) and not isinstance(v, bool) else None
+
+
+def _field_b(raw: dict, name: str) -> Optional[bool]:
+    v = raw.get(name)
+    return v if isinstance(v, bool) else None
+
+
 def resolve_config(model: PreparedModel, max_positions: Optional[int] = None) -> dict:
-    """Qwen2 subset of `DecoderConfig::resolve` (`decoder.rs:260-486`):
+    """The dense subset of `DecoderConfig::resolve` (`decoder.rs:260-486`):
     config.json first, then the units manifest's shapes, then the family
-    constants. Returns the fields of `CheetahCudaConfig`."""
+    constants. Returns the fields of `CheetahCudaConfig`. Compositions the
+    CUDA backend does not build (routed experts, partial rotary, GELU
+    feed-forward) raise instead of resolving to a wrong model."""
     raw = model.raw_config
+    _, fam = family_for(raw)
     embed = model.units.get("model.embed_tokens.weight")
-    hidden = raw.get("hidden_size") or (embed.shape[1] if embed else None)
-    vocab = raw.get("vocab_size") or (embed.shape[0] if embed else None)
-    layers = raw.get("num_hidden_layers") or (model.max_layer_id() + 1)
-    profile = next((p for p in QWEN2_FAMILY["profiles"] if p[0] == hidden), None)
-    q_heads = raw.get("num_attention_heads") or (profile[2] if profile else None)
-    kv_heads = raw.get("num_key_value_heads") or (profile[3] if profile else q_heads)
-    head_dim = raw.get("head_dim") or (hidden // q_heads if hidden and q_heads else None)
+    if embed is None or len(embed.shape) != 2:
+        raise ValueError("Native backend: units manifest has no embedding tensor.")
+    pick = lambda v, d: d if v is None else v  # noqa: E731  (`unwrap_or`)
+    hidden = pick(_field_u(raw, "hidden_size"), embed.shape[1])
+    vocab = pick(_field_u(raw, "vocab_size"), embed.shape[0])
+    layers = pick(_field_u(raw, "num_hidden_layers"), max(model.max_layer_id() + 1, 1))
+    q_unit = model.units.get("model.layers.0.self_attn.q_proj.weight")
+    k_unit = model.units.get("model.layers.0.self_attn.k_proj.weight")
+    if q_unit is None or k_unit is None:
+        raise ValueError("Native backend: units manifest has no q_proj / k_proj tensor.")
+    q_out, k_out = q_unit.shape[0], k_unit.shape[0]
     gate = model.units.get("model.layers.0.mlp.gate_proj.weight")
-    inter = raw.get("intermediate_size") or (gate.shape[0] if gate else None)
-    if None in (hidden, vocab, q_heads, kv_heads, head_dim, inter):
-        raise ValueError("Native backend: could not resolve the decoder configuration.")
-    tie = raw.get("tie_word_embeddings", QWEN2_FAMILY["tie_word_embeddings"])
-    if "lm_head.weight" in model.units and "tie_word_embeddings" not in raw:
-        tie = False
-    window = 0
-    if raw.get("use_sliding_window", False) and raw.get("sliding_window"):
-        window = int(raw["sliding_window"])
-    max_pos = max_positions or int(raw.get("max_position_embeddings", 32768))
+    inter = pick(_field_u(raw, "intermediate_size"), gate.shape[0] if gate else 0)
+    if not inter:
+        raise ValueError("Native backend: cannot resolve the intermediate size from config.json "
+                         "or the units manifest.")
+    if (_field_u(raw, "num_local_experts") or 0) > 0:
+        raise ValueError("CUDA backend: routed-expert (sparse) feed-forward layers are not served.")
+    window = (_field_u(raw, "sliding_window") or 0) if pick(_field_b(raw, "use_sliding_window"), True) else 0
+    profile = next(((q, kv, hd) for h, v, q, kv, hd in fam["profiles"] if h == hidden and v == vocab), None)
+    q_heads = _field_u(raw, "num_attention_heads")
+    if q_heads is not None:
+        head_dim = pick(_field_u(raw, "head_dim"), profile[2] if profile else q_out // max(q_heads, 1))
+        kv_heads = _field_u(raw, "num_key_value_heads")
+        if kv_heads is None:
+            kv_heads = k_out // head_dim if head_dim and k_out % head_dim == 0 else q_heads
+    elif profile is not None:
+        q_heads, kv_heads, head_dim = profile
+    else:
+        raise ValueError(f"Native backend: cannot determine the attention head layout for hidden size "
+                         f"{hidden}; provide config.json or extend the family profiles.")
+    factor = pick(_field_f(raw, "partial_rotary_factor"), 1.0)
+    if factor < 1.0:
+        raise ValueError("CUDA backend: partial rotary embeddings are not served.")
+    if raw.get("hidden_act") in ("gelu", "gelu_new", "gelu_pytorch_tanh"):
+        raise ValueError("CUDA backend: GELU feed-forward layers are not served.")
+    tie = pick(_field_b(raw, "tie_word_embeddings"), fam["tie_word_embeddings"])
+    if max_positions is None:
+        max_positions = pick(_field_u(raw, "max_position_embeddings"), 32768)
+        if fam["max_position_embeddings"]:
+            max_positions = min(max_positions, fam["max_position_embeddings"])
     return {
         "hidden_size": int(hidden), "num_layers": int(layers), "q_heads": int(q_heads),
         "kv_heads": int(kv_heads), "head_dim": int(head_dim), "rotary_dim": int(head_dim),
         "intermediate_size": int(inter), "vocab_size": int(vocab),
-        "rms_eps": float(raw.get("rms_norm_eps", QWEN2_FAMILY["rms_norm_eps"])),
-        "rope_theta": float(raw.get("rope_theta", QWEN2_FAMILY["rope_theta"])),
-        "tie_word_embeddings": 1 if tie else 0, "sliding_window": window,
-        "max_positions": int(max_pos),
+        "rms_eps": float(pick(_field_f(raw, "rms_norm_eps"), fam["rms_norm_eps"])),
+        "rope_theta": float(pick(_field_f(raw, "rope_theta"), fam["rope_theta"])),
+        "tie_word_embeddings": 1 if tie else 0, "sliding_window": int(window),
+        "max_positions": int(max_positions),
     }
 
 
-SHAPES = {"qwen2-0.5b": QWEN2_0_5B, "qwen2-7b": QWEN2_7B, "tiny": TINY, "tiny-7b-heads": TINY_7B_HEADS}
+SHAPES = {"qwen2-0.5b": QWEN2_0_5B, "qwen2-7b": QWEN2_7B, "tiny": TINY, "tiny-7b-heads": TINY_7B_HEADS,
+          "tiny-llama": TINY_LLAMA, "tiny-mistral": TINY_MISTRAL, "tiny-qwen3": TINY_QWEN3,
+          "llama-1b": LLAMA_1B}
 
 
 def cached_synthetic_path(name: str, seed: int = 0, root: Optional[os.PathLike] = None) -> Path:

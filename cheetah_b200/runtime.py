@@ -65,6 +65,16 @@ class DecodeAttentionArgs(C.Structure):
     ]
 
 
+class PrefillAttentionArgs(C.Structure):
+    _fields_ = [
+        ("q", C.c_void_p), ("k_pool", C.c_void_p), ("v_pool", C.c_void_p),
+        ("page_table", C.c_void_p), ("max_pages", C.c_uint32), ("num_pages", C.c_uint32),
+        ("page_tokens", C.c_uint32), ("tokens", C.c_uint32), ("offset", C.c_uint32),
+        ("q_heads", C.c_uint32), ("kv_heads", C.c_uint32), ("head_dim", C.c_uint32),
+        ("sliding_window", C.c_uint32), ("out", C.c_void_p),
+    ]
+
+
 # Every symbol include/cheetah_cuda.h declares, with its ctypes signature.
 _P, _S, _I = C.c_void_p, C.c_size_t, C.c_int
 SIGNATURES = {
@@ -80,6 +90,8 @@ SIGNATURES = {
     "cheetah_cuda_seq_positions": (_I, [_P, C.POINTER(_S)]),
     "cheetah_cuda_forward": (_I, [_P, _P, _S, _S, _P]),
     "cheetah_cuda_forward_ex": (_I, [_P, _P, _S, _S, _P, _P]),
+    "cheetah_cuda_model_coalesce_stats": (_I, [_P, C.POINTER(C.c_uint64), C.POINTER(C.c_uint64),
+                                                C.POINTER(C.c_uint64)]),
     "cheetah_cuda_forward_batch": (_I, [_P, _P, _P, _P, _S, _P, _P]),
     "cheetah_cuda_forward_batch_greedy": (_I, [_P, _P, _P, _P, _S, _S, _P]),
     "cheetah_cuda_generate_greedy": (_I, [_P, C.c_uint32, _S, _S, _P]),
@@ -93,6 +105,7 @@ SIGNATURES = {
     "cheetah_cuda_op_gemv_bf16": (_I, [_P, _S, _S, _P, _S, _P, _P]),
     "cheetah_cuda_op_decode_attention": (_I, [C.POINTER(DecodeAttentionArgs), _P]),
     "cheetah_cuda_op_decode_attention_noalloc": (_I, [C.POINTER(DecodeAttentionArgs), _P]),
+    "cheetah_cuda_op_prefill_attention": (_I, [C.POINTER(PrefillAttentionArgs), _P]),
     "cheetah_cuda_quant_buffer_bytes": (_I, [C.c_char_p, _S, _S, C.POINTER(_S)]),
     "cheetah_cuda_op_quantize_q8": (_I, [_P, _S, _S, _P, _P]),
     "cheetah_cuda_op_quantize_q4": (_I, [_P, _S, _S, _P, _P]),
@@ -193,6 +206,13 @@ class CudaModel:
         _check(lib().cheetah_cuda_forward_batch(self._h, handles, _ptr(t), _ptr(o), B,
                                                 _ptr(logits) if want_logits else None, _ptr(am)))
         return (am, logits) if want_logits else am
+
+    def coalesce_stats(self) -> dict:
+        """Counters of the batcher behind `forward`: single-token calls,
+        calls that ran inside batched steps, batched steps."""
+        a, b, c = C.c_uint64(0), C.c_uint64(0), C.c_uint64(0)
+        _check(lib().cheetah_cuda_model_coalesce_stats(self._h, C.byref(a), C.byref(b), C.byref(c)))
+        return {"calls": a.value, "batched_calls": b.value, "batches": c.value}
 
     def batch_stream_handle(self) -> int:
         """The stream batched calls run on (0 before the first batched call)."""
@@ -389,4 +409,26 @@ def decode_attention(q, k_pool, v_pool, page_table, seq_lens, max_seq_len: int,
         B, qh, kvh, D, sliding_window, out.data_ptr())
     fn = lib().cheetah_cuda_op_decode_attention_noalloc if noalloc else lib().cheetah_cuda_op_decode_attention
     _check(fn(C.byref(args), _stream_ptr(stream)))
+    return out
+
+
+def prefill_attention(q, k_pool, v_pool, page_table, offset: int, sliding_window: int = 0,
+                      out=None, stream=None):
+    """Causal attention of a prefill chunk (`ops.rs:1357-1421` per query row).
+
+    q [T, q_heads, D] bf16 (RoPE applied) for positions offset .. offset+T-1;
+    k_pool/v_pool [pages, kv_heads, page_tokens, D] bf16 holding positions
+    0 .. offset+T-1 of the sequence; page_table [max_pages] int32.
+    Returns out [T, q_heads, D] bf16."""
+    import torch
+    T, qh, D = q.shape
+    pages, kvh, pt, D2 = k_pool.shape
+    assert D == D2 and v_pool.shape == k_pool.shape and page_table.dtype == torch.int32
+    assert q.dtype == torch.bfloat16 and k_pool.dtype == torch.bfloat16 and q.is_contiguous()
+    if out is None:
+        out = torch.empty_like(q)
+    args = PrefillAttentionArgs(q.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(), page_table.data_ptr(),
+                                page_table.numel(), pages, pt, T, offset, qh, kvh, D, sliding_window,
+                                out.data_ptr())
+    _check(lib().cheetah_cuda_op_prefill_attention(C.byref(args), _stream_ptr(stream)))
     return out

@@ -117,6 +117,21 @@ CHEETAH_CUDA_API int cheetah_cuda_forward(CheetahCudaSeq *seq, const uint32_t *t
 CHEETAH_CUDA_API int cheetah_cuda_forward_ex(CheetahCudaSeq *seq, const uint32_t *tokens, size_t n,
                             size_t offset, float *logits_out, uint32_t *argmax_out);
 
+/* Continuous batching behind cheetah_cuda_forward / _ex. Each concurrent
+ * generation owns a sequence of one shared model (the clone of the
+ * reference's per-generation `ModelForward`, `engine.rs:1872-1876`) and calls
+ * forward from its own thread. Single-token calls (n == 1) that arrive while
+ * a step runs wait and run together as the next batched step: one pass over
+ * the weights for all of them, each with its own pages, results and errors
+ * (an invalid call fails alone). A lone caller runs at once. Groups below
+ * CHEETAH_CUDA_COALESCE_MIN calls (default 3) run one at a time on the
+ * single-sequence path; CHEETAH_CUDA_COALESCE=0 switches batching off. Needs
+ * bf16 weights and a bf16 KV cache (other models run every call alone).
+ * Counters: single-token calls seen, calls that ran in batched steps, and
+ * batched steps run. */
+CHEETAH_CUDA_API int cheetah_cuda_model_coalesce_stats(const CheetahCudaModel *model, uint64_t *calls,
+                                                       uint64_t *batched_calls, uint64_t *batches);
+
 /* One decode token for each of `batch` (1..128) sequences of `model`: seqs[b]
  * consumes tokens[b] at position offsets[b] (= its cached position count).
  * The batch shares one pass over the weights (tensor-core GEMMs); attention
@@ -158,7 +173,12 @@ CHEETAH_CUDA_API int cheetah_cuda_seq_stream(const CheetahCudaSeq *seq, void **s
 CHEETAH_CUDA_API int cheetah_cuda_model_batch_stream(const CheetahCudaModel *model, void **stream);
 
 /* `ModelForward::kv_snapshot` / `restore_kv_prefix` (`registry.rs:68-79`,
- * `ops.rs:1575-1607`): a device-resident copy of the sequence's KV pages. */
+ * `ops.rs:1575-1607`) without copying: a snapshot holds a reference on each
+ * KV page of the cached positions, and a restored sequence references the
+ * snapshot's pages. Shared pages are never written: the first append into a
+ * shared partial page copies that one page (copy on write), so the source
+ * sequence, the snapshot and every restored sequence stay independent.
+ * Pages return to the pool when their last holder lets go. */
 CHEETAH_CUDA_API int cheetah_cuda_seq_snapshot(const CheetahCudaSeq *seq, CheetahCudaSnapshot **out);
 CHEETAH_CUDA_API int cheetah_cuda_snapshot_positions(const CheetahCudaSnapshot *snapshot, size_t *positions);
 CHEETAH_CUDA_API int cheetah_cuda_seq_restore_prefix(CheetahCudaSeq *seq, const CheetahCudaSnapshot *snapshot,
@@ -223,6 +243,31 @@ typedef struct CheetahCudaDecodeAttention {
     float *out;                /* [batch][q_heads][head_dim] */
 } CheetahCudaDecodeAttention;
 CHEETAH_CUDA_API int cheetah_cuda_op_decode_attention(const CheetahCudaDecodeAttention *args, void *stream);
+
+/* Causal attention of a prefill chunk: query rows offset .. offset+tokens-1
+ * of one sequence, each over its cached keys up to and including its own
+ * position (less the sliding window), over a paged bf16 pool that already
+ * holds those rows' K/V. Replaces `OpsToolbox::attention` (`ops.rs:1357-1421`)
+ * as the per-row loop of `forward_layer_chunk` (`qwen2.rs:314-343`) calls it.
+ * Tensor cores for head_dim 64 (tcgen05) and 128. Asynchronous on `stream`;
+ * split scratch is allocated on first use per (device, stream). */
+typedef struct CheetahCudaPrefillAttention {
+    const void *q;             /* bf16 [tokens][q_heads][head_dim], RoPE applied */
+    const void *k_pool;        /* bf16 [num_pages][kv_heads][page_tokens][head_dim] */
+    const void *v_pool;        /* same layout as k_pool */
+    const int32_t *page_table; /* [max_pages] the sequence's page ids */
+    uint32_t max_pages;
+    uint32_t num_pages;        /* pages in the pool (bounds check) */
+    uint32_t page_tokens;      /* a multiple of 64 */
+    uint32_t tokens;           /* query rows */
+    uint32_t offset;           /* absolute position of query row 0 */
+    uint32_t q_heads;
+    uint32_t kv_heads;
+    uint32_t head_dim;         /* 64 or 128 */
+    uint32_t sliding_window;   /* 0 = full */
+    void *out;                 /* bf16 [tokens][q_heads][head_dim] */
+} CheetahCudaPrefillAttention;
+CHEETAH_CUDA_API int cheetah_cuda_op_prefill_attention(const CheetahCudaPrefillAttention *args, void *stream);
 
 /* Decode attention for callers that cannot let the library allocate device
  * memory — e.g. a host that runs a fixed device-memory budget of its own and

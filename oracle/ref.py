@@ -32,7 +32,8 @@ def build() -> Path:
 def lib() -> C.CDLL:
     global _lib
     if _lib is None:
-        if not LIB_PATH.exists():
+        sources = [HERE / "ref_cpu.cpp", HERE / "ref_cpu.h"]
+        if not LIB_PATH.exists() or any(f.stat().st_mtime > LIB_PATH.stat().st_mtime for f in sources):
             build()
         _lib = C.CDLL(str(LIB_PATH))
         _declare(_lib)

@@ -742,6 +742,15 @@ struct OracleModel {
         for (size_t i = 0; i < n; ++i) values[i] += scalar_at(b->data, i, b->dtype);
     }
 
+    // ops.rs:1130-1152 qk_norm: per-head RMSNorm of q or k against
+    // {unit}.weight (qwen3); a no-op when the unit is absent.
+    void qk_norm(float *values, size_t heads, const std::string &unit) const {
+        const OracleUnitRef *w = find(unit + ".weight");
+        if (w == nullptr || w->bytes == 0) return;
+        for (size_t head = 0; head < heads; ++head)
+            rmsnorm_impl(values + head * cfg.head_dim, cfg.head_dim, w->data, w->dtype, cfg.rms_eps);
+    }
+
     // ops.rs:1180-1237 linear (quantised buffer if prepared).
     bool linear(const std::string &unit, size_t rows, size_t cols, const float *x, float *y) const {
         auto qit = quant.find(unit);
@@ -813,6 +822,9 @@ struct OracleModel {
         v.assign(kd, 0.0f);
         if (!linear(prefix + "self_attn.v_proj.weight", kd, cfg.hidden_size, normed.data(), v.data())) return false;
         add_bias(v.data(), kd, prefix + "self_attn.v_proj");
+        // qwen3.rs:505-528: per-head q/k norms between the bias and rope.
+        qk_norm(q.data(), cfg.q_heads, prefix + "self_attn.q_norm");
+        qk_norm(k.data(), cfg.kv_heads, prefix + "self_attn.k_norm");
         rope_heads_impl(q.data(), cfg.q_heads, cfg.head_dim, cfg.rotary_dim, position, cfg.rope_theta);
         rope_heads_impl(k.data(), cfg.kv_heads, cfg.head_dim, cfg.rotary_dim, position, cfg.rope_theta);
         cache_append(layer, k.data(), v.data());
@@ -878,6 +890,11 @@ struct OracleModel {
             add_bias(c_q.data() + r * qd, qd, prefix + "self_attn.q_proj");
             add_bias(c_k.data() + r * kd, kd, prefix + "self_attn.k_proj");
             add_bias(c_v.data() + r * kd, kd, prefix + "self_attn.v_proj");
+        }
+        // qwen3.rs:301-318: per-row q/k norms after the bias adds.
+        for (size_t r = 0; r < rows; ++r) {
+            qk_norm(c_q.data() + r * qd, cfg.q_heads, prefix + "self_attn.q_norm");
+            qk_norm(c_k.data() + r * kd, cfg.kv_heads, prefix + "self_attn.k_norm");
         }
         c_attn_out.assign(rows * qd, 0.0f);
         for (size_t r = 0; r < rows; ++r) {

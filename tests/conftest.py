@@ -57,3 +57,18 @@ def tinywide_prepared(tmp_path_factory):
     root = tmp_path_factory.mktemp("tiny_qwen2_widemlp")
     write_prepared(root, TINY_WIDE_MLP, seed=0)
     return root
+
+
+FAMILY_SHAPES = ("tiny-llama", "tiny-mistral", "tiny-qwen3")
+
+
+@pytest.fixture(scope="session", params=FAMILY_SHAPES)
+def family_prepared(request, tmp_path_factory):
+    """Seeded synthetic models of the other dense families: llama (no
+    biases, multi-head), mistral (sliding window 48) and qwen3 (per-head q/k
+    norms, head_dim 128)."""
+    from cheetah_b200.prepared import SHAPES, write_prepared
+
+    root = tmp_path_factory.mktemp(request.param.replace("-", "_"))
+    write_prepared(root, SHAPES[request.param], seed=0)
+    return root

@@ -132,3 +132,75 @@ def test_chained_greedy_batch_errors(tiny_prepared):
     assert a.positions() == 3
     out = model.forward_batch_greedy([a], [4], [3], 61)
     assert out.shape == (1, 61) and a.positions() == 64
+
+
+def test_concurrent_clone_forwards_are_batched_and_match_oracle(tiny_prepared, monkeypatch):
+    """The batcher behind `forward`: eight threads, each owning a clone (a
+    sequence of the one model), decode concurrently through the plain
+    single-sequence call. Calls that meet while a step runs go out together
+    as batched steps; every thread's logits stay within tolerance of the
+    oracle and of the same clones run serially with batching off."""
+    import threading
+    from cheetah_b200 import runtime as R
+    from tests.greedy import check_greedy, reference_choice
+    monkeypatch.setenv("CHEETAH_CUDA_COALESCE_MIN", "2")
+    pm = PreparedModel(tiny_prepared)
+    cfg = resolve_config(pm)
+    model = R.CudaModel(tiny_prepared, max_positions=1024)
+    rng = np.random.default_rng(41)
+    prompts = [rng.integers(0, cfg["vocab_size"], n).astype(np.uint32) for n in (3, 40, 64, 65, 100, 7, 130, 20)]
+    steps = 10
+
+    def run(concurrent):
+        monkeypatch.setenv("CHEETAH_CUDA_COALESCE", "1" if concurrent else "0")
+        seqs = [model.new_sequence() for _ in prompts]
+        firsts = [reference_choice(s.forward(p, 0)) for s, p in zip(seqs, prompts)]
+        logs = [[] for _ in prompts]
+        barrier = threading.Barrier(len(prompts)) if concurrent else None
+        errors = []
+
+        def worker(i):
+            try:
+                tok, pos = firsts[i], len(prompts[i])
+                for _ in range(steps):
+                    if barrier:
+                        barrier.wait()
+                    logits = np.empty(cfg["vocab_size"], np.float32)
+                    am = seqs[i].forward_greedy([tok], pos, logits_out=logits)
+                    logs[i].append((tok, pos, logits, am))
+                    tok, pos = reference_choice(logits), pos + 1
+            except Exception as e:  # noqa: BLE001 - reported below
+                errors.append(e)
+                if barrier:
+                    barrier.abort()
+
+        if not concurrent:  # serial calls, one sequence after another
+            for i in range(len(prompts)):
+                worker(i)
+        else:
+            threads = [threading.Thread(target=worker, args=(i,)) for i in range(len(prompts))]
+            for t in threads:
+                t.start()
+            for t in threads:
+                t.join(timeout=120)
+        assert not errors, errors
+        return logs
+
+    before = model.coalesce_stats()
+    together = run(True)
+    stats = model.coalesce_stats()
+    assert stats["calls"] - before["calls"] == len(prompts) * steps
+    assert stats["batched_calls"] - before["batched_calls"] > len(prompts) * steps // 2, stats
+    alone = run(False)
+    for i, prompt in enumerate(prompts):
+        ref = O.OracleModel(pm, cfg)
+        ref.forward(prompt, 0)
+        for (tok, pos, logits, am), (tok2, pos2, logits2, _) in zip(together[i], alone[i]):
+            want = ref.forward([tok], pos)
+            assert np.abs(logits - want).max() < 2e-3, (i, pos)
+            check_greedy(am, want, 2e-3, f"sequence {i} position {pos}")
+            if (tok2, pos2) == (tok, pos):
+                assert np.abs(logits - logits2).max() < 2e-3, (i, pos)
+            else:
+                break  # a near-tie sent the serial run down another path
+    model.close()

@@ -139,3 +139,33 @@ def test_decode_attention_full_size_sampled():
     # Linearity property over the whole batch: a repeated call is identical.
     again = R.decode_attention(torch.from_numpy(q).cuda(), kt, vt, table, lens, L).cpu().numpy()
     np.testing.assert_array_equal(out, again)
+
+
+# Prefill attention through its C-ABI op entry: query rows offset ..
+# offset+T-1 each against the oracle's `attention` at that row's position
+# (`ops.rs:1357-1421`; the chunk's own rows are already in the cache, as the
+# per-row append-then-attend loop of `qwen2.rs:314-343` leaves them). q is
+# bf16 (the GEMM epilogue's output), so the oracle reads the same rounded q.
+@pytest.mark.parametrize("q_heads,kv_heads,D", [(14, 2, 64), (28, 4, 128), (8, 8, 64)])
+@pytest.mark.parametrize("offset,T,window", [(0, 1, 0), (0, 130, 0), (700, 257, 0), (2048, 64, 0),
+                                             (300, 200, 96), (5000, 77, 4096)])
+def test_prefill_attention_op_matches_oracle(q_heads, kv_heads, D, offset, T, window):
+    from cheetah_b200 import runtime as R
+    from cheetah_b200.prepared import bf16_bits_to_f32, f32_to_bf16_bits
+    L = offset + T
+    kt, vt, table, dense = make_paged_kv(1, [L], kv_heads, D, 64, "bf16", seed=offset + T + D)
+    rng = np.random.default_rng(7 + T)
+    q = bf16_bits_to_f32(f32_to_bf16_bits(rng.standard_normal((T, q_heads, D), dtype=np.float32)))
+    q = q.reshape(T, q_heads, D)
+    qt = torch.from_numpy(q).to(torch.bfloat16).cuda()
+    out = R.prefill_attention(qt, kt, vt, table[0].contiguous(), offset, sliding_window=window)
+    torch.cuda.synchronize()
+    got = out.float().cpu().numpy()
+    k, v = dense[0]
+    rows = sorted(set([0, T - 1] + list(np.random.default_rng(T).integers(0, T, 12))))
+    for r in rows:
+        pos = offset + r
+        want = O.attention(k[:pos + 1], v[:pos + 1], q[r].reshape(-1), q_heads, kv_heads, D,
+                           position=pos, sliding_window=window)
+        err = np.abs(got[r].reshape(-1) - want).max()
+        assert err < 1e-2, f"row {r} (position {pos}): max err {err}"

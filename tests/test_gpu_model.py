@@ -103,6 +103,52 @@ def test_continuation_snapshot_clone_and_clear_are_exact(tiny_prepared):
     np.testing.assert_array_equal(d.forward([7], 80), e.forward([7], 80))
 
 
+def test_snapshots_share_pages_and_copy_on_write(tiny_prepared):
+    """Snapshots and restored sequences reference the source's KV pages
+    instead of copying them; the first append into a shared partial page
+    copies that page alone. Every holder stays independent: each restored
+    sequence decodes bit-exactly like a sequence that prefilled the same
+    prompt itself, while the source keeps decoding other tokens."""
+    cfg, _, model = _pair(tiny_prepared, "bf16")
+    total = model.info()["kv_pages_total"]
+    toks = _tokens(100, cfg["vocab_size"], 12)  # two 64-token pages, the second partial
+    a = model.new_sequence()
+    a.forward(toks, 0)
+    free0 = model.info()["kv_pages_free"]
+    snap = a.kv_snapshot()
+    assert model.info()["kv_pages_free"] == free0  # nothing copied
+    clones = [model.new_sequence() for _ in range(3)]
+    for c in clones:
+        c.restore_kv_prefix(snap, 100)
+    assert model.info()["kv_pages_free"] == free0  # still shared
+    fresh = model.new_sequence()
+    fresh.forward(toks, 0)
+    free1 = model.info()["kv_pages_free"]
+    # The source appends first (copy of its tail page), then every clone.
+    a.forward([5], 100)
+    outs = [c.forward([9], 100) for c in clones]
+    assert model.info()["kv_pages_free"] == free1 - 1 - len(clones)
+    want = fresh.forward([9], 100)
+    for got in outs:
+        np.testing.assert_array_equal(got, want)
+    # Restoring a shorter prefix shares the pages below it; appends there
+    # overwrite only the copy.
+    d = model.new_sequence()
+    d.restore_kv_prefix(snap, 70)
+    e = model.new_sequence()
+    e.forward(toks[:70], 0)
+    np.testing.assert_array_equal(d.forward(toks[70:80], 70), e.forward(toks[70:80], 70))
+    np.testing.assert_array_equal(clones[0].forward([3], 101), clones[1].forward([3], 101))
+    # Pages go back to the pool once their last holder lets go.
+    for seq in [a, fresh, d, e] + clones:
+        seq.clear_cache()
+    assert model.info()["kv_pages_free"] < total  # the snapshot still holds its pages
+    del snap
+    import gc
+    gc.collect()
+    assert model.info()["kv_pages_free"] == total
+
+
 def test_forward_errors(tiny_prepared):
     from cheetah_b200 import runtime as R
     cfg, _, model = _pair(tiny_prepared, "bf16", max_positions=128)

@@ -90,6 +90,25 @@ def test_oracle_matches_torch_fp32(fixture, request):
         np.testing.assert_allclose(step, ref[i].numpy(), rtol=0, atol=2e-5)
 
 
+def test_family_oracle_matches_torch_fp32(family_prepared):
+    """llama / mistral / qwen3 compositions (`llama.rs:431-560`,
+    `mistral.rs`, `qwen3.rs:441-585`): the oracle's chunked and per-position
+    forwards against the torch fp32 decoder, 80 tokens so mistral's 48-token
+    window is engaged."""
+    pytest.importorskip("torch")
+    from tests.torch_ref import TorchDecoder
+
+    pm, cfg, m = _model(family_prepared)
+    toks = _tokens(80, cfg["vocab_size"], 9)
+    ref = TorchDecoder(pm, cfg).forward(toks.tolist())
+    got = m.forward(toks, 0, chunk_rows=32)
+    np.testing.assert_allclose(got, ref[-1].numpy(), rtol=0, atol=2e-5)
+    m.clear_cache()
+    for i, t in enumerate(toks):
+        step = m.forward([t], i)
+        np.testing.assert_allclose(step, ref[i].numpy(), rtol=0, atol=2e-5)
+
+
 @pytest.mark.parametrize("quant", ["q8", "q4"])
 def test_quantised_forward_matches_dequantised_math(tiny_prepared, quant):
     # ops.rs:1180-1237: quantised linears compute scale*code*x; compare to the

@@ -73,3 +73,75 @@ def test_reader_rejects_bad_manifests(tmp_path):
         "source_file": "global.safetensors", "source_offset": 0, "shard": "s", "layer_id": 0}]))
     with pytest.raises(ValueError, match="header exceeds"):
         PreparedModel(tmp_path)
+
+
+def _with_config(root: Path, **changes) -> PreparedModel:
+    """The prepared directory at `root` with config.json fields replaced
+    (None removes a field)."""
+    cfg = json.loads((root / "config.json").read_text())
+    for key, value in changes.items():
+        if value is None:
+            cfg.pop(key, None)
+        else:
+            cfg[key] = value
+    (root / "config.json").write_text(json.dumps(cfg))
+    return PreparedModel(root)
+
+
+@pytest.mark.parametrize("name", ["tiny-llama", "tiny-mistral", "tiny-qwen3"])
+def test_family_configs_resolve_like_the_reference(tmp_path, name):
+    """`decoder.rs:260-486` over each dense family's config: the written
+    fields round-trip; absent fields fall back to the family constants
+    (`llama.rs:66-82`, `mistral.rs:63-77`, `qwen3.rs:62-77`) and the
+    manifest; `use_sliding_window` defaults to on (`decoder.rs:384-391`)."""
+    from cheetah_b200.prepared import FAMILIES, SHAPES, write_prepared
+
+    shape = SHAPES[name]
+    root = write_prepared(tmp_path / "m", shape, seed=0)
+    cfg = resolve_config(PreparedModel(root))
+    assert (cfg["q_heads"], cfg["kv_heads"], cfg["head_dim"]) == (shape.q_heads, shape.kv_heads, shape.head_dim)
+    assert cfg["sliding_window"] == shape.sliding_window
+    assert cfg["tie_word_embeddings"] == int(shape.tie_word_embeddings)
+    fam = FAMILIES[shape.family]
+    # Family constants when the config omits them; heads from the manifest.
+    bare = resolve_config(_with_config(root, rope_theta=None, rms_norm_eps=None, tie_word_embeddings=None,
+                                       num_key_value_heads=None, head_dim=None, intermediate_size=None))
+    assert bare["rope_theta"] == fam["rope_theta"] and bare["rms_eps"] == pytest.approx(fam["rms_norm_eps"])
+    assert bare["tie_word_embeddings"] == int(fam["tie_word_embeddings"])
+    assert bare["head_dim"] == shape.q_dim // shape.q_heads
+    assert bare["kv_heads"] == shape.kv_dim // bare["head_dim"]
+    assert bare["intermediate_size"] == shape.intermediate_size
+    # The window: on unless `use_sliding_window` is false.
+    assert resolve_config(_with_config(root, sliding_window=4, use_sliding_window=None))["sliding_window"] == 4
+    assert resolve_config(_with_config(root, sliding_window=4, use_sliding_window=True))["sliding_window"] == 4
+    assert resolve_config(_with_config(root, sliding_window=4096, use_sliding_window=False))["sliding_window"] == 0
+    # The family's context cap bounds max_position_embeddings (`engine.rs:1146-1162`).
+    capped = resolve_config(_with_config(root, max_position_embeddings=10 ** 6))["max_positions"]
+    assert capped == (fam["max_position_embeddings"] or 10 ** 6)
+
+
+def test_architecture_selection_and_unserved_compositions(tmp_path):
+    """The first `architectures` entry selects the family, else `model_type`
+    (`chat/mod.rs:62-67`); no name at all resolves against the llama-shaped
+    defaults (`decoder.rs:283-296`); other registered compositions are
+    refused rather than resolved into a different model."""
+    from cheetah_b200.prepared import DEFAULT_FAMILY, family_for, write_prepared
+
+    assert family_for({"architectures": ["LlamaForCausalLM"], "model_type": "qwen2"})[0] == "llama"
+    assert family_for({"model_type": "mistral"})[0] == "mistral"
+    assert family_for({"architectures": [], "model_type": "qwen3"})[0] == "qwen3"
+    assert family_for({}) == (None, DEFAULT_FAMILY)
+    for arch in ("GemmaForCausalLM", "PhiForCausalLM", "MixtralForCausalLM"):
+        with pytest.raises(ValueError, match="not served"):
+            family_for({"architectures": [arch]})
+    root = write_prepared(tmp_path / "m", TINY, seed=0)
+    anon = resolve_config(_with_config(root, architectures=None, model_type=None, rope_theta=None,
+                                       rms_norm_eps=None, tie_word_embeddings=None))
+    assert (anon["rope_theta"], anon["tie_word_embeddings"]) == (1_000_000.0, 0)
+    for field, value, match in (("num_local_experts", 8, "routed-expert"),
+                                ("partial_rotary_factor", 0.5, "partial rotary"),
+                                ("hidden_act", "gelu_pytorch_tanh", "GELU")):
+        pm = _with_config(root, **{field: value})
+        with pytest.raises(ValueError, match=match):
+            resolve_config(pm)
+        _with_config(root, **{field: None})

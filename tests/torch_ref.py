@@ -1,6 +1,8 @@
-"""Test-only third opinion: a plain PyTorch fp32 Qwen2 decoder forward over a
-prepared directory (HF Qwen2 math: RMSNorm, rotate-half RoPE, GQA causal
-attention, SwiGLU, tied head). Cross-checks the C++ oracle; never shipped."""
+"""Test-only third opinion: a plain PyTorch fp32 decoder forward over a
+prepared directory, written from the Hugging Face modeling of the dense
+families (RMSNorm, rotate-half RoPE, GQA causal attention, SwiGLU; optional
+biases, qwen3's per-head q/k RMSNorm before RoPE, mistral's sliding window).
+Cross-checks the C++ oracle; never shipped."""
 
 from __future__ import annotations
 
@@ -40,14 +42,23 @@ class TorchQwen2:
         pos = torch.arange(T, device=self.dev)
         group = c["q_heads"] // c["kv_heads"]
         mask = torch.full((T, T), float("-inf"), device=self.dev).triu(1)
+        if c.get("sliding_window"):
+            # query t sees keys t - window + 1 .. t
+            mask = mask + torch.full((T, T), float("-inf"), device=self.dev).tril(-c["sliding_window"])
         for l in range(c["num_layers"]):
             p = f"model.layers.{l}."
             h = self._norm(x, self.w[p + "input_layernorm.weight"])
             q = h @ self.w[p + "self_attn.q_proj.weight"].T + self.w.get(p + "self_attn.q_proj.bias", 0)
             k = h @ self.w[p + "self_attn.k_proj.weight"].T + self.w.get(p + "self_attn.k_proj.bias", 0)
             v = h @ self.w[p + "self_attn.v_proj.weight"].T + self.w.get(p + "self_attn.v_proj.bias", 0)
-            q = self._rope(q.view(T, c["q_heads"], c["head_dim"]), pos)
-            k = self._rope(k.view(T, c["kv_heads"], c["head_dim"]), pos)
+            q = q.view(T, c["q_heads"], c["head_dim"])
+            k = k.view(T, c["kv_heads"], c["head_dim"])
+            if p + "self_attn.q_norm.weight" in self.w:
+                q = self._norm(q, self.w[p + "self_attn.q_norm.weight"])
+            if p + "self_attn.k_norm.weight" in self.w:
+                k = self._norm(k, self.w[p + "self_attn.k_norm.weight"])
+            q = self._rope(q, pos)
+            k = self._rope(k, pos)
             v = v.view(T, c["kv_heads"], c["head_dim"])
             k = k.repeat_interleave(group, 1)
             v = v.repeat_interleave(group, 1)
@@ -62,3 +73,6 @@ class TorchQwen2:
         x = self._norm(x, self.w["model.norm.weight"])
         head = self.w["model.embed_tokens.weight"] if c["tie_word_embeddings"] else self.w["lm_head.weight"]
         return x @ head.T
+
+
+TorchDecoder = TorchQwen2
