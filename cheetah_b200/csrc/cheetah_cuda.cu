@@ -15,12 +15,14 @@
 #include <string.h>
 
 #include <algorithm>
+#include <array>
 #include <atomic>
 #include <chrono>
 #include <condition_variable>
 #include <cstdlib>
 #include <map>
 #include <mutex>
+#include <set>
 #include <string>
 #include <vector>
 
@@ -423,6 +425,25 @@ struct LayerWeights {
     const uint16_t *mk_wo = nullptr;
 };
 
+// Ant residency of one streamable linear of a layer (the fused q/k/v
+// matrix, o_proj, gate_proj, up_proj, down_proj) in a model opened with a
+// residency plan. The pinned host copy is authoritative (as the reference's
+// GPU backend keeps its host `WeightData`, `vulkan/transformer.rs:484-489`):
+// a resident linear also has its own HBM allocation, a streamed one is copied
+// into the layer's staging slot before every use.
+struct LinearHome {
+    uint8_t *dev = nullptr;     // HBM copy while resident
+    uint8_t *host = nullptr;    // pinned host copy
+    size_t bytes = 0;           // bf16 rows, or f32 row scales + code rows
+    size_t codes_off = 0;       // code rows' offset in the buffer (q8/q4)
+    size_t slot_off = 0;        // offset in a staging slot
+    size_t rows = 0, cols = 0;  // logical shape
+    int units = 1;              // reference units fused into the linear (q/k/v: 3)
+    unsigned unit_bits = 1;     // units planned into HBM (all set: resident)
+    bool resident = true;
+};
+constexpr int kHomeQkv = 0, kHomeO = 1, kHomeGate = 2, kHomeUp = 3, kHomeDown = 4, kHomes = 5;
+
 }  // namespace
 
 struct Seq;
@@ -477,6 +498,19 @@ struct Model {
     size_t mk_smem = 0;
     size_t mk_copy_bytes = 0;  // arena bytes of the decode-kernel weight copies
     MkLayer *mk_layers = nullptr;
+    // Ant VRAM tier (model opened with a residency plan): per layer, the
+    // streamable linears' homes; two staging slots (layer parity) that
+    // streamed linears are copied into before their layer runs. Planned
+    // models run without graphs, PDL or the persistent kernel, and their
+    // forwards are serialised (plan_mutex on the host, plan_event across
+    // streams) because every stream shares the staging slots.
+    bool planned = false;
+    std::vector<std::array<LinearHome, kHomes>> homes;
+    uint8_t *stage = nullptr;
+    size_t stage_slot_bytes = 0;
+    std::recursive_mutex plan_mutex;
+    cudaEvent_t plan_event = nullptr;
+    std::set<std::string> unit_ids;  // every unit of the prepared directory
     // Batched decode workspace (one batch at a time per model).
     std::mutex batch_mutex;
     int batch_cap = 0;
@@ -605,12 +639,78 @@ struct Model {
         cudaFree(k_pool);
         cudaFree(v_pool);
         cudaFree(mk_layers);
+        for (auto &layer : homes) {
+            for (LinearHome &h : layer) {
+                cudaFree(h.dev);
+                cudaFreeHost(h.host);
+            }
+        }
+        cudaFree(stage);
+        if (plan_event) cudaEventDestroy(plan_event);
     }
 };
 
 void model_unref(Model *m) {
     if (m != nullptr && m->refs.fetch_sub(1) == 1) delete m;
 }
+
+// ---- Ant VRAM tier -----------------------------------------------------------
+// Where linear `j` of `layer` is read from now: its own HBM copy while
+// resident, the layer's staging slot (layer parity) while streamed. Sets the
+// layer's pointers and, for models with tensor-core prefill operands,
+// re-encodes the linear's tensor map.
+int bind_linear(Model &m, uint32_t layer, int j, bool encode_map) {
+    LinearHome &h = m.homes[layer][j];
+    LayerWeights &w = m.layers[layer];
+    uint8_t *base = h.resident ? h.dev : m.stage + (layer % 2) * m.stage_slot_bytes + h.slot_off;
+    QuantMatrix *q[kHomes] = {&w.qqkv, &w.qo, &w.qgate, &w.qup, &w.qdown};
+    const uint16_t **raw[kHomes] = {&w.wqkv, &w.wo, &w.wgate, &w.wup, &w.wdown};
+    CUtensorMap *map[kHomes] = {&w.map_qkv, &w.map_o, &w.map_gate, &w.map_up, &w.map_down};
+    if (m.quant == kWBf16) {
+        q[j]->codes = reinterpret_cast<const uint16_t *>(base);
+        q[j]->scales = nullptr;
+    } else {
+        q[j]->scales = reinterpret_cast<const float *>(base);
+        q[j]->codes = reinterpret_cast<const uint16_t *>(base + h.codes_off);
+    }
+    *raw[j] = q[j]->codes;
+    if (encode_map && m.quant == kWBf16)
+        return make_bf16_tensor_map(map[j], q[j]->codes, (unsigned long long)h.rows, (unsigned long long)h.cols, 64);
+    return 0;
+}
+
+// Copies the streamed linears of `layer` into its staging slot, in stream
+// order before the layer's kernels (the slot's previous user, layer - 2,
+// precedes them in the same stream).
+int stage_layer(Model &m, uint32_t layer, cudaStream_t st) {
+    if (!m.planned) return 0;
+    for (int j = 0; j < kHomes; ++j) {
+        const LinearHome &h = m.homes[layer][j];
+        if (h.resident) continue;
+        CH_CUDA_TRY(cudaMemcpyAsync(m.stage + (layer % 2) * m.stage_slot_bytes + h.slot_off, h.host, h.bytes,
+                                    cudaMemcpyHostToDevice, st));
+    }
+    return 0;
+}
+
+// Serialises the forwards of a planned model: one host thread at a time
+// enqueues, and each forward's device work starts after the previous one's
+// (whatever stream that ran on), since all of them share the staging slots.
+struct PlanGuard {
+    Model &m;
+    cudaStream_t st;
+    bool on;
+    PlanGuard(Model &model, cudaStream_t stream) : m(model), st(stream), on(model.planned) {
+        if (!on) return;
+        m.plan_mutex.lock();
+        cudaStreamWaitEvent(st, m.plan_event, 0);
+    }
+    ~PlanGuard() {
+        if (!on) return;
+        cudaEventRecord(m.plan_event, st);
+        m.plan_mutex.unlock();
+    }
+};
 
 struct Seq {
     Model *m = nullptr;
@@ -825,6 +925,7 @@ int enqueue_decode_step(Seq &s, bool chain) {
     const int32_t *seq_lens = &s.d_step->seq_len;
 
     for (uint32_t layer = 0; layer < c.num_layers; ++layer) {
+        if (stage_layer(m, layer, st) != 0) return -1;
         const LayerWeights &w = m.layers[layer];
         uint8_t *k_layer = m.k_pool + layer * m.layer_stride_bytes;
         uint8_t *v_layer = m.v_pool + layer * m.layer_stride_bytes;
@@ -1021,7 +1122,7 @@ int run_decode_step(Seq &s, uint32_t token, size_t position) {
         return 0;
     }
     if (s.graph == nullptr) {
-        if (env_flag("CHEETAH_CUDA_GRAPH", true)) {
+        if (env_flag("CHEETAH_CUDA_GRAPH", true) && !s.m->planned) {
             if (build_decode_graph(s, false, &s.graph) != 0) return -1;
         }
     }
@@ -1062,8 +1163,15 @@ float bf16_bits_to_float(uint16_t bits) {
     return f;
 }
 
+// Tier of a unit in a residency plan ("vram" when the plan does not list it).
+bool plan_in_vram(const std::map<std::string, std::string> *plan, const std::string &unit) {
+    if (plan == nullptr) return true;
+    auto it = plan->find(unit);
+    return it == plan->end() || it->second == "vram";
+}
+
 int open_model(const char *prepared_dir, const CheetahCudaConfig *config, const char *quant,
-               int device, Model **out) {
+               int device, Model **out, const std::map<std::string, std::string> *plan = nullptr) {
     CH_REQUIRE(prepared_dir != nullptr && config != nullptr && out != nullptr,
                "cheetah_cuda_model_open: null argument");
     const std::string q = quant ? quant : "bf16";
@@ -1107,6 +1215,20 @@ int open_model(const char *prepared_dir, const CheetahCudaConfig *config, const 
     m->page_tokens = (int)c.kv_page_tokens;
     m->kv_f32 = c.kv_dtype == CHEETAH_CUDA_KV_F32;
     m->quant = wfmt;
+    m->planned = plan != nullptr;
+    if (m->planned) {
+        // Streamed layers put host copies between kernels: plain stream order.
+        m->pdl = false;
+        for (const auto &kv : *plan) {
+            if (kv.second != "vram" && kv.second != "ram" && kv.second != "disk") {
+                set_error("CUDA backend: unknown Ant tier '" + kv.second + "' for unit '" + kv.first +
+                          "' (expected vram, ram or disk).");
+                delete m;
+                return -1;
+            }
+        }
+    }
+    for (const std::string &id : store.unit_ids()) m->unit_ids.insert(id);
 
     const size_t H = c.hidden_size, I = c.intermediate_size, V = c.vocab_size;
     const size_t QD = (size_t)c.q_heads * c.head_dim, KD = (size_t)c.kv_heads * c.head_dim;
@@ -1159,7 +1281,7 @@ int open_model(const char *prepared_dir, const CheetahCudaConfig *config, const 
         m->qk_norm = store.contains("model.layers.0.self_attn.q_norm.weight") ||
                      store.contains("model.layers.0.self_attn.k_norm.weight");
         m->mk_enabled = env_flag("CHEETAH_CUDA_MEGAKERNEL", true) && coop != 0 && wfmt == kWBf16 && !m->kv_f32 &&
-                        !m->qk_norm &&
+                        !m->qk_norm && !m->planned &&
                         4 * H <= (size_t)kMkSlotBytes && 2 * I <= (size_t)kMkSlotBytes &&
                         c.q_heads <= (uint32_t)kMkMaxHeads && c.q_heads <= (uint32_t)m->sms &&
                         mma_attention_eligible((int)c.head_dim, m->page_tokens) && slots >= 3;
@@ -1169,8 +1291,12 @@ int open_model(const char *prepared_dir, const CheetahCudaConfig *config, const 
             m->mk_group_units = (m->sms + (int)c.q_heads - 1) / (int)c.q_heads;
         }
     }
-    size_t per_layer = linear_bytes(QD + 2 * KD, H) + linear_bytes(H, QD) + 2 * linear_bytes(I, H) +
-                       linear_bytes(H, I) + (2 * H + (QD + 2 * KD) + H) * 4 + 8 * 256;
+    // A planned model's linears live outside the arena (own HBM copies, or
+    // host copies streamed through the staging slots).
+    size_t per_layer = (m->planned ? 0
+                                   : linear_bytes(QD + 2 * KD, H) + linear_bytes(H, QD) + 2 * linear_bytes(I, H) +
+                                         linear_bytes(H, I)) +
+                       (2 * H + (QD + 2 * KD) + H) * 4 + 8 * 256;
     if (m->mk_enabled) per_layer += H * QD * 2 + (QD + 2 * KD) * H * 2 + 2 * 256;
     total += per_layer * c.num_layers;
     cudaError_t err = cudaMalloc(&m->arena, total);
@@ -1227,7 +1353,55 @@ int open_model(const char *prepared_dir, const CheetahCudaConfig *config, const 
         const size_t max_elems = std::max(std::max((QD + 2 * KD) * H, H * QD), std::max(I * H, H * I));
         if (cudaMalloc(&staging, max_elems * 2) != cudaSuccess) return fail("CUDA backend: staging allocation failed");
     }
-    auto place_linear = [&](const uint16_t *host, size_t rows, size_t cols, QuantMatrix *out) -> bool {
+    // Planned models: quantised buffers are built in a device scratch buffer,
+    // then copied to the pinned host copy (and to an own HBM copy when the
+    // linear is resident).
+    uint8_t *qtmp = nullptr;
+    if (m->planned && wfmt != kWBf16) {
+        const size_t max_elems = std::max(std::max((QD + 2 * KD) * H, H * QD), std::max(I * H, H * I));
+        if (cudaMalloc(&qtmp, max_elems + 8 * std::max(std::max(QD + 2 * KD, H), I) + 4096) != cudaSuccess)
+            return fail("CUDA backend: quantisation scratch allocation failed");
+    }
+    auto place_home = [&](const uint16_t *host, size_t rows, size_t cols, QuantMatrix *out, LinearHome *home) -> bool {
+        home->rows = rows;
+        home->cols = cols;
+        const uint8_t *src_dev = nullptr;  // device bytes to copy from (quantised formats)
+        if (wfmt == kWBf16) {
+            home->bytes = rows * cols * 2;
+            home->codes_off = 0;
+            out->row_stride = (long long)cols * 2;
+        } else {
+            if (!upload(staging, host, rows * cols * 2)) return false;
+            long long rb = wfmt == kWQ8 ? q8_row_bytes((long long)cols) : q4_row_bytes((long long)cols);
+            if (wfmt == kWQ4 && cols % 128 == 0) rb = (long long)cols / 2;
+            const int blocks = (int)((rows * kWarp + 255) / 256);
+            if (wfmt == kWQ8) quantize_rows_kernel<8><<<blocks, 256>>>(staging, (int)rows, (int)cols, qtmp, rb);
+            else quantize_rows_kernel<4><<<blocks, 256>>>(staging, (int)rows, (int)cols, qtmp, rb);
+            home->bytes = rows * 4 + rows * (size_t)rb;
+            home->codes_off = rows * 4;
+            out->row_stride = rb;
+            src_dev = qtmp;
+        }
+        cudaError_t e = cudaHostAlloc(reinterpret_cast<void **>(&home->host), home->bytes, cudaHostAllocDefault);
+        if (e == cudaSuccess) {
+            if (src_dev) e = cudaMemcpy(home->host, src_dev, home->bytes, cudaMemcpyDeviceToHost);
+            else memcpy(home->host, host, home->bytes);
+        }
+        if (e == cudaSuccess && home->resident) {
+            e = cudaMalloc(reinterpret_cast<void **>(&home->dev), home->bytes);
+            if (e == cudaSuccess)
+                e = cudaMemcpy(home->dev, src_dev ? (const void *)src_dev : (const void *)home->host, home->bytes,
+                               src_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice);
+        }
+        if (e != cudaSuccess) {
+            error = std::string("CUDA backend: Ant residency placement failed: ") + cudaGetErrorString(e);
+            return false;
+        }
+        return true;
+    };
+    auto place_linear = [&](const uint16_t *host, size_t rows, size_t cols, QuantMatrix *out,
+                            LinearHome *home = nullptr) -> bool {
+        if (home != nullptr) return place_home(host, rows, cols, out, home);
         if (wfmt == kWBf16) {
             uint16_t *dst = (uint16_t *)m->take(rows * cols * 2);
             if (!upload(dst, host, rows * cols * 2)) return false;
@@ -1269,6 +1443,31 @@ int open_model(const char *prepared_dir, const CheetahCudaConfig *config, const 
         return true;
     };
     m->layers.resize(c.num_layers);
+    // Residency of each streamable linear: resident when every reference
+    // unit fused into it is planned into HBM ("vram" or absent from the plan).
+    static const char *kHomeUnits[kHomes][3] = {
+        {"self_attn.q_proj.weight", "self_attn.k_proj.weight", "self_attn.v_proj.weight"},
+        {"self_attn.o_proj.weight", nullptr, nullptr},
+        {"mlp.gate_proj.weight", nullptr, nullptr},
+        {"mlp.up_proj.weight", nullptr, nullptr},
+        {"mlp.down_proj.weight", nullptr, nullptr}};
+    if (m->planned) {
+        m->homes.resize(c.num_layers);
+        for (uint32_t layer = 0; layer < c.num_layers; ++layer) {
+            const std::string p = "model.layers." + std::to_string(layer) + ".";
+            for (int j = 0; j < kHomes; ++j) {
+                LinearHome &h = m->homes[layer][j];
+                h.units = j == kHomeQkv ? 3 : 1;
+                h.unit_bits = 0;
+                for (int u = 0; u < h.units; ++u)
+                    if (plan_in_vram(plan, p + kHomeUnits[j][u])) h.unit_bits |= 1u << u;
+                h.resident = h.unit_bits == (1u << h.units) - 1;
+            }
+        }
+    }
+    auto home = [&](uint32_t layer, int j) -> LinearHome * {
+        return m->planned ? &m->homes[layer][j] : nullptr;
+    };
     for (uint32_t layer = 0; layer < c.num_layers; ++layer) {
         const std::string p = "model.layers." + std::to_string(layer) + ".";
         LayerWeights &w = m->layers[layer];
@@ -1308,10 +1507,10 @@ int open_model(const char *prepared_dir, const CheetahCudaConfig *config, const 
                 }
                 staged.swap(perm);
             }
-            if (!place_linear(staged.data(), QD + 2 * KD, H, &w.qqkv)) return fail(error);
+            if (!place_linear(staged.data(), QD + 2 * KD, H, &w.qqkv, home(layer, kHomeQkv))) return fail(error);
         }
         if (!check_unit(p + "self_attn.o_proj.weight", {H, QD}, &bytes) ||
-            !place_linear((const uint16_t *)bytes, H, QD, &w.qo)) return fail(error);
+            !place_linear((const uint16_t *)bytes, H, QD, &w.qo, home(layer, kHomeO))) return fail(error);
         if (m->mk_enabled) {
             // W_o[:, head] blocks, head-major: [q_heads][H][head_dim].
             const size_t hd = c.head_dim;
@@ -1327,11 +1526,11 @@ int open_model(const char *prepared_dir, const CheetahCudaConfig *config, const 
             m->mk_copy_bytes += heads_major.size() * 2;
         }
         if (!check_unit(p + "mlp.gate_proj.weight", {I, H}, &bytes) ||
-            !place_linear((const uint16_t *)bytes, I, H, &w.qgate)) return fail(error);
+            !place_linear((const uint16_t *)bytes, I, H, &w.qgate, home(layer, kHomeGate))) return fail(error);
         if (!check_unit(p + "mlp.up_proj.weight", {I, H}, &bytes) ||
-            !place_linear((const uint16_t *)bytes, I, H, &w.qup)) return fail(error);
+            !place_linear((const uint16_t *)bytes, I, H, &w.qup, home(layer, kHomeUp))) return fail(error);
         if (!check_unit(p + "mlp.down_proj.weight", {H, I}, &bytes) ||
-            !place_linear((const uint16_t *)bytes, H, I, &w.qdown)) return fail(error);
+            !place_linear((const uint16_t *)bytes, H, I, &w.qdown, home(layer, kHomeDown))) return fail(error);
         w.wqkv = w.qqkv.codes;
         w.wo = w.qo.codes;
         w.wgate = w.qgate.codes;
@@ -1385,6 +1584,24 @@ int open_model(const char *prepared_dir, const CheetahCudaConfig *config, const 
     }
 
     cudaFree(staging);
+    cudaFree(qtmp);
+
+    if (m->planned) {
+        // Staging slots: every streamable linear of a layer at a fixed
+        // offset, two slots (layer parity).
+        size_t off = 0;
+        for (int j = 0; j < kHomes; ++j) {
+            const size_t slot_off = off;
+            for (auto &layer : m->homes) layer[j].slot_off = slot_off;
+            off += (m->homes[0][j].bytes + 255) & ~size_t(255);
+        }
+        m->stage_slot_bytes = off;
+        cudaError_t e = cudaMalloc(&m->stage, 2 * off);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&m->plan_event, cudaEventDisableTiming);
+        if (e != cudaSuccess) return fail(std::string("CUDA backend: Ant staging allocation failed: ") + cudaGetErrorString(e));
+        for (uint32_t layer = 0; layer < c.num_layers; ++layer)
+            for (int j = 0; j < kHomes; ++j) bind_linear(*m, layer, j, false);
+    }
 
     if (m->mk_enabled) {
         std::vector<MkLayer> table(c.num_layers);
@@ -1549,6 +1766,7 @@ int forward(Seq *s, const uint32_t *tokens, size_t n, size_t offset, float *logi
                "CUDA backend: position " + std::to_string(offset + n - 1) +
                    " exceeds the sequence capacity " + std::to_string(c.max_positions) + ".");
     CH_CUDA_TRY(cudaSetDevice(s->m->device));
+    PlanGuard plan_guard(*s->m, s->stream);
     if (make_tail_page_private(*s) != 0) return -1;
     const bool chunked = n > 1 && s->m->gemm_prefill && std::getenv("CHEETAH_CUDA_STEPWISE_PREFILL") == nullptr;
     if (chunked) {
@@ -1822,6 +2040,7 @@ int run_prefill_chunk(Seq &s, const uint32_t *tokens, int M, size_t offset, bool
     CH_CUDA_TRY(launch_ex(embed_rows_kernel, dim3(M), dim3(256), 0, st, pdl, m.embed, H, (const int32_t *)s.ptokens, M,
                           s.phid));
     for (uint32_t layer = 0; layer < c.num_layers; ++layer) {
+        if (stage_layer(m, layer, st) != 0) return -1;
         const LayerWeights &w = m.layers[layer];
         uint8_t *k_layer = m.k_pool + layer * m.layer_stride_bytes;
         uint8_t *v_layer = m.v_pool + layer * m.layer_stride_bytes;
@@ -2039,6 +2258,7 @@ int enqueue_batch_step_gemv(Model &m, int M, int table_stride, bool want_logits,
     CH_CUDA_TRY(launch_ex(embed_rows_kernel, dim3(M), dim3(256), 0, st, pdl, m.embed, H, d_tok, M, m.b_hid));
     const int splits = mma_attention_splits(M, c.kv_heads, m.sms);
     for (uint32_t layer = 0; layer < c.num_layers; ++layer) {
+        if (stage_layer(m, layer, st) != 0) return -1;
         const LayerWeights &w = m.layers[layer];
         GemvParams q = {};
         q.w0 = w.wqkv;
@@ -2189,6 +2409,7 @@ int enqueue_batch_step(Model &m, int M, int table_stride, bool want_logits, bool
     CH_CUDA_TRY(launch_ex(embed_rows_kernel, dim3(M), dim3(256), 0, st, pdl, m.embed, H, d_tok, M, m.b_hid));
     const int splits = mma_attention_splits(M, c.kv_heads, m.sms);
     for (uint32_t layer = 0; layer < c.num_layers; ++layer) {
+        if (stage_layer(m, layer, st) != 0) return -1;
         const LayerWeights &w = m.layers[layer];
         CH_CUDA_TRY(launch_ex(norm_rows_bf16_kernel, dim3(M), dim3(256), 0, st, pdl, (const float *)m.b_hid, M, H,
                               w.ln1, c.rms_eps, m.b_xb));
@@ -2348,7 +2569,7 @@ int batch_graph(Model &m, int M, int table_stride, bool want_logits, bool chaine
     const uint64_t key = ((uint64_t)M << 40) | ((uint64_t)table_stride << 8) | (chained ? 2u : 0u) |
                          (want_logits ? 1u : 0u);
     auto it = m.batch_graphs.find(key);
-    if (it == m.batch_graphs.end() && env_flag("CHEETAH_CUDA_GRAPH", true)) {
+    if (it == m.batch_graphs.end() && env_flag("CHEETAH_CUDA_GRAPH", true) && !m.planned) {
         cudaGraph_t graph = nullptr;
         CH_CUDA_TRY(cudaStreamBeginCapture(m.batch_stream, cudaStreamCaptureModeThreadLocal));
         const int rc = enqueue_batch_step(m, M, table_stride, want_logits, chained);
@@ -2398,6 +2619,7 @@ int forward_batch_rows(Model *mp, Seq *const *seqs, const uint32_t *tokens, cons
     std::lock_guard<std::mutex> lock(m.batch_mutex);
     int M = 0, table_stride = 0;
     if (prepare_batch(m, seqs, tokens, offsets, B, 1, "cheetah_cuda_forward_batch", &M, &table_stride) != 0) return -1;
+    PlanGuard plan_guard(m, m.batch_stream);
     bool want_logits = false;
     for (size_t b = 0; row_logits != nullptr && b < B; ++b) want_logits |= row_logits[b] != nullptr;
     cudaGraphExec_t exec = nullptr;
@@ -2583,6 +2805,7 @@ int forward_batch_greedy(Model *mp, Seq *const *seqs, const uint32_t *tokens, co
     int M = 0, table_stride = 0;
     if (prepare_batch(m, seqs, tokens, offsets, B, steps, "cheetah_cuda_forward_batch_greedy", &M, &table_stride) != 0)
         return -1;
+    PlanGuard plan_guard(m, m.batch_stream);
     cudaGraphExec_t exec = nullptr;
     if (batch_graph(m, M, table_stride, false, true, &exec) != 0) return -1;
     cudaStream_t st = m.batch_stream;
@@ -2653,6 +2876,7 @@ int generate_greedy(Seq *s, uint32_t first_token, size_t offset, size_t steps, u
         std::vector<int32_t> ids(s->pages.begin() + first_page, s->pages.end());
         CH_CUDA_TRY(cudaMemcpy(s->page_table + first_page, ids.data(), ids.size() * 4, cudaMemcpyHostToDevice));
     }
+    PlanGuard plan_guard(*s->m, s->stream);
     if (s->m->mk_enabled) {
         // One cooperative launch runs every step; token i is logged at i.
         if (ensure_mk_buffers(*s) != 0) return -1;
@@ -2677,7 +2901,8 @@ int generate_greedy(Seq *s, uint32_t first_token, size_t offset, size_t steps, u
         for (size_t i = 0; i < steps; ++i) tokens_out[i] = (uint32_t)log[i];
         return 0;
     }
-    if (s->chain_graph == nullptr && build_decode_graph(*s, true, &s->chain_graph) != 0) return -1;
+    const bool eager = s->m->planned || !env_flag("CHEETAH_CUDA_GRAPH", true);
+    if (!eager && s->chain_graph == nullptr && build_decode_graph(*s, true, &s->chain_graph) != 0) return -1;
     StepState init = {};
     init.token = (int32_t)first_token;
     init.position = (int32_t)offset - 1;
@@ -2691,7 +2916,13 @@ int generate_greedy(Seq *s, uint32_t first_token, size_t offset, size_t steps, u
     CH_CUDA_TRY(cudaMemcpyAsync(s->d_step, s->h_step, sizeof(StepState), cudaMemcpyHostToDevice, s->stream));
     CH_CUDA_TRY(cudaMemcpyAsync(s->argmax, s->h_argmax, 8, cudaMemcpyHostToDevice, s->stream));
     CH_CUDA_TRY(cudaStreamSynchronize(s->stream));
-    for (size_t i = 0; i < steps; ++i) CH_CUDA_TRY(cudaGraphLaunch(s->chain_graph, s->stream));
+    for (size_t i = 0; i < steps; ++i) {
+        if (eager) {
+            if (enqueue_decode_step(*s, true) != 0) return -1;
+        } else {
+            CH_CUDA_TRY(cudaGraphLaunch(s->chain_graph, s->stream));
+        }
+    }
     s->positions = offset + steps;
     if (tokens_out == nullptr) return 0;  // asynchronous: caller synchronises the stream
     std::vector<int32_t> log(steps);
@@ -2704,6 +2935,82 @@ int generate_greedy(Seq *s, uint32_t first_token, size_t offset, size_t steps, u
     }
     for (size_t i = 0; i + 1 < steps; ++i) tokens_out[i] = (uint32_t)log[i + 1];
     tokens_out[steps - 1] = (uint32_t)(*s->h_argmax & 0xFFFFFFFFull);
+    return 0;
+}
+
+// Layer, linear and unit bit of a streamable unit id
+// ("model.layers.<n>.<suffix>"); false for every other unit.
+bool parse_home_unit(const Model &m, const std::string &id, uint32_t *layer, int *j, int *bit) {
+    static const char *kPrefix = "model.layers.";
+    if (id.compare(0, 13, kPrefix) != 0) return false;
+    size_t pos = 13, end = id.find('.', pos);
+    if (end == std::string::npos || end == pos) return false;
+    uint32_t n = 0;
+    for (size_t i = pos; i < end; ++i) {
+        if (id[i] < '0' || id[i] > '9') return false;
+        n = n * 10 + (uint32_t)(id[i] - '0');
+    }
+    if (n >= m.cfg.num_layers) return false;
+    const std::string suffix = id.substr(end + 1);
+    static const struct {
+        const char *suffix;
+        int j, bit;
+    } kMap[] = {{"self_attn.q_proj.weight", kHomeQkv, 0}, {"self_attn.k_proj.weight", kHomeQkv, 1},
+                {"self_attn.v_proj.weight", kHomeQkv, 2}, {"self_attn.o_proj.weight", kHomeO, 0},
+                {"mlp.gate_proj.weight", kHomeGate, 0},  {"mlp.up_proj.weight", kHomeUp, 0},
+                {"mlp.down_proj.weight", kHomeDown, 0}};
+    for (const auto &e : kMap) {
+        if (suffix == e.suffix) {
+            *layer = n;
+            *j = e.j;
+            *bit = e.bit;
+            return true;
+        }
+    }
+    return false;
+}
+
+// AntTierControl (`registry.rs:88-93`): moves one unit into HBM (resident)
+// or out of it (streamed from its pinned host copy). A fused linear (q/k/v)
+// is resident only while all of its units are. Units outside the layer
+// linears (embedding, lm_head, norms, biases) always stay resident.
+int set_unit_residency(Model *m, const char *unit_id, bool resident, int *known) {
+    CH_REQUIRE(m != nullptr && unit_id != nullptr, "cheetah_cuda_model_set_residency: null argument");
+    const std::string id(unit_id);
+    const bool exists = m->unit_ids.count(id) != 0;
+    if (known) *known = exists ? 1 : 0;
+    if (!exists) return 0;
+    uint32_t layer = 0;
+    int j = 0, bit = 0;
+    if (!parse_home_unit(*m, id, &layer, &j, &bit)) return 0;
+    CH_REQUIRE(m->planned,
+               "CUDA backend: the model was opened without a residency plan (cheetah_cuda_model_open_ex).");
+    std::lock_guard<std::recursive_mutex> lock(m->plan_mutex);
+    CH_CUDA_TRY(cudaSetDevice(m->device));
+    CH_CUDA_TRY(cudaEventSynchronize(m->plan_event));  // the last forward's device work is done
+    LinearHome &h = m->homes[layer][j];
+    const unsigned old_bits = h.unit_bits;
+    if (resident) h.unit_bits |= 1u << bit;
+    else h.unit_bits &= ~(1u << bit);
+    const bool want = h.unit_bits == (1u << h.units) - 1;
+    if (want == h.resident) return 0;
+    if (want) {
+        cudaError_t e = cudaMalloc(reinterpret_cast<void **>(&h.dev), h.bytes);
+        if (e == cudaSuccess) e = cudaMemcpy(h.dev, h.host, h.bytes, cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) {
+            cudaFree(h.dev);
+            h.dev = nullptr;
+            h.unit_bits = old_bits;
+            set_error(std::string("CUDA backend: Ant page-in failed: ") + cudaGetErrorString(e));
+            return -1;
+        }
+        h.resident = true;
+        return bind_linear(*m, layer, j, true);
+    }
+    h.resident = false;
+    if (bind_linear(*m, layer, j, true) != 0) return -1;
+    cudaFree(h.dev);
+    h.dev = nullptr;
     return 0;
 }
 
@@ -2753,6 +3060,54 @@ int cheetah_cuda_model_open(const char *prepared_dir, const CheetahCudaConfig *c
     return 0;
 }
 
+int cheetah_cuda_model_open_ex(const char *prepared_dir, const CheetahCudaConfig *config, const char *quant,
+                               int device, const CheetahCudaResidency *plan, CheetahCudaModel **out) {
+    std::map<std::string, std::string> tiers;
+    if (plan != nullptr) {
+        CH_REQUIRE(plan->count == 0 || (plan->unit_ids != nullptr && plan->tiers != nullptr),
+                   "cheetah_cuda_model_open_ex: null plan arrays");
+        for (size_t i = 0; i < plan->count; ++i) {
+            CH_REQUIRE(plan->unit_ids[i] != nullptr && plan->tiers[i] != nullptr,
+                       "cheetah_cuda_model_open_ex: null plan entry");
+            tiers[plan->unit_ids[i]] = plan->tiers[i];
+        }
+    }
+    Model *m = nullptr;
+    if (cheetah::open_model(prepared_dir, config, quant, device, &m, plan ? &tiers : nullptr) != 0) return -1;
+    *out = reinterpret_cast<CheetahCudaModel *>(m);
+    return 0;
+}
+
+int cheetah_cuda_model_page_in_unit(CheetahCudaModel *model, const char *unit_id, int tier, int *known) {
+    CH_REQUIRE(tier >= 0 && tier <= 2, "cheetah_cuda_model_page_in_unit: tier must be 0 (vram), 1 (ram) or 2 (disk)");
+    return cheetah::set_unit_residency(reinterpret_cast<Model *>(model), unit_id, tier == 0, known);
+}
+
+int cheetah_cuda_model_evict_unit(CheetahCudaModel *model, const char *unit_id, int *known) {
+    return cheetah::set_unit_residency(reinterpret_cast<Model *>(model), unit_id, false, known);
+}
+
+int cheetah_cuda_model_residency(const CheetahCudaModel *model, CheetahCudaResidencyInfo *info) {
+    CH_REQUIRE(model != nullptr && info != nullptr, "cheetah_cuda_model_residency: null argument");
+    Model *m = const_cast<Model *>(reinterpret_cast<const Model *>(model));
+    std::lock_guard<std::recursive_mutex> lock(m->plan_mutex);
+    *info = CheetahCudaResidencyInfo{};
+    info->planned = m->planned ? 1 : 0;
+    info->staging_bytes = m->planned ? 2 * (uint64_t)m->stage_slot_bytes : 0;
+    for (auto &layer : m->homes) {
+        for (const cheetah::LinearHome &h : layer) {
+            if (h.resident) {
+                info->resident_linear_bytes += h.bytes;
+                info->resident_linears += 1;
+            } else {
+                info->streamed_linear_bytes += h.bytes;
+                info->streamed_linears += 1;
+            }
+        }
+    }
+    return 0;
+}
+
 int cheetah_cuda_model_free(CheetahCudaModel *model) {
     if (model != nullptr) cheetah::model_unref(reinterpret_cast<Model *>(model));
     return 0;
@@ -2762,6 +3117,12 @@ int cheetah_cuda_model_info(const CheetahCudaModel *model, CheetahCudaModelInfo 
     CH_REQUIRE(model != nullptr && info != nullptr, "cheetah_cuda_model_info: null argument");
     Model *m = const_cast<Model *>(reinterpret_cast<const Model *>(model));
     info->weight_bytes = m->arena_used - m->mk_copy_bytes;  // distinct weights, not the decode-kernel copies
+    {
+        std::lock_guard<std::recursive_mutex> lock(m->plan_mutex);
+        for (auto &layer : m->homes)
+            for (const cheetah::LinearHome &h : layer)
+                if (h.resident) info->weight_bytes += h.bytes;  // planned models' HBM-resident linears
+    }
     info->kv_pool_bytes = (uint64_t)m->layer_stride_bytes * m->cfg.num_layers * 2;
     info->kv_pages_total = (uint32_t)m->num_pages;
     {

@@ -44,6 +44,11 @@ class PreparedStore {
     bool open(const std::string &root, std::string *error);
     bool contains(const std::string &unit_id) const { return units_.count(unit_id) != 0; }
     const UnitRecord *record(const std::string &unit_id) const;
+    std::vector<std::string> unit_ids() const {
+        std::vector<std::string> ids;
+        for (const auto &kv : units_) ids.push_back(kv.first);
+        return ids;
+    }
     // Byte view of one unit inside its shard mapping (nullptr + error if absent).
     const uint8_t *slice(const std::string &unit_id, std::string *error) const;
 

@@ -54,6 +54,18 @@ class ModelInfo(C.Structure):
     ]
 
 
+class Residency(C.Structure):
+    _fields_ = [("unit_ids", C.POINTER(C.c_char_p)), ("tiers", C.POINTER(C.c_char_p)), ("count", C.c_size_t)]
+
+
+class ResidencyInfo(C.Structure):
+    _fields_ = [
+        ("resident_linear_bytes", C.c_uint64), ("streamed_linear_bytes", C.c_uint64),
+        ("staging_bytes", C.c_uint64), ("resident_linears", C.c_uint32), ("streamed_linears", C.c_uint32),
+        ("planned", C.c_int32), ("reserved", C.c_int32),
+    ]
+
+
 class DecodeAttentionArgs(C.Structure):
     _fields_ = [
         ("q", C.c_void_p), ("k_pool", C.c_void_p), ("v_pool", C.c_void_p),
@@ -84,6 +96,11 @@ SIGNATURES = {
     "cheetah_cuda_model_open": (_I, [C.c_char_p, C.POINTER(CudaConfig), C.c_char_p, _I, C.POINTER(_P)]),
     "cheetah_cuda_model_free": (_I, [_P]),
     "cheetah_cuda_model_info": (_I, [_P, C.POINTER(ModelInfo)]),
+    "cheetah_cuda_model_open_ex": (_I, [C.c_char_p, C.POINTER(CudaConfig), C.c_char_p, _I, C.POINTER(Residency),
+                                        C.POINTER(_P)]),
+    "cheetah_cuda_model_page_in_unit": (_I, [_P, C.c_char_p, _I, C.POINTER(_I)]),
+    "cheetah_cuda_model_evict_unit": (_I, [_P, C.c_char_p, C.POINTER(_I)]),
+    "cheetah_cuda_model_residency": (_I, [_P, C.POINTER(ResidencyInfo)]),
     "cheetah_cuda_seq_new": (_I, [_P, C.POINTER(_P)]),
     "cheetah_cuda_seq_free": (_I, [_P]),
     "cheetah_cuda_seq_clear": (_I, [_P]),
@@ -154,7 +171,9 @@ class CudaModel:
     def __init__(self, prepared_dir: os.PathLike, quant: str = "bf16", device: int = 0,
                  kv_dtype: str = "bf16", max_positions: Optional[int] = None,
                  kv_pool_tokens: int = 0, kv_page_tokens: int = 0,
-                 config: Optional[dict] = None):
+                 config: Optional[dict] = None, residency: Optional[dict] = None):
+        """`residency`: an Ant plan {unit id: "vram" | "ram" | "disk"}
+        (`cheetah_cuda_model_open_ex`); None opens every unit HBM-resident."""
         self.prepared_dir = Path(prepared_dir)
         cfg = dict(config) if config else resolve_config(PreparedModel(self.prepared_dir), max_positions)
         if max_positions:
@@ -167,8 +186,16 @@ class CudaModel:
                        cfg["sliding_window"], cfg["max_positions"], kv_page_tokens, kv_pool_tokens,
                        KV_F32 if kv_dtype == "f32" else KV_BF16)
         handle = C.c_void_p()
-        _check(lib().cheetah_cuda_model_open(str(self.prepared_dir).encode(), C.byref(c),
-                                             quant.encode(), device, C.byref(handle)))
+        if residency is None:
+            _check(lib().cheetah_cuda_model_open(str(self.prepared_dir).encode(), C.byref(c),
+                                                 quant.encode(), device, C.byref(handle)))
+        else:
+            items = sorted(residency.items())
+            ids = (C.c_char_p * max(1, len(items)))(*[k.encode() for k, _ in items])
+            tiers = (C.c_char_p * max(1, len(items)))(*[v.encode() for _, v in items])
+            plan = Residency(ids, tiers, len(items))
+            _check(lib().cheetah_cuda_model_open_ex(str(self.prepared_dir).encode(), C.byref(c), quant.encode(),
+                                                    device, C.byref(plan), C.byref(handle)))
         self._h = handle
 
     @property
@@ -179,6 +206,23 @@ class CudaModel:
         info = ModelInfo()
         _check(lib().cheetah_cuda_model_info(self._h, C.byref(info)))
         return {f: getattr(info, f) for f, _ in ModelInfo._fields_}
+
+    def residency(self) -> dict:
+        info = ResidencyInfo()
+        _check(lib().cheetah_cuda_model_residency(self._h, C.byref(info)))
+        return {f: getattr(info, f) for f, _ in ResidencyInfo._fields_}
+
+    def page_in_unit(self, unit_id: str, tier: int = 0) -> bool:
+        """`AntTierControl::page_in_unit`: True when the manifest knows the unit."""
+        known = C.c_int(0)
+        _check(lib().cheetah_cuda_model_page_in_unit(self._h, unit_id.encode(), tier, C.byref(known)))
+        return bool(known.value)
+
+    def evict_unit(self, unit_id: str) -> bool:
+        """`AntTierControl::evict_unit`: True when the manifest knows the unit."""
+        known = C.c_int(0)
+        _check(lib().cheetah_cuda_model_evict_unit(self._h, unit_id.encode(), C.byref(known)))
+        return bool(known.value)
 
     def close(self) -> None:
         if getattr(self, "_h", None):

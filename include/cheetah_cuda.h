@@ -92,6 +92,49 @@ CHEETAH_CUDA_API int cheetah_cuda_model_open(const char *prepared_dir, const Che
 CHEETAH_CUDA_API int cheetah_cuda_model_free(CheetahCudaModel *model);
 CHEETAH_CUDA_API int cheetah_cuda_model_info(const CheetahCudaModel *model, CheetahCudaModelInfo *info);
 
+/* Ant residency plan: the loader's `plan` argument (unit id -> "vram" /
+ * "ram" / "disk", `BackendLoader` `registry.rs:138-146`, produced by
+ * `Ant::plan_residency` `ant.rs:655-710`). Units it does not list are "vram". */
+typedef struct CheetahCudaResidency {
+    const char *const *unit_ids;
+    const char *const *tiers;
+    size_t count;
+} CheetahCudaResidency;
+
+/* `cheetah_cuda_model_open` with the Ant VRAM tier (`ant.rs:667-710`,
+ * `cheetah_memory.h:12-16`; the reference's GPU backend buckets weights the
+ * same way, `vulkan/transformer.rs:484-560`). The layer linears (q/k/v fused,
+ * o, gate, up, down) planned into "vram" get their own HBM copy; the others
+ * are kept in pinned host memory and streamed into one of two per-model
+ * staging slots (layer parity) before their layer runs, in every forward.
+ * A fused q/k/v linear is resident only when all three units are. The
+ * embedding, lm_head, norms and biases are always HBM-resident. A planned
+ * model runs without CUDA graphs, programmatic dependent launch or the
+ * persistent decode kernel, and serialises its forwards (the staging slots
+ * are shared). plan == NULL is `cheetah_cuda_model_open`. */
+CHEETAH_CUDA_API int cheetah_cuda_model_open_ex(const char *prepared_dir, const CheetahCudaConfig *config,
+                                                const char *quant, int device, const CheetahCudaResidency *plan,
+                                                CheetahCudaModel **out);
+/* `AntTierControl::page_in_unit` / `evict_unit` (`registry.rs:88-93`):
+ * tier 0 (CHEETAH_ANT_TIER_VRAM) uploads the unit's linear into its own HBM
+ * copy, tiers 1/2 and eviction release it (the pinned host copy stays
+ * authoritative, so later forwards stream it). *known = 0 for a unit id the
+ * units manifest does not list (no error); units that always stay resident
+ * report known = 1 and do not move. Only for models opened with a plan. */
+CHEETAH_CUDA_API int cheetah_cuda_model_page_in_unit(CheetahCudaModel *model, const char *unit_id, int tier,
+                                                     int *known);
+CHEETAH_CUDA_API int cheetah_cuda_model_evict_unit(CheetahCudaModel *model, const char *unit_id, int *known);
+typedef struct CheetahCudaResidencyInfo {
+    uint64_t resident_linear_bytes; /* layer linears with their own HBM copy */
+    uint64_t streamed_linear_bytes; /* layer linears streamed from pinned host memory */
+    uint64_t staging_bytes;         /* the two staging slots */
+    uint32_t resident_linears;
+    uint32_t streamed_linears;
+    int32_t planned;                /* 1: opened with a residency plan */
+    int32_t reserved;
+} CheetahCudaResidencyInfo;
+CHEETAH_CUDA_API int cheetah_cuda_model_residency(const CheetahCudaModel *model, CheetahCudaResidencyInfo *info);
+
 /* A sequence: an empty KV cache that shares the model's weights — the
  * `ModelForwardClone` contract (`registry.rs:95-117`, pinned by
  * `decoder.rs:1761`). One thread uses a sequence at a time. */
