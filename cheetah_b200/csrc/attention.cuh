@@ -153,45 +153,59 @@ __device__ __forceinline__ void merge_splits(const AttnParams &p, int b, int kvh
     __syncthreads();
     if (!*is_last) return;
     __threadfence();
-    // Per-head global max and split weights (warp g handles heads g, g+4).
+    // Per-head global max and split weights (warp g handles heads g, g+4):
+    // every split's (m, l) is loaded at once (kMaxSplits / 32 per lane), so
+    // the pass costs one L2 round trip; each lane folds its splits in split
+    // order before the warp sum.
+    constexpr int kPerLane = kMaxSplits / kWarp;
     for (int g = warp; g < group; g += kAttnWarps) {
+        float ms[kPerLane], ls[kPerLane];
+#pragma unroll
+        for (int k = 0; k < kPerLane; ++k) {
+            const int s2 = lane + k * kWarp;
+            const bool in = s2 < active;
+            ms[k] = in ? __ldcg(&p.part_ml[((base + s2) * kMaxGroup + g) * 2]) : -INFINITY;
+            ls[k] = in ? __ldcg(&p.part_ml[((base + s2) * kMaxGroup + g) * 2 + 1]) : 0.0f;
+        }
         float m = -INFINITY;
-        for (int s2 = lane; s2 < active; s2 += kWarp) m = fmaxf(m, __ldcg(&p.part_ml[((base + s2) * kMaxGroup + g) * 2]));
+#pragma unroll
+        for (int k = 0; k < kPerLane; ++k) m = fmaxf(m, ms[k]);
         m = warp_max(m);
         float l = 0.0f;
-        for (int s2 = lane; s2 < active; s2 += kWarp) {
-            const float ms = __ldcg(&p.part_ml[((base + s2) * kMaxGroup + g) * 2]);
-            const float w = (m == -INFINITY) ? 0.0f : expf(ms - m);
-            w_s[s2][g] = w;
-            l += w * __ldcg(&p.part_ml[((base + s2) * kMaxGroup + g) * 2 + 1]);
+#pragma unroll
+        for (int k = 0; k < kPerLane; ++k) {
+            const int s2 = lane + k * kWarp;
+            if (s2 < active) {
+                const float w = (m == -INFINITY) ? 0.0f : expf(ms[k] - m);
+                w_s[s2][g] = w;
+                l += w * ls[k];
+            }
         }
         l = warp_sum(l);
         if (lane == 0) big_l[g] = l;
     }
     __syncthreads();
-    // Weighted sum of the split outputs, four dimensions per thread.
+    // Weighted sum of the split outputs, four dimensions per thread, split
+    // order; 16 splits' loads in flight at a time.
     for (int i = threadIdx.x; i < group * (HD / 4); i += kAttnThreads) {
         const int g = i / (HD / 4), d4 = i % (HD / 4);
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
         const float4 *src = reinterpret_cast<const float4 *>(p.part_o + ((base * kMaxGroup) + g) * HD) + d4;
         const long long stride4 = (long long)kMaxGroup * HD / 4;
-        int s2 = 0;
-        for (; s2 + 8 <= active; s2 += 8) {
-            float4 v[8];
+        constexpr int kB = 16;
+        for (int s2 = 0; s2 < active; s2 += kB) {
+            float4 v[kB];
 #pragma unroll
-            for (int u = 0; u < 8; ++u) v[u] = __ldcg(src + (s2 + u) * stride4);
+            for (int u = 0; u < kB; ++u)
+                v[u] = s2 + u < active ? __ldcg(src + (s2 + u) * stride4) : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                const float w = w_s[s2 + u][g];
-                acc.x = fmaf(w, v[u].x, acc.x); acc.y = fmaf(w, v[u].y, acc.y);
-                acc.z = fmaf(w, v[u].z, acc.z); acc.w = fmaf(w, v[u].w, acc.w);
+            for (int u = 0; u < kB; ++u) {
+                if (s2 + u < active) {
+                    const float w = w_s[s2 + u][g];
+                    acc.x = fmaf(w, v[u].x, acc.x); acc.y = fmaf(w, v[u].y, acc.y);
+                    acc.z = fmaf(w, v[u].z, acc.z); acc.w = fmaf(w, v[u].w, acc.w);
+                }
             }
-        }
-        for (; s2 < active; ++s2) {
-            const float4 v = __ldcg(src + s2 * stride4);
-            const float w = w_s[s2][g];
-            acc.x = fmaf(w, v.x, acc.x); acc.y = fmaf(w, v.y, acc.y);
-            acc.z = fmaf(w, v.z, acc.z); acc.w = fmaf(w, v.w, acc.w);
         }
         const float l = big_l[g];
         const float inv = l > 0.0f ? 1.0f / l : 0.0f;

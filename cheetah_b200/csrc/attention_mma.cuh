@@ -94,6 +94,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
     __shared__ float w_s[kMaxSplits][kMaxGroup];
     __shared__ float big_l[kMaxGroup];
     __shared__ int is_last;
+    __shared__ int page_s[kMmaWarps][kMmaStages];  // page of the tile in each stage
 
     const AttnParams &p = mp.a;
     const int split = blockIdx.x;
@@ -134,14 +135,33 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
     const int my_count = t_end - t_begin > warp ? (t_end - t_begin - warp + kMmaWarps - 1) / kMmaWarps : 0;
     const int32_t *table = p.page_table + (long long)b * p.max_pages;
 
-    // Issue the TMA loads of this warp's i-th tile into stage i % kMmaStages.
-    auto issue = [&](int i) {
+    // Page of this warp's tiles i0 .. i0 + 31 (lane j: tile i0 + j): one
+    // coalesced page-table read per 32 tiles, so issuing a tile's loads never
+    // waits on a dependent global read. Called by all lanes, i warp-uniform.
+    int pg_lane = -1, pg_i0 = -1;
+    auto page_for = [&](int i) -> int {
+        const int i0 = i & ~(kWarp - 1);
+        if (i0 != pg_i0) {
+            pg_i0 = i0;
+            const int ti = i0 + lane;
+            pg_lane = -1;
+            if (ti < my_count) {
+                const int pidx = (t_begin + warp + ti * kMmaWarps) * TILE / mp.page_tokens;
+                pg_lane = pidx < p.max_pages ? table[pidx] : -1;
+            }
+        }
+        return __shfl_sync(0xFFFFFFFFu, pg_lane, i & (kWarp - 1));
+    };
+
+    // Issue the TMA loads of this warp's i-th tile (on `page`) into stage
+    // i % kMmaStages.
+    auto issue = [&](int i, int page) {
         const int tile = t_begin + warp + i * kMmaWarps;
         const int stage = i % kMmaStages;
         const uint32_t bar = smem_u32(&bars[warp][stage]);
         const int pos0 = tile * TILE;
         const int pidx = pos0 / mp.page_tokens;
-        const int page = pidx < p.max_pages ? table[pidx] : -1;
+        page_s[warp][stage] = page;
         if (page < 0 || page >= p.num_pages) {
             if (p.error) *p.error = 1;
             mbar_arrive(bar);  // complete the phase without data; the tile is masked
@@ -159,8 +179,14 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
         }
     };
 
-    if (lane == 0) {
-        for (int i = 0; i < kMmaStages && i < my_count; ++i) issue(i);
+    {
+        int pg0[kMmaStages];
+#pragma unroll
+        for (int i = 0; i < kMmaStages; ++i) pg0[i] = page_for(i);
+        if (lane == 0) {
+            for (int i = 0; i < kMmaStages && i < my_count; ++i) issue(i, pg0[i]);
+        }
+        __syncwarp();
     }
 
     // Q as bf16 A fragments (rows >= group are zero padding).
@@ -199,8 +225,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
             failed = true;
             break;
         }
-        const int pidx = pos0 / mp.page_tokens;
-        const int page = pidx < p.max_pages ? table[pidx] : -1;
+        const int page = page_s[warp][stage];
         const bool tile_ok = page >= 0 && page < p.num_pages;
         const uint32_t ks_base = smem_u32(warp_smem + stage * 2 * kTileBytes);
         const uint32_t vs_base = ks_base + kTileBytes;
@@ -268,7 +293,11 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
             }
         }
         __syncwarp();
-        if (lane == 0 && i + kMmaStages < my_count) issue(i + kMmaStages);
+        if (i + kMmaStages < my_count) {
+            const int pg = page_for(i + kMmaStages);
+            if (lane == 0) issue(i + kMmaStages, pg);
+            __syncwarp();
+        }
     }
     if (failed) {
         // Drain this warp's loads still in flight (bounded) before exiting.

@@ -3482,7 +3482,7 @@ int cheetah_cuda_op_decode_attention(const CheetahCudaDecodeAttention *a, void *
     p.part_ml = reinterpret_cast<float *>(scratch + o_bytes);
     p.tickets = tickets;
     p.error = nullptr;
-    if (!mma) return cheetah::launch_attention(p, (int)a->head_dim, a->kv_dtype == CHEETAH_CUDA_KV_F32, st, false);
+    if (!mma) return cheetah::launch_attention(p, (int)a->head_dim, a->kv_dtype == CHEETAH_CUDA_KV_F32, st, true);
     CUtensorMap k_map, v_map;
     const unsigned long long rows = (unsigned long long)a->num_pages * a->kv_heads * a->page_tokens;
     if (cheetah::make_kv_tensor_map(&k_map, a->k_pool, rows, (int)a->head_dim) != 0 ||
@@ -3493,7 +3493,10 @@ int cheetah_cuda_op_decode_attention(const CheetahCudaDecodeAttention *a, void *
     mp.a = p;
     mp.layer_row_offset = 0;
     mp.page_tokens = (int)a->page_tokens;
-    return cheetah::launch_attention_mma(k_map, v_map, mp, (int)a->head_dim, st, false);
+    // Programmatic dependent launch: the kernel sets up its barriers while
+    // the stream's previous kernel drains, and reads nothing before that
+    // kernel has completed (griddepcontrol.wait).
+    return cheetah::launch_attention_mma(k_map, v_map, mp, (int)a->head_dim, st, true);
 }
 
 int cheetah_cuda_op_prefill_attention(const CheetahCudaPrefillAttention *a, void *stream) {
