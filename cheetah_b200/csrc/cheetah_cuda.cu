@@ -2616,6 +2616,12 @@ int forward_batch_rows(Model *mp, Seq *const *seqs, const uint32_t *tokens, cons
                "cheetah_cuda_forward_batch: null argument");
     Model &m = *mp;
     const CheetahCudaConfig &c = m.cfg;
+    if (B == 1) {
+        // A batch of one: the single-sequence step (see forward_batch_greedy).
+        CH_REQUIRE(seqs[0] != nullptr && seqs[0]->m == &m, "cheetah_cuda_forward_batch: sequence of another model");
+        CH_REQUIRE(m.gemm_prefill, "cheetah_cuda_forward_batch: needs bf16 weights and a bf16 KV cache");
+        return forward(seqs[0], tokens, 1, offsets[0], row_logits ? row_logits[0] : nullptr, argmax_out);
+    }
     std::lock_guard<std::mutex> lock(m.batch_mutex);
     int M = 0, table_stride = 0;
     if (prepare_batch(m, seqs, tokens, offsets, B, 1, "cheetah_cuda_forward_batch", &M, &table_stride) != 0) return -1;
@@ -2795,12 +2801,22 @@ int forward_entry(Seq *s, const uint32_t *tokens, size_t n, size_t offset, float
 // by feeding its greedy ids to the next (batch_advance_kernel). The host
 // reads the token log every kChainSteps steps. tokens_out[b * steps + i] is
 // sequence b's greedy token after consuming position offsets[b] + i.
+int generate_greedy(Seq *s, uint32_t first_token, size_t offset, size_t steps, uint32_t *tokens_out);
+
 int forward_batch_greedy(Model *mp, Seq *const *seqs, const uint32_t *tokens, const size_t *offsets, size_t B,
                          size_t steps, uint32_t *tokens_out) {
     CH_REQUIRE(mp != nullptr && seqs != nullptr && tokens != nullptr && offsets != nullptr && tokens_out != nullptr,
                "cheetah_cuda_forward_batch_greedy: null argument");
     CH_REQUIRE(steps > 0, "cheetah_cuda_forward_batch_greedy: steps must be positive");
     Model &m = *mp;
+    // A batch of one runs the single-sequence greedy chain (the persistent
+    // decode kernel where the model has it): a batched step pays the fixed
+    // cost of ~5 launches per layer whatever its row count.
+    if (B == 1) {
+        CH_REQUIRE(seqs[0] != nullptr && seqs[0]->m == &m,
+                   "cheetah_cuda_forward_batch_greedy: sequence of another model");
+        return generate_greedy(seqs[0], tokens[0], offsets[0], steps, tokens_out);
+    }
     std::lock_guard<std::mutex> lock(m.batch_mutex);
     int M = 0, table_stride = 0;
     if (prepare_batch(m, seqs, tokens, offsets, B, steps, "cheetah_cuda_forward_batch_greedy", &M, &table_stride) != 0)

@@ -182,7 +182,8 @@ CHEETAH_CUDA_API int cheetah_cuda_model_coalesce_stats(const CheetahCudaModel *m
  * batch x vocab f32; argmax_out (nullable, host) each row's greedy token
  * (`engine.rs:2247-2253`). The batched form of `ModelForward::forward`
  * (`registry.rs:60`) for concurrent sequences (serve: `engine.rs:1874`,
- * `serve/queue.rs:48-67`). Needs bf16 weights and a bf16 KV cache. */
+ * `serve/queue.rs:48-67`). Needs bf16 weights and a bf16 KV cache. A
+ * batch of one runs the single-sequence step on the sequence's stream. */
 CHEETAH_CUDA_API int cheetah_cuda_forward_batch(CheetahCudaModel *model, CheetahCudaSeq *const *seqs,
                                                 const uint32_t *tokens, const size_t *offsets, size_t batch,
                                                 float *logits_out, uint32_t *argmax_out);
@@ -194,7 +195,9 @@ CHEETAH_CUDA_API int cheetah_cuda_forward_batch(CheetahCudaModel *model, Cheetah
  * The same results as `steps` calls of cheetah_cuda_forward_batch, each fed
  * the previous call's ids: the serving loop's greedy batch
  * (`engine.rs:1874`, `engine.rs:1920-1958`) between changes of the batch.
- * Needs bf16 weights and a bf16 KV cache. */
+ * Needs bf16 weights and a bf16 KV cache. A batch of one runs
+ * cheetah_cuda_generate_greedy (the persistent decode kernel where the model
+ * has it) on the sequence's stream. */
 CHEETAH_CUDA_API int cheetah_cuda_forward_batch_greedy(CheetahCudaModel *model, CheetahCudaSeq *const *seqs,
                                                        const uint32_t *tokens, const size_t *offsets,
                                                        size_t batch, size_t steps, uint32_t *tokens_out);
@@ -210,7 +213,8 @@ CHEETAH_CUDA_API int cheetah_cuda_generate_greedy(CheetahCudaSeq *seq, uint32_t 
 /* The sequence's CUDA stream (cudaStream_t) for event timing / synchronisation. */
 CHEETAH_CUDA_API int cheetah_cuda_seq_stream(const CheetahCudaSeq *seq, void **stream);
 /* The model's batch stream (cudaStream_t), on which cheetah_cuda_forward_batch
- * and cheetah_cuda_forward_batch_greedy run, for event timing. Created by the
+ * and cheetah_cuda_forward_batch_greedy run batches of two or more, for
+ * event timing. Created by the
  * first batched call; *stream is NULL before it. A harness accessor: the
  * reference times `forward` on the host (no counterpart in `registry.rs`). */
 CHEETAH_CUDA_API int cheetah_cuda_model_batch_stream(const CheetahCudaModel *model, void **stream);
