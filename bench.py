@@ -1053,14 +1053,45 @@ def case_batch_decode(batch: int, context: int, steps: int) -> int:
         prompt = rng.integers(0, cfg["vocab_size"], context).astype(np.uint32)
         toks.append(int(np.argmax(seq.forward(prompt, 0))))
         seqs.append(seq)
+    import torch
     pos = context
     for i in range(steps + 2):
         if i == 2:
+            torch.cuda.profiler.start()  # `ncu --profile-from-start off` captures the timed steps only
             t0 = time.perf_counter()
         toks = model.forward_batch(seqs, toks, [pos] * batch).tolist()
         pos += 1
     ms = (time.perf_counter() - t0) * 1e3 / steps
+    torch.cuda.profiler.stop()
     print(f"batch-decode B={batch} L={context}: {ms:.4f} ms/step (host-synchronous calls)")
+    return 0
+
+
+def case_attention(shape: str, batch: int, context: int, launches: int = 3) -> int:
+    """One config-2 case, `launches` plain back-to-back launches of the
+    decode attention op (no graph): the profiling target for one kernel."""
+    import torch
+    from cheetah_b200 import runtime as R
+    qh, kvh, D = (int(v) for v in shape.split("/"))
+    page = 64
+    pages_per = context // page
+    total = batch * pages_per
+    gen = torch.Generator(device="cuda").manual_seed(batch * 100003 + context + D)
+    k = torch.randn(total, kvh, page, D, device="cuda", dtype=torch.bfloat16, generator=gen)
+    v = torch.randn(total, kvh, page, D, device="cuda", dtype=torch.bfloat16, generator=gen)
+    table = torch.randperm(total, device="cuda", generator=gen).to(torch.int32).view(batch, pages_per).contiguous()
+    q = torch.randn(batch, qh, D, device="cuda", generator=gen)
+    lens = torch.full((batch,), context, dtype=torch.int32, device="cuda")
+    out = torch.empty_like(q)
+    R.decode_attention(q, k, v, table, lens, context, out=out)  # scratch allocation, function attributes
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(launches):
+        R.decode_attention(q, k, v, table, lens, context, out=out)
+    torch.cuda.synchronize()
+    us = (time.perf_counter() - t0) / launches * 1e6
+    print(f"attention {shape} B={batch} L={context}: 1 + {launches} launches, {us:.1f} us each after the "
+          "first (host clock)")
     return 0
 
 
@@ -1132,11 +1163,13 @@ def main():
     ap.add_argument("--prompt-7b", type=int, default=1024, help="decode-7b-* workloads: prompt tokens")
     ap.add_argument("--workload", default="default",
                     choices=["default", "decode-7b-q8", "decode-7b-q4", "decode-7b-bf16", "serve-0.5b",
-                             "prefill-0.5b", "attention", "gemv-q8", "gemv-q4", "batch-decode"])
+                             "prefill-0.5b", "attention", "attention-case", "gemv-q8", "gemv-q4",
+                             "batch-decode"])
     ap.add_argument("--rows", type=int, default=18944, help="gemv-q8/q4 case")
     ap.add_argument("--cols", type=int, default=3584, help="gemv-q8/q4 case")
     ap.add_argument("--batch", type=int, default=32, help="batch-decode case")
-    ap.add_argument("--context", type=int, default=4096, help="batch-decode case")
+    ap.add_argument("--context", type=int, default=4096, help="batch-decode / attention-case")
+    ap.add_argument("--shape", default="14/2/64", help="attention-case: q_heads/kv_heads/head_dim")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -1151,6 +1184,8 @@ def main():
         return case_gemv(args.workload.split("-")[1], args.rows, args.cols)
     if args.workload == "batch-decode":
         return case_batch_decode(args.batch, args.context, args.steps)
+    if args.workload == "attention-case":
+        return case_attention(args.shape, args.batch, args.context)
     if world > 1 or args.workload == "serve-0.5b":
         return run_serve(args)
     return run_ours(args)

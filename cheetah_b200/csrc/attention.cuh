@@ -110,7 +110,7 @@ __device__ __forceinline__ void split_range(int span, int splits, int split, int
 
 // Merge this CTA's partial (m, l, o) into the per-split scratch, then the
 // last CTA to arrive merges all active splits into `out`.
-template <int HD>
+template <int HD, int NW = kAttnWarps>
 __device__ __forceinline__ void merge_splits(const AttnParams &p, int b, int kvh, int split, int active,
                                              int group, float (*m_s)[kMaxGroup], float (*l_s)[kMaxGroup],
                                              float (*o_s)[kMaxGroup][HD], float (*w_s)[kMaxGroup],
@@ -119,14 +119,14 @@ __device__ __forceinline__ void merge_splits(const AttnParams &p, int b, int kvh
     const int lane = threadIdx.x % kWarp;
     const long long base = ((long long)b * p.kv_heads + kvh) * p.splits;
     const long long part = base + split;
-    for (int i = threadIdx.x; i < group * HD; i += kAttnThreads) {
+    for (int i = threadIdx.x; i < group * HD; i += (NW * kWarp)) {
         const int g = i / HD, d = i % HD;
         float m = -INFINITY;
 #pragma unroll
-        for (int w = 0; w < kAttnWarps; ++w) m = fmaxf(m, m_s[w][g]);
+        for (int w = 0; w < NW; ++w) m = fmaxf(m, m_s[w][g]);
         float l = 0.0f, o = 0.0f;
 #pragma unroll
-        for (int w = 0; w < kAttnWarps; ++w) {
+        for (int w = 0; w < NW; ++w) {
             const float f = (m == -INFINITY) ? 0.0f : expf(m_s[w][g] - m);
             l += l_s[w][g] * f;
             o += o_s[w][g][d] * f;
@@ -158,7 +158,7 @@ __device__ __forceinline__ void merge_splits(const AttnParams &p, int b, int kvh
     // the pass costs one L2 round trip; each lane folds its splits in split
     // order before the warp sum.
     constexpr int kPerLane = kMaxSplits / kWarp;
-    for (int g = warp; g < group; g += kAttnWarps) {
+    for (int g = warp; g < group; g += NW) {
         float ms[kPerLane], ls[kPerLane];
 #pragma unroll
         for (int k = 0; k < kPerLane; ++k) {
@@ -187,7 +187,7 @@ __device__ __forceinline__ void merge_splits(const AttnParams &p, int b, int kvh
     __syncthreads();
     // Weighted sum of the split outputs, four dimensions per thread, split
     // order; 16 splits' loads in flight at a time.
-    for (int i = threadIdx.x; i < group * (HD / 4); i += kAttnThreads) {
+    for (int i = threadIdx.x; i < group * (HD / 4); i += (NW * kWarp)) {
         const int g = i / (HD / 4), d4 = i % (HD / 4);
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
         const float4 *src = reinterpret_cast<const float4 *>(p.part_o + ((base * kMaxGroup) + g) * HD) + d4;

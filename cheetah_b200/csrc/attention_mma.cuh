@@ -88,9 +88,9 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
     constexpr int TILE = T::kRows;
     extern __shared__ __align__(1024) uint8_t dyn_smem[];
     __shared__ __align__(8) uint64_t bars[kMmaWarps][kMmaStages];
-    __shared__ float m_s[kAttnWarps][kMaxGroup];
-    __shared__ float l_s[kAttnWarps][kMaxGroup];
-    __shared__ __align__(16) float o_s[kAttnWarps][kMaxGroup][HD];
+    __shared__ float m_s[kMmaWarps][kMaxGroup];
+    __shared__ float l_s[kMmaWarps][kMaxGroup];
+    __shared__ __align__(16) float o_s[kMmaWarps][kMaxGroup][HD];
     __shared__ float w_s[kMaxSplits][kMaxGroup];
     __shared__ float big_l[kMaxGroup];
     __shared__ int is_last;
@@ -326,7 +326,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
         }
     }
     __syncthreads();
-    merge_splits<HD>(p, b, kvh, split, active, group, m_s, l_s, o_s, w_s, big_l, &is_last);
+    merge_splits<HD, kMmaWarps>(p, b, kvh, split, active, group, m_s, l_s, o_s, w_s, big_l, &is_last);
 }
 
 inline size_t mma_attention_smem() { return (size_t)kMmaWarps * kMmaStages * 2 * kTileBytes + 1024; }
