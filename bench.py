@@ -649,10 +649,13 @@ def serve_run(torch, R, model_dir, cfg, world, rank, local, hbm_peak, reqs, prom
             s.restore_kv_prefix(sn, offs[j])
         torch.cuda.synchronize()
 
-    # Warm-up: one short chained call captures the step graphs of the
-    # first batch size.
+    # Warm-up: one untimed pass of the whole decode (both forms) captures the
+    # step graph of every (batch rows, page-table width) the run meets, so
+    # the timed passes replay graphs only; the K/V is rewound after each.
     if seqs:
-        model.forward_batch_greedy(seqs, first, offs, 1)
+        decode(True)
+        rewind()
+        decode(False)
         rewind()
     stream = torch.cuda.ExternalStream(model.batch_stream_handle()) if seqs else torch.cuda.current_stream()
     if world > 1:
@@ -821,7 +824,8 @@ def run_serve(args):
                 "e2e": summ["e2e"], "gpu_launches": launches, "clocks": summ["clocks"],
                 "roofline": summ["roofline"] | {"peak_kind": peak_kind},
                 "serve": {k: v for k, v in summ.items() if k not in ("e2e", "roofline", "clocks")},
-                "warmup_note": "one chained step per rank captures the step graphs before the timed region"}
+                "warmup_note": "one untimed pass of the whole decode per rank (chained and per-step forms) "
+                               "captures every step graph before the timed region"}
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.barrier()
