@@ -147,3 +147,34 @@ def test_residency_needs_a_plan(tiny_prepared):
         model.evict_unit("model.layers.0.mlp.up_proj.weight")
     with pytest.raises(R.CheetahCudaError, match="unknown Ant tier"):
         R.CudaModel(tiny_prepared, max_positions=256, residency={"model.layers.0.mlp.up_proj.weight": "hbm"})
+
+
+def test_real_05b_shape_half_streamed_decodes_like_the_resident_model():
+    """The 0.5B shape planned into a VRAM pool of half its bytes (17 layers
+    partly streamed): prefill and 16 greedy steps give the resident model's
+    logits bit for bit (same kernels, operands copied from host memory)."""
+    from cheetah_b200 import runtime as R
+    from cheetah_b200.ant import layer_residency_summary
+    from cheetah_b200.prepared import cached_synthetic
+    root = cached_synthetic("qwen2-0.5b")
+    pm = PreparedModel(root)
+    cfg = resolve_config(pm)
+    units = units_of(pm)
+    plan = plan_residency(units, vram_pool_bytes=sum(u.bytes for u in units) // 2, ram_budget_bytes=1 << 40)
+    states = [e.state() for e in layer_residency_summary(units, plan)]
+    assert "partial" in states and "full_vram" in states
+    planned = R.CudaModel(root, max_positions=1024, residency=plan)
+    assert planned.residency()["streamed_linears"] > 0
+    plain = _plain(root, "bf16")
+    prompt = np.random.default_rng(21).integers(0, cfg["vocab_size"], 200).astype(np.uint32)
+    a, b = planned.new_sequence(), plain.new_sequence()
+    la, lb = a.forward(prompt, 0), b.forward(prompt, 0)
+    np.testing.assert_array_equal(la, lb)
+    tok, pos = int(np.argmax(la)), len(prompt)
+    for _ in range(16):
+        ga, gb = np.empty_like(la), np.empty_like(lb)
+        ta = a.forward_greedy([tok], pos, logits_out=ga)
+        tb = b.forward_greedy([tok], pos, logits_out=gb)
+        np.testing.assert_array_equal(ga, gb)
+        assert ta == tb
+        tok, pos = ta, pos + 1

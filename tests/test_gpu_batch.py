@@ -204,3 +204,26 @@ def test_concurrent_clone_forwards_are_batched_and_match_oracle(tiny_prepared, m
             else:
                 break  # a near-tie sent the serial run down another path
     model.close()
+
+
+def test_batch_of_one_is_the_single_sequence_path(tiny_prepared):
+    """A batched call with one sequence runs the single-sequence path: its
+    greedy chain equals `generate_greedy` on a twin sequence token for
+    token, and a one-row `forward_batch` equals `forward` bit for bit."""
+    from cheetah_b200 import runtime as R
+    from tests.greedy import reference_choice
+    pm = PreparedModel(tiny_prepared)
+    cfg = resolve_config(pm)
+    model = R.CudaModel(tiny_prepared, max_positions=512)
+    prompt = np.random.default_rng(8).integers(0, cfg["vocab_size"], 37).astype(np.uint32)
+    a, b, c, d = (model.new_sequence() for _ in range(4))
+    first = int(np.argmax(a.forward(prompt, 0)))
+    for s in (b, c, d):
+        s.forward(prompt, 0)
+    chained = model.forward_batch_greedy([a], [first], [37], 24)
+    alone = b.generate_greedy(first, 37, 24)
+    assert np.array_equal(chained[0], alone)
+    ids, logits = model.forward_batch([c], [first], [37], want_logits=True)
+    ref = d.forward([first], 37)
+    np.testing.assert_array_equal(logits[0], ref)
+    assert int(ids[0]) == reference_choice(ref)
