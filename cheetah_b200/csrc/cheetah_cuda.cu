@@ -1995,6 +1995,22 @@ int launch_prefill_attention(PrefillAttnParams ap, const CUtensorMap &q_map, con
         }
         return 0;
     }
+    if (head_dim == 128 && env_flag("CHEETAH_PREFILL_TC", true)) {
+        // The same split rule for head_dim 128 (O accumulated in TMEM).
+        const int blocks = ((M + kTcRows - 1) / kTcRows) * ap.q_heads;
+        const int key_tiles = (int)((offset + M + kTcKeys - 1) / kTcKeys);
+        ap.splits = std::max(1, std::min(std::min(kPrefillMaxSplits, sms / blocks), key_tiles / 2));
+        const size_t tsmem = prefill_attention_tc128_smem();
+        CH_CUDA_TRY(cudaFuncSetAttribute(prefill_attention_tc128_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)tsmem));
+        dim3 tgrid((M + kTcRows - 1) / kTcRows, ap.q_heads, ap.splits);
+        CH_CUDA_TRY(launch_ex(prefill_attention_tc128_kernel, tgrid, dim3(kTcThreads), tsmem, st, pdl, q_map, k_map,
+                              v_map, ap));
+        if (ap.splits > 1) {
+            CH_CUDA_TRY(launch_ex(prefill_merge_kernel<128>, dim3(2 * sms), dim3(256), 0, st, pdl, ap));
+        }
+        return 0;
+    }
     const size_t asmem = prefill_attention_smem();
     // Key-range splits: about two CTAs per SM (each CTA covers >= 4 key tiles).
     const int blocks = ((M + 15) / 16) * ap.kv_heads;

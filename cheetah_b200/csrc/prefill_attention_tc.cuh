@@ -382,4 +382,354 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
 }
 
+// ---- head_dim 128 --------------------------------------------------------
+// The same contract for head_dim 128 (the 7B / 1.5B shapes). Differences from
+// the head_dim-64 kernel: Q and every K / V tile are two 64-dimension halves
+// (K-major, 128-byte swizzle), loaded as 32-row boxes of the cache's tensor
+// maps; S = Q K^T takes eight K=16 steps across the halves; O = P V is two
+// N=64 MMAs (one per V half) that accumulate into one 128-column O in TMEM
+// across all key tiles. A softmax thread keeps no O in registers: when its
+// warp's running max grows (alpha < 1 for some row) it rescales its O row in
+// TMEM (load, multiply, store) before releasing P_j; rows whose max did not
+// grow are multiplied by 1 (exact). The last tile's O is read back once,
+// normalised and stored. Two K/V stages of 64 KB (shared memory: Q 32 KB,
+// ring 128 KB, P 32 KB).
+constexpr int kTc2Stages = 2;
+constexpr int kTc2QBytes = kTcRows * 128 * 2;    // 32 KB (two 16 KB halves)
+constexpr int kTc2KvBytes = kTcKeys * 128 * 2;   // 32 KB per K or V tile (two halves)
+constexpr int kTc2Half = kTcKeys * 128;          // bytes of one 64-dimension half (128 rows x 128 B)
+constexpr int kTc2OCol = 2 * kTcKeys;            // O: 128 TMEM columns after S0 | S1
+
+inline size_t prefill_attention_tc128_smem() {
+    return (size_t)kTc2QBytes + (size_t)kTc2Stages * 2 * kTc2KvBytes + kTcPBytes + 1024;
+}
+
+__global__ void __launch_bounds__(kTcThreads, 1)
+    prefill_attention_tc128_kernel(const __grid_constant__ CUtensorMap q_map,
+                                   const __grid_constant__ CUtensorMap k_map,
+                                   const __grid_constant__ CUtensorMap v_map, const PrefillAttnParams p) {
+    constexpr int HD = 128;
+    constexpr int kBoxRows = kTileBytes / (HD * 2);  // 32: rows of one cache-map box
+    constexpr uint32_t kIdescS = umma_idesc_bf16(kTcRows, kTcKeys);
+    constexpr uint32_t kIdescPV = umma_idesc_bf16(kTcRows, 64) | (1u << 16);  // B (V) MN-major
+    extern __shared__ __align__(1024) uint8_t attn_tc2_smem[];
+    __shared__ __align__(8) uint64_t q_full;
+    __shared__ __align__(8) uint64_t kv_full[kTc2Stages];
+    __shared__ __align__(8) uint64_t kv_empty[kTc2Stages];
+    __shared__ __align__(8) uint64_t s_full[2];
+    __shared__ __align__(8) uint64_t s_empty[2];
+    __shared__ __align__(8) uint64_t p_full;
+    __shared__ __align__(8) uint64_t o_full;
+    __shared__ __align__(8) uint64_t drain_bar;
+    __shared__ uint32_t tmem_base_s;
+    __shared__ int abort_s;
+
+    uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(attn_tc2_smem) + 1023) & ~uintptr_t(1023));
+    uint8_t *q_s = base;
+    uint8_t *ring = q_s + kTc2QBytes;
+    uint8_t *p_s = ring + kTc2Stages * 2 * kTc2KvBytes;
+    const int warp = threadIdx.x / kWarp;
+    const int lane = threadIdx.x % kWarp;
+    const int group = p.q_heads / p.kv_heads;
+    const int head = blockIdx.y;
+    const int kvh = head / group;
+    const int t0 = blockIdx.x * kTcRows;
+    const int t_last = min(p.T, t0 + kTcRows) - 1;
+    const int pos_first = p.offset + t0;
+    const int pos_last = p.offset + t_last;
+    int ws = 0;
+    if (p.window > 0) ws = max(0, pos_first + 1 - p.window);
+    const int all_lo = ws / kTcKeys;
+    const int all_hi = pos_last / kTcKeys + 1;
+    const int per_split = (all_hi - all_lo + p.splits - 1) / p.splits;
+    const int split = blockIdx.z;
+    const int tile_lo = all_lo + split * per_split;
+    const int tile_hi = min(all_hi, tile_lo + per_split);
+    const int n_tiles = max(0, tile_hi - tile_lo);
+
+    if (threadIdx.x == 0) {
+        mbar_init(smem_u32(&q_full), 1);
+        for (int s = 0; s < kTc2Stages; ++s) {
+            mbar_init(smem_u32(&kv_full[s]), 1);
+            mbar_init(smem_u32(&kv_empty[s]), 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(smem_u32(&s_full[b]), 1);
+            mbar_init(smem_u32(&s_empty[b]), kTcRows);
+        }
+        mbar_init(smem_u32(&p_full), kTcRows);
+        mbar_init(smem_u32(&o_full), 1);
+        mbar_init(smem_u32(&drain_bar), 1);
+        abort_s = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_s)),
+                     "r"((uint32_t)kTcTmemCols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_base_s;
+
+    pdl_wait();
+    pdl_launch_dependents();
+
+    int issued = 0;  // K/V tiles the producer has requested
+    if (warp == 0) {
+        if (lane == 0 && n_tiles > 0) {
+            mbar_expect_tx(smem_u32(&q_full), kTc2QBytes);
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+                tma_load_2d(smem_u32(q_s + h * kTc2Half), &q_map, head * HD + h * 64, t0, smem_u32(&q_full));
+            for (int j = 0; j < n_tiles; ++j) {
+                const int s = j % kTc2Stages;
+                if (!mbar_wait(smem_u32(&kv_empty[s]), ((j / kTc2Stages) & 1) ^ 1)) {
+                    abort_s = 1;
+                    break;
+                }
+                const int tile = tile_lo + j;
+                // Pool rows of the tile's two 64-key spans (a span never
+                // crosses a page). A span past the chunk's last position holds
+                // only masked keys: it re-reads span 0 so the ring stays finite.
+                int rows[2];
+#pragma unroll
+                for (int b = 0; b < 2; ++b) {
+                    const int pos0 = tile * kTcKeys + b * 64;
+                    const int pidx = pos0 / p.page_tokens;
+                    const int page = pidx < p.max_pages ? p.page_table[pidx] : -1;
+                    if (page < 0 || page >= p.num_pages) {
+                        if (b == 0 || pos0 <= pos_last) {
+                            if (p.error) *p.error = 6;
+                        }
+                        rows[b] = b == 0 ? (int)p.layer_row_offset : rows[0];
+                    } else {
+                        rows[b] = (int)(p.layer_row_offset + ((long long)page * p.kv_heads + kvh) * p.page_tokens +
+                                        (pos0 - pidx * p.page_tokens));
+                    }
+                    if (b == 1 && pos0 > pos_last) rows[1] = rows[0];
+                }
+                uint8_t *ks = ring + s * 2 * kTc2KvBytes;
+                uint8_t *vs = ks + kTc2KvBytes;
+                const uint32_t bar = smem_u32(&kv_full[s]);
+                mbar_expect_tx(bar, 2 * kTc2KvBytes);
+#pragma unroll
+                for (int b = 0; b < 2; ++b) {
+#pragma unroll
+                    for (int r = 0; r < 64 / kBoxRows; ++r) {
+                        const uint32_t row_off = (uint32_t)((b * 64 + r * kBoxRows) * 128);
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            tma_load_2d(smem_u32(ks + h * kTc2Half + row_off), &k_map, h * 64, rows[b] + r * kBoxRows,
+                                        bar);
+                            tma_load_2d(smem_u32(vs + h * kTc2Half + row_off), &v_map, h * 64, rows[b] + r * kBoxRows,
+                                        bar);
+                        }
+                    }
+                }
+                issued = j + 1;
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && n_tiles > 0) {
+            const uint32_t q_addr = smem_u32(q_s);
+            const uint32_t p_addr = smem_u32(p_s);
+            bool ok = mbar_wait(smem_u32(&q_full), 0);
+            auto issue_s = [&](int j) -> bool {
+                const int s = j % kTc2Stages;
+                if (!mbar_wait(smem_u32(&kv_full[s]), (j / kTc2Stages) & 1)) return false;
+                if (!mbar_wait(smem_u32(&s_empty[j & 1]), ((j >> 1) & 1) ^ 1)) return false;
+                tc_fence_after();
+                const uint32_t k_addr = smem_u32(ring + s * 2 * kTc2KvBytes);
+                const uint32_t d = tmem + (uint32_t)((j & 1) * kTcKeys);
+#pragma unroll
+                for (int k = 0; k < HD / 16; ++k) {
+                    const uint32_t off = (uint32_t)((k >> 2) * kTc2Half + (k & 3) * 32);
+                    umma_bf16(d, umma_smem_desc(q_addr + off), umma_smem_desc(k_addr + off), kIdescS, k > 0 ? 1u : 0u);
+                }
+                umma_commit(smem_u32(&s_full[j & 1]));
+                return true;
+            };
+            if (ok) ok = issue_s(0);
+            for (int j = 0; ok && j < n_tiles; ++j) {
+                if (j + 1 < n_tiles && !issue_s(j + 1)) {
+                    ok = false;
+                    break;
+                }
+                if (!mbar_wait(smem_u32(&p_full), j & 1)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const int s = j % kTc2Stages;
+                const uint32_t v_addr = smem_u32(ring + s * 2 * kTc2KvBytes + kTc2KvBytes);
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+#pragma unroll
+                    for (int k = 0; k < kTcKeys / 16; ++k) {
+                        umma_bf16(tmem + kTc2OCol + h * 64,
+                                  umma_smem_desc(p_addr + (k >> 2) * (kTcRows * 128) + (k & 3) * 32),
+                                  umma_smem_desc_mn(v_addr + h * kTc2Half + k * 2048), kIdescPV,
+                                  (j > 0 || k > 0) ? 1u : 0u);
+                    }
+                }
+                umma_commit(smem_u32(&o_full));
+                umma_commit(smem_u32(&kv_empty[s]));
+            }
+            if (!ok) abort_s = 1;
+        }
+    } else {
+        // Softmax warps 2..5: TMEM lane quadrant = warp % 4; thread = query row.
+        const int quad = warp % 4;
+        const int r = quad * 32 + lane;
+        const int t = t0 + r;
+        const int qpos = p.offset + t;
+        const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+        const uint32_t o_addr = tmem + lane_off + kTc2OCol;
+        const float scale_log2 = p.scale * 1.4426950408889634f;
+        float m_run = -INFINITY, l_run = 0.0f;
+        bool ok = true;
+        uint8_t *p_row0 = p_s + r * 128;
+        for (int j = 0; j < n_tiles; ++j) {
+            // Waits decide warp-uniformly (the TMEM accesses below are warp-wide).
+            if (!__all_sync(0xFFFFFFFFu, mbar_wait(smem_u32(&s_full[j & 1]), (j >> 1) & 1))) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            float sc[kTcKeys];
+            const uint32_t s_addr = tmem + lane_off + (uint32_t)((j & 1) * kTcKeys);
+#pragma unroll
+            for (int c = 0; c < kTcKeys / 32; ++c) tmem_ld32_nowait(s_addr + c * 32, sc + c * 32);
+            tmem_wait_ld();
+            tc_fence_before();
+            mbar_arrive(smem_u32(&s_empty[j & 1]));
+            const int kp0 = (tile_lo + j) * kTcKeys;
+            if (p.window > 0 || kp0 + kTcKeys - 1 > pos_first) {
+                const int lim = qpos - kp0;
+                const int wlo = p.window > 0 ? lim - p.window : -1;
+#pragma unroll
+                for (int i = 0; i < kTcKeys; ++i) sc[i] = (i <= lim && i > wlo) ? sc[i] : -INFINITY;
+            }
+            float mx[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) mx[k] = sc[k];
+#pragma unroll
+            for (int i = 8; i < kTcKeys; ++i) mx[i & 7] = fmaxf(mx[i & 7], sc[i]);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) mx[k] = fmaxf(mx[k], mx[k + 4]);
+            const float tmax = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+            const float m_new = fmaxf(m_run, tmax * scale_log2);
+            const float alpha = m_new == -INFINITY ? 1.0f : exp2f(m_run - m_new);
+            const float neg_m = m_new == -INFINITY ? 0.0f : -m_new;
+            float sums[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) sums[k] = 0.0f;
+            uint32_t packed[kTcKeys / 2];
+#pragma unroll
+            for (int i = 0; i < kTcKeys / 2; ++i) {
+                const float e0 = fast_exp2(fmaf(sc[2 * i], scale_log2, neg_m));
+                const float e1 = fast_exp2(fmaf(sc[2 * i + 1], scale_log2, neg_m));
+                sums[i & 7] += e0 + e1;
+                packed[i] = pack_bf16(e0, e1);
+            }
+#pragma unroll
+            for (int k = 0; k < 4; ++k) sums[k] += sums[k + 4];
+            const float rsum = (sums[0] + sums[1]) + (sums[2] + sums[3]);
+            l_run = l_run * alpha + rsum;
+            m_run = m_new;
+            if (j > 0) {
+                // PV_{j-1} done: P's buffer is free and O holds tiles < j.
+                if (!__all_sync(0xFFFFFFFFu, mbar_wait(smem_u32(&o_full), (j - 1) & 1))) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                // O *= alpha where any row of the warp's max grew (warp-wide
+                // TMEM access; alpha == 1 rows are unchanged).
+                if (__any_sync(0xFFFFFFFFu, alpha < 1.0f)) {
+#pragma unroll 1
+                    for (int c = 0; c < HD / 32; ++c) {
+                        float ov[32];
+                        tmem_ld32_nowait(o_addr + c * 32, ov);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) ov[i] *= alpha;
+                        tmem_st32(o_addr + c * 32, ov);
+                    }
+                }
+                tc_fence_before();
+            }
+#pragma unroll
+            for (int c = 0; c < kTcKeys / 8; ++c) {
+                const int blk = c >> 3, cc = c & 7;
+                uint4 *dst = reinterpret_cast<uint4 *>(p_row0 + blk * (kTcRows * 128) + ((cc ^ (r & 7)) << 4));
+                *dst = make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2], packed[4 * c + 3]);
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            mbar_arrive(smem_u32(&p_full));
+        }
+        if (ok && n_tiles > 0) {
+            if (__all_sync(0xFFFFFFFFu, mbar_wait(smem_u32(&o_full), (n_tiles - 1) & 1))) {
+                tc_fence_after();
+            } else {
+                ok = false;
+            }
+        }
+        if (!ok) {
+            abort_s = 1;
+        } else if (n_tiles > 0) {
+            // O row from TMEM (warp-wide loads), then partial or output.
+            const bool live = t <= t_last;
+            const float inv = l_run > 0.0f ? 1.0f / l_run : 0.0f;
+            const long long rh = ((long long)split * p.T + t) * p.q_heads + head;
+#pragma unroll 1
+            for (int c = 0; c < HD / 32; ++c) {
+                float ov[32];
+                tmem_ld32_nowait(o_addr + c * 32, ov);
+                tmem_wait_ld();
+                if (!live) continue;
+                if (p.splits > 1) {
+                    float4 *dst = reinterpret_cast<float4 *>(p.part_o + rh * HD + c * 32);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) dst[i] = make_float4(ov[4 * i], ov[4 * i + 1], ov[4 * i + 2], ov[4 * i + 3]);
+                } else {
+                    uint4 *dst = reinterpret_cast<uint4 *>(p.out + (long long)t * p.q_heads * HD + head * HD + c * 32);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        dst[i] = make_uint4(pack_bf16(ov[8 * i] * inv, ov[8 * i + 1] * inv),
+                                            pack_bf16(ov[8 * i + 2] * inv, ov[8 * i + 3] * inv),
+                                            pack_bf16(ov[8 * i + 4] * inv, ov[8 * i + 5] * inv),
+                                            pack_bf16(ov[8 * i + 6] * inv, ov[8 * i + 7] * inv));
+                    }
+                }
+            }
+            if (live && p.splits > 1) *reinterpret_cast<float2 *>(p.part_ml + rh * 2) = make_float2(m_run, l_run);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (abort_s) {
+        // A wait gave up: let this CTA's copies and MMAs still in flight land
+        // before its shared memory and TMEM are released (bounded waits).
+        if (warp == 0 && lane == 0 && n_tiles > 0) {
+            mbar_wait(smem_u32(&q_full), 0);
+            for (int j = max(0, issued - kTc2Stages); j < issued; ++j) {
+                mbar_wait(smem_u32(&kv_full[j % kTc2Stages]), (j / kTc2Stages) & 1);
+            }
+        } else if (warp == 1 && lane == 0) {
+            umma_commit(smem_u32(&drain_bar));
+            mbar_wait(smem_u32(&drain_bar), 0);
+        }
+        tc_fence_before();
+        __syncthreads();
+        if (threadIdx.x == 0 && p.error) *p.error = 8;
+    }
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)kTcTmemCols));
+    }
+}
+
 }  // namespace cheetah

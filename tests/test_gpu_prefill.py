@@ -103,15 +103,16 @@ def test_config3_shape_chunked_equals_stepwise(monkeypatch):
     assert np.abs(ka - kb).max() < 5e-2 * max(1.0, np.abs(kb).max())
 
 
+@pytest.mark.parametrize("fixture", ["tiny_prepared", "tiny7b_prepared"])
 @pytest.mark.parametrize("chunk", ["256", "512"])
-def test_prefill_attention_key_splits_match_oracle(tiny_prepared, chunk, monkeypatch):
+def test_prefill_attention_key_splits_match_oracle(fixture, chunk, monkeypatch, request):
     """A long cached prefix at an odd offset, then a multi-chunk prompt: the
     tensor-core attention splits each row block's key range over several CTAs
     (merged afterwards) and crosses 128-key tiles and 64-token pages
-    mid-chunk. Checked against the oracle and against the mma.sync kernel
-    (CHEETAH_PREFILL_TC=0)."""
+    mid-chunk, for head_dim 64 and 128. Checked against the oracle and
+    against the mma.sync kernel (CHEETAH_PREFILL_TC=0)."""
     monkeypatch.setenv("CHEETAH_PREFILL_CHUNK", chunk)
-    cfg, ref, model = _models(tiny_prepared)
+    cfg, ref, model = _models(request.getfixturevalue(fixture))
     toks = _toks(1700, cfg["vocab_size"], 19)
     seq = model.new_sequence()
     seq.forward(toks[:1003], 0)
