@@ -2000,12 +2000,12 @@ int launch_prefill_attention(PrefillAttnParams ap, const CUtensorMap &q_map, con
         const int blocks = ((M + kTcRows - 1) / kTcRows) * ap.q_heads;
         const int key_tiles = (int)((offset + M + kTcKeys - 1) / kTcKeys);
         ap.splits = std::max(1, std::min(std::min(kPrefillMaxSplits, sms / blocks), key_tiles / 2));
-        const size_t tsmem = prefill_attention_tc128_smem();
-        CH_CUDA_TRY(cudaFuncSetAttribute(prefill_attention_tc128_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)tsmem));
+        const size_t tsmem = prefill_attention_tc2_smem<128>();
+        CH_CUDA_TRY(cudaFuncSetAttribute(prefill_attention_tc2_kernel<128>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tsmem));
         dim3 tgrid((M + kTcRows - 1) / kTcRows, ap.q_heads, ap.splits);
-        CH_CUDA_TRY(launch_ex(prefill_attention_tc128_kernel, tgrid, dim3(kTcThreads), tsmem, st, pdl, q_map, k_map,
-                              v_map, ap));
+        CH_CUDA_TRY(launch_ex(prefill_attention_tc2_kernel<128>, tgrid, dim3(kTcThreads), tsmem, st, pdl, q_map,
+                              k_map, v_map, ap));
         if (ap.splits > 1) {
             CH_CUDA_TRY(launch_ex(prefill_merge_kernel<128>, dim3(2 * sms), dim3(256), 0, st, pdl, ap));
         }

@@ -382,9 +382,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
 }
 
-// ---- head_dim 128 --------------------------------------------------------
-// The same contract for head_dim 128 (the 7B / 1.5B shapes). Differences from
-// the head_dim-64 kernel: Q and every K / V tile are two 64-dimension halves
+// ---- O accumulated in TMEM (head_dim 64 and 128) ---------------------------
+// The same contract with O kept in TMEM instead of registers. Differences from
+// the kernel above: Q and every K / V tile are two 64-dimension halves
 // (K-major, 128-byte swizzle), loaded as 32-row boxes of the cache's tensor
 // maps; S = Q K^T takes eight K=16 steps across the halves; O = P V is two
 // N=64 MMAs (one per V half) that accumulate into one 128-column O in TMEM
@@ -392,27 +392,40 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 // warp's running max grows (alpha < 1 for some row) it rescales its O row in
 // TMEM (load, multiply, store) before releasing P_j; rows whose max did not
 // grow are multiplied by 1 (exact). The last tile's O is read back once,
-// normalised and stored. Two K/V stages of 64 KB (shared memory: Q 32 KB,
-// ring 128 KB, P 32 KB).
-constexpr int kTc2Stages = 2;
-constexpr int kTc2QBytes = kTcRows * 128 * 2;    // 32 KB (two 16 KB halves)
-constexpr int kTc2KvBytes = kTcKeys * 128 * 2;   // 32 KB per K or V tile (two halves)
-constexpr int kTc2Half = kTcKeys * 128;          // bytes of one 64-dimension half (128 rows x 128 B)
-constexpr int kTc2OCol = 2 * kTcKeys;            // O: 128 TMEM columns after S0 | S1
+// normalised and stored. At head_dim 128: two K/V stages of 64 KB (Q 32 KB, ring
+// 128 KB, P 32 KB); at 64: three of 32 KB.
+template <int HD>
+struct Tc2 {
+    static constexpr int kStages = HD == 64 ? 3 : 2;
+    static constexpr int kHalves = HD / 64;
+    static constexpr int kHalf = kTcKeys * 128;       // bytes of one 64-dimension half (128 rows x 128 B)
+    static constexpr int kQBytes = kTcRows * HD * 2;  // 16 / 32 KB
+    static constexpr int kKvBytes = kTcKeys * HD * 2; // per K or V tile
+    static constexpr int kOCol = 2 * kTcKeys;         // O: HD TMEM columns after S0 | S1
+};
 
-inline size_t prefill_attention_tc128_smem() {
-    return (size_t)kTc2QBytes + (size_t)kTc2Stages * 2 * kTc2KvBytes + kTcPBytes + 1024;
+template <int HD>
+inline size_t prefill_attention_tc2_smem() {
+    using C = Tc2<HD>;
+    return (size_t)C::kQBytes + (size_t)C::kStages * 2 * C::kKvBytes + kTcPBytes + 1024;
 }
 
+template <int HD>
 __global__ void __launch_bounds__(kTcThreads, 1)
-    prefill_attention_tc128_kernel(const __grid_constant__ CUtensorMap q_map,
-                                   const __grid_constant__ CUtensorMap k_map,
-                                   const __grid_constant__ CUtensorMap v_map, const PrefillAttnParams p) {
-    constexpr int HD = 128;
-    constexpr int kBoxRows = kTileBytes / (HD * 2);  // 32: rows of one cache-map box
+    prefill_attention_tc2_kernel(const __grid_constant__ CUtensorMap q_map,
+                                 const __grid_constant__ CUtensorMap k_map,
+                                 const __grid_constant__ CUtensorMap v_map, const PrefillAttnParams p) {
+    using C = Tc2<HD>;
+    constexpr int kTc2Stages = C::kStages;
+    constexpr int kTc2QBytes = C::kQBytes;
+    constexpr int kTc2KvBytes = C::kKvBytes;
+    constexpr int kTc2Half = C::kHalf;
+    constexpr int kTc2OCol = C::kOCol;
+    constexpr int kBoxRows = kTileBytes / (HD * 2);  // rows of one cache-map box: 64 (d=64) or 32 (d=128)
     constexpr uint32_t kIdescS = umma_idesc_bf16(kTcRows, kTcKeys);
     constexpr uint32_t kIdescPV = umma_idesc_bf16(kTcRows, 64) | (1u << 16);  // B (V) MN-major
     extern __shared__ __align__(1024) uint8_t attn_tc2_smem[];
+    static_assert(HD == 64 || HD == 128, "head_dim 64 or 128");
     __shared__ __align__(8) uint64_t q_full;
     __shared__ __align__(8) uint64_t kv_full[kTc2Stages];
     __shared__ __align__(8) uint64_t kv_empty[kTc2Stages];
@@ -481,7 +494,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (lane == 0 && n_tiles > 0) {
             mbar_expect_tx(smem_u32(&q_full), kTc2QBytes);
 #pragma unroll
-            for (int h = 0; h < 2; ++h)
+            for (int h = 0; h < C::kHalves; ++h)
                 tma_load_2d(smem_u32(q_s + h * kTc2Half), &q_map, head * HD + h * 64, t0, smem_u32(&q_full));
             for (int j = 0; j < n_tiles; ++j) {
                 const int s = j % kTc2Stages;
@@ -520,7 +533,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     for (int r = 0; r < 64 / kBoxRows; ++r) {
                         const uint32_t row_off = (uint32_t)((b * 64 + r * kBoxRows) * 128);
 #pragma unroll
-                        for (int h = 0; h < 2; ++h) {
+                        for (int h = 0; h < C::kHalves; ++h) {
                             tma_load_2d(smem_u32(ks + h * kTc2Half + row_off), &k_map, h * 64, rows[b] + r * kBoxRows,
                                         bar);
                             tma_load_2d(smem_u32(vs + h * kTc2Half + row_off), &v_map, h * 64, rows[b] + r * kBoxRows,
@@ -565,7 +578,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 const int s = j % kTc2Stages;
                 const uint32_t v_addr = smem_u32(ring + s * 2 * kTc2KvBytes + kTc2KvBytes);
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
+                for (int h = 0; h < C::kHalves; ++h) {
 #pragma unroll
                     for (int k = 0; k < kTcKeys / 16; ++k) {
                         umma_bf16(tmem + kTc2OCol + h * 64,
@@ -706,6 +719,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 }
             }
             if (live && p.splits > 1) *reinterpret_cast<float2 *>(p.part_ml + rh * 2) = make_float2(m_run, l_run);
+        } else if (t <= t_last) {
+            // A key split with no tiles (the split count rounds up): an empty
+            // partial (O = 0, m = -inf, l = 0) that the merge weighs by zero.
+            const long long rh = ((long long)split * p.T + t) * p.q_heads + head;
+            if (p.splits > 1) {
+                float4 *dst = reinterpret_cast<float4 *>(p.part_o + rh * HD);
+#pragma unroll
+                for (int i = 0; i < HD / 4; ++i) dst[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+                *reinterpret_cast<float2 *>(p.part_ml + rh * 2) = make_float2(-INFINITY, 0.0f);
+            } else {
+                uint4 *dst = reinterpret_cast<uint4 *>(p.out + (long long)t * p.q_heads * HD + head * HD);
+#pragma unroll
+                for (int i = 0; i < HD / 8; ++i) dst[i] = make_uint4(0u, 0u, 0u, 0u);
+            }
         }
     }
     tc_fence_before();

@@ -148,7 +148,7 @@ def test_decode_attention_full_size_sampled():
 # bf16 (the GEMM epilogue's output), so the oracle reads the same rounded q.
 @pytest.mark.parametrize("q_heads,kv_heads,D", [(14, 2, 64), (28, 4, 128), (8, 8, 64)])
 @pytest.mark.parametrize("offset,T,window", [(0, 1, 0), (0, 130, 0), (700, 257, 0), (2048, 64, 0),
-                                             (300, 200, 96), (5000, 77, 4096)])
+                                             (1024, 64, 0), (300, 200, 96), (5000, 77, 4096)])
 def test_prefill_attention_op_matches_oracle(q_heads, kv_heads, D, offset, T, window):
     from cheetah_b200 import runtime as R
     from cheetah_b200.prepared import bf16_bits_to_f32, f32_to_bf16_bits

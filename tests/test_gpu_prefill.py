@@ -126,17 +126,19 @@ def test_prefill_attention_key_splits_match_oracle(fixture, chunk, monkeypatch, 
     assert np.abs(other.forward(toks[1003:], 1003) - got).max() < TOL
 
 
-def test_prefill_sliding_window_matches_oracle(tiny_prepared, monkeypatch):
+@pytest.mark.parametrize("fixture", ["tiny_prepared", "tiny7b_prepared"])
+def test_prefill_sliding_window_matches_oracle(fixture, monkeypatch, request):
     """A 150-token sliding window (not a multiple of the 128-key tile) over a
     cached prefix and two chunks: keys below the window are masked per row in
     the tensor-core attention (`ops.rs:1366-1372`)."""
     from cheetah_b200 import runtime as R
     monkeypatch.setenv("CHEETAH_PREFILL_CHUNK", "256")
-    pm = PreparedModel(tiny_prepared)
+    root = request.getfixturevalue(fixture)
+    pm = PreparedModel(root)
     cfg = dict(resolve_config(pm, 2048))
     cfg["sliding_window"] = 150
     ref = O.OracleModel(pm, cfg)
-    model = R.CudaModel(tiny_prepared, config=cfg)
+    model = R.CudaModel(root, config=cfg)
     toks = _toks(900, cfg["vocab_size"], 23)
     seq = model.new_sequence()
     seq.forward(toks[:300], 0)
