@@ -1978,6 +1978,22 @@ int launch_prefill_attention(PrefillAttnParams ap, const CUtensorMap &q_map, con
                              const CUtensorMap &v_map, int head_dim, size_t offset, int sms, cudaStream_t st,
                              bool pdl) {
     const int M = ap.T;
+    if (head_dim == 64 && env_flag("CHEETAH_PREFILL_TC", true) && env_flag("CHEETAH_PREFILL_TC_PAIR", true)) {
+        // Two 128-row query tiles per CTA; the same split rule over its blocks.
+        const int blocks = ((M + kTpRows - 1) / kTpRows) * ap.q_heads;
+        const int key_tiles = (int)((offset + M + kTcKeys - 1) / kTcKeys);
+        ap.splits = std::max(1, std::min(std::min(kPrefillMaxSplits, sms / blocks), key_tiles / 2));
+        const size_t tsmem = prefill_attention_tc_pair_smem();
+        CH_CUDA_TRY(cudaFuncSetAttribute(prefill_attention_tc_pair_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tsmem));
+        dim3 tgrid((M + kTpRows - 1) / kTpRows, ap.q_heads, ap.splits);
+        CH_CUDA_TRY(launch_ex(prefill_attention_tc_pair_kernel, tgrid, dim3(kTpThreads), tsmem, st, pdl, q_map,
+                              k_map, v_map, ap));
+        if (ap.splits > 1) {
+            CH_CUDA_TRY(launch_ex(prefill_merge_kernel<64>, dim3(2 * sms), dim3(256), 0, st, pdl, ap));
+        }
+        return 0;
+    }
     if (head_dim == 64 && env_flag("CHEETAH_PREFILL_TC", true)) {
         // Tensor-core attention: one CTA per SM (512 TMEM columns each);
         // key-range splits fill the SMs, each split >= 2 key tiles.

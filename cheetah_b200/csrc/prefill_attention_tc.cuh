@@ -761,4 +761,396 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
 }
 
+// ---- two query tiles per CTA (head_dim 64) --------------------------------
+// 256 query rows x one head per CTA: two softmax groups (warps 2-5 and 6-9,
+// each covering the four TMEM lane quadrants) work on the two 128-row query
+// tiles A and B against the same K/V tiles, so while one group runs its
+// softmax the tensor core computes the other group's S or P.V.
+//
+// S tiles rotate through three 128-column TMEM buffers in the order S_A(0),
+// S_B(0), S_A(1), S_B(1), ... (S tile n = 2j + g in buffer n % 3), so a
+// group's next S is computed while it still runs the softmax of the current
+// one: per key tile j the MMA thread issues PV_A(j), S_B(j+1), PV_B(j) (the
+// K/V stage is then free), S_A(j+2). Each S buffer has its own full/empty
+// barriers, so no barrier can run two phases ahead of its consumer. O of each
+// group is accumulated in TMEM (columns 384 and 448) and rescaled only when a
+// row's running max grows by more than 2^8 (until then the old max is kept:
+// P <= 256, and O and l use the same max, so the normalised result is the
+// same softmax). A softmax thread reads its S row from TMEM twice, 64 columns
+// at a time (the row max, then the exponentials), which keeps it within the
+// 168 registers a thread of a 10-warp CTA can have. Shared memory: Q_A, Q_B
+// (16 KB each), four 32 KB K/V stages, P_A, P_B (32 KB each): 225 KB.
+constexpr int kTpRows = 2 * kTcRows;  // query rows per CTA
+constexpr int kTpThreads = 320;       // producer, MMA, 2 x 4 softmax warps
+constexpr int kTpStages = 4;
+constexpr int kTpSBufs = 3;
+constexpr int kTpQBytes = kTcRows * 64 * 2;   // per query tile
+constexpr int kTpKvBytes = kTcKeys * 64 * 2;  // per K or V tile
+constexpr int kTpOCol = kTpSBufs * kTcKeys;   // O_A at 384, O_B at 448
+constexpr float kTpRescaleLog2 = 8.0f;        // keep the running max until it grows by 2^8
+static_assert(kTpOCol + 2 * 64 <= kTcTmemCols, "TMEM columns");
+
+inline size_t prefill_attention_tc_pair_smem() {
+    return (size_t)2 * kTpQBytes + (size_t)kTpStages * 2 * kTpKvBytes + 2 * (size_t)kTcPBytes + 1024;
+}
+
+__global__ void __launch_bounds__(kTpThreads, 1)
+    prefill_attention_tc_pair_kernel(const __grid_constant__ CUtensorMap q_map,
+                                     const __grid_constant__ CUtensorMap k_map,
+                                     const __grid_constant__ CUtensorMap v_map, const PrefillAttnParams p) {
+    constexpr int HD = 64;
+    constexpr uint32_t kIdescS = umma_idesc_bf16(kTcRows, kTcKeys);
+    constexpr uint32_t kIdescPV = umma_idesc_bf16(kTcRows, HD) | (1u << 16);  // B (V) MN-major
+    extern __shared__ __align__(1024) uint8_t attn_tp_smem[];
+    __shared__ __align__(8) uint64_t q_full;
+    __shared__ __align__(8) uint64_t kv_full[kTpStages];
+    __shared__ __align__(8) uint64_t kv_empty[kTpStages];
+    __shared__ __align__(8) uint64_t s_full[kTpSBufs];  // per S buffer
+    __shared__ __align__(8) uint64_t s_empty[kTpSBufs];
+    __shared__ __align__(8) uint64_t p_full[2];  // per group
+    __shared__ __align__(8) uint64_t o_full[2];
+    __shared__ __align__(8) uint64_t drain_bar;
+    __shared__ uint32_t tmem_base_s;
+    __shared__ int abort_s;
+
+    uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(attn_tp_smem) + 1023) & ~uintptr_t(1023));
+    uint8_t *q_s = base;                                // Q_A | Q_B
+    uint8_t *ring = q_s + 2 * kTpQBytes;
+    uint8_t *p_s = ring + kTpStages * 2 * kTpKvBytes;  // P_A | P_B
+    const int warp = threadIdx.x / kWarp;
+    const int lane = threadIdx.x % kWarp;
+    const int group = p.q_heads / p.kv_heads;
+    const int head = blockIdx.y;
+    const int kvh = head / group;
+    const int t0 = blockIdx.x * kTpRows;
+    const int t_last = min(p.T, t0 + kTpRows) - 1;
+    const int pos_first = p.offset + t0;
+    const int pos_last = p.offset + t_last;
+    int ws = 0;
+    if (p.window > 0) ws = max(0, pos_first + 1 - p.window);
+    const int all_lo = ws / kTcKeys;
+    const int all_hi = pos_last / kTcKeys + 1;
+    const int per_split = (all_hi - all_lo + p.splits - 1) / p.splits;
+    const int split = blockIdx.z;
+    const int tile_lo = all_lo + split * per_split;
+    const int tile_hi = min(all_hi, tile_lo + per_split);
+    const int n_tiles = max(0, tile_hi - tile_lo);
+
+    if (threadIdx.x == 0) {
+        mbar_init(smem_u32(&q_full), 1);
+        for (int s = 0; s < kTpStages; ++s) {
+            mbar_init(smem_u32(&kv_full[s]), 1);
+            mbar_init(smem_u32(&kv_empty[s]), 1);
+        }
+        for (int b = 0; b < kTpSBufs; ++b) {
+            mbar_init(smem_u32(&s_full[b]), 1);
+            mbar_init(smem_u32(&s_empty[b]), kTcRows);
+        }
+        for (int g = 0; g < 2; ++g) {
+            mbar_init(smem_u32(&p_full[g]), kTcRows);
+            mbar_init(smem_u32(&o_full[g]), 1);
+        }
+        mbar_init(smem_u32(&drain_bar), 1);
+        abort_s = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_s)),
+                     "r"((uint32_t)kTcTmemCols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_base_s;
+
+    pdl_wait();
+    pdl_launch_dependents();
+
+    int issued = 0;  // K/V tiles the producer has requested
+    if (warp == 0) {
+        if (lane == 0 && n_tiles > 0) {
+            // Both query tiles (rows past the chunk read whatever the buffer
+            // holds; their rows are computed but never stored).
+            mbar_expect_tx(smem_u32(&q_full), 2 * kTpQBytes);
+#pragma unroll
+            for (int g = 0; g < 2; ++g)
+                tma_load_2d(smem_u32(q_s + g * kTpQBytes), &q_map, head * HD, t0 + g * kTcRows, smem_u32(&q_full));
+            for (int j = 0; j < n_tiles; ++j) {
+                const int s = j % kTpStages;
+                if (!mbar_wait(smem_u32(&kv_empty[s]), ((j / kTpStages) & 1) ^ 1)) {
+                    abort_s = 1;
+                    break;
+                }
+                const int tile = tile_lo + j;
+                // Rows of the pool for the tile's two 64-key boxes (a box past
+                // the chunk's last position re-reads box 0, as above).
+                int rows[2];
+#pragma unroll
+                for (int b = 0; b < 2; ++b) {
+                    const int pos0 = tile * kTcKeys + b * 64;
+                    const int pidx = pos0 / p.page_tokens;
+                    const int page = pidx < p.max_pages ? p.page_table[pidx] : -1;
+                    if (page < 0 || page >= p.num_pages) {
+                        if (b == 0 || pos0 <= pos_last) {
+                            if (p.error) *p.error = 6;
+                        }
+                        rows[b] = b == 0 ? (int)p.layer_row_offset : rows[0];
+                    } else {
+                        rows[b] = (int)(p.layer_row_offset + ((long long)page * p.kv_heads + kvh) * p.page_tokens +
+                                        (pos0 - pidx * p.page_tokens));
+                    }
+                    if (b == 1 && pos0 > pos_last) rows[1] = rows[0];
+                }
+                uint8_t *ks = ring + s * 2 * kTpKvBytes;
+                uint8_t *vs = ks + kTpKvBytes;
+                const uint32_t bar = smem_u32(&kv_full[s]);
+                mbar_expect_tx(bar, 2 * kTpKvBytes);
+#pragma unroll
+                for (int b = 0; b < 2; ++b) {
+                    tma_load_2d(smem_u32(ks + b * 64 * 128), &k_map, 0, rows[b], bar);
+                    tma_load_2d(smem_u32(vs + b * 64 * 128), &v_map, 0, rows[b], bar);
+                }
+                issued = j + 1;
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && n_tiles > 0) {
+            const uint32_t q_addr = smem_u32(q_s);
+            const uint32_t p_addr = smem_u32(p_s);
+            bool ok = mbar_wait(smem_u32(&q_full), 0);
+            // S_g(j) = Q_g K_j^T into S buffer (2j + g) % 3.
+            auto issue_s = [&](int g, int j) -> bool {
+                const int n = 2 * j + g, sb = n % kTpSBufs;
+                const int s = j % kTpStages;
+                if (!mbar_wait(smem_u32(&kv_full[s]), (j / kTpStages) & 1)) return false;
+                if (!mbar_wait(smem_u32(&s_empty[sb]), ((n / kTpSBufs) & 1) ^ 1)) return false;
+                tc_fence_after();
+                const uint32_t k_addr = smem_u32(ring + s * 2 * kTpKvBytes);
+                const uint32_t qg = q_addr + (uint32_t)(g * kTpQBytes);
+#pragma unroll
+                for (int k = 0; k < HD / 16; ++k) {
+                    umma_bf16(tmem + (uint32_t)(sb * kTcKeys), umma_smem_desc(qg + k * 32),
+                              umma_smem_desc(k_addr + k * 32), kIdescS, k > 0 ? 1u : 0u);
+                }
+                umma_commit(smem_u32(&s_full[sb]));
+                return true;
+            };
+            // O_g += P_g(j) V_j.
+            auto issue_pv = [&](int g, int j) -> bool {
+                if (!mbar_wait(smem_u32(&p_full[g]), j & 1)) return false;
+                tc_fence_after();
+                const int s = j % kTpStages;
+                const uint32_t v_addr = smem_u32(ring + s * 2 * kTpKvBytes + kTpKvBytes);
+                const uint32_t pg = p_addr + (uint32_t)(g * kTcPBytes);
+#pragma unroll
+                for (int k = 0; k < kTcKeys / 16; ++k) {
+                    umma_bf16(tmem + kTpOCol + (uint32_t)(g * HD),
+                              umma_smem_desc(pg + (k >> 2) * (kTcRows * 128) + (k & 3) * 32),
+                              umma_smem_desc_mn(v_addr + k * 2048), kIdescPV, (j > 0 || k > 0) ? 1u : 0u);
+                }
+                umma_commit(smem_u32(&o_full[g]));
+                return true;
+            };
+            // S_B(j+1) reuses S_A(j)'s buffer and S_A(j+2) S_B(j)'s: both are
+            // released (s_empty) before the P they follow (p_full).
+            if (ok) ok = issue_s(0, 0) && issue_s(1, 0) && (n_tiles < 2 || issue_s(0, 1));
+            for (int j = 0; ok && j < n_tiles; ++j) {
+                ok = issue_pv(0, j);
+                if (ok && j + 1 < n_tiles) ok = issue_s(1, j + 1);
+                if (ok) ok = issue_pv(1, j);
+                if (ok) umma_commit(smem_u32(&kv_empty[j % kTpStages]));
+                if (ok && j + 2 < n_tiles) ok = issue_s(0, j + 2);
+            }
+            if (!ok) abort_s = 1;
+        }
+    } else {
+        // Softmax group g (warps 2-5: tile A, 6-9: tile B); TMEM lane quadrant
+        // = warp % 4; thread = query row of its tile.
+        const int g = (warp - 2) / 4;
+        const int quad = warp % 4;
+        const int r = quad * 32 + lane;
+        const int t = t0 + g * kTcRows + r;
+        const int qpos = p.offset + t;
+        const int gpos_first = pos_first + g * kTcRows;
+        const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+        const uint32_t o_addr = tmem + lane_off + kTpOCol + (uint32_t)(g * HD);
+        const float scale_log2 = p.scale * 1.4426950408889634f;
+        float m_run = -INFINITY, l_run = 0.0f;
+        bool ok = true;
+        uint8_t *p_row0 = p_s + g * kTcPBytes + r * 128;
+        for (int j = 0; j < n_tiles; ++j) {
+            const int n = 2 * j + g, sb = n % kTpSBufs;
+            const uint32_t s_addr = tmem + lane_off + (uint32_t)(sb * kTcKeys);
+            // Waits decide warp-uniformly (the TMEM accesses below are warp-wide).
+            if (!__all_sync(0xFFFFFFFFu, mbar_wait(smem_u32(&s_full[sb]), (n / kTpSBufs) & 1))) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const int kp0 = (tile_lo + j) * kTcKeys;
+            // Tiles wholly at or below the group's first position need no mask
+            // (no window); otherwise key i is visible iff wlo < i <= lim.
+            const bool masked = p.window > 0 || kp0 + kTcKeys - 1 > gpos_first;
+            const int lim = qpos - kp0;
+            const int wlo = p.window > 0 ? lim - p.window : -1;
+            // Pass 1: the row max of the raw scores (scale > 0), eight chains.
+            float mx[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) mx[k] = -INFINITY;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                float sc[64];
+                tmem_ld32_nowait(s_addr + h * 64, sc);
+                tmem_ld32_nowait(s_addr + h * 64 + 32, sc + 32);
+                tmem_wait_ld();
+                if (masked) {
+#pragma unroll
+                    for (int i = 0; i < 64; ++i) sc[i] = (h * 64 + i <= lim && h * 64 + i > wlo) ? sc[i] : -INFINITY;
+                }
+#pragma unroll
+                for (int i = 0; i < 64; ++i) mx[i & 7] = fmaxf(mx[i & 7], sc[i]);
+            }
+#pragma unroll
+            for (int k = 0; k < 4; ++k) mx[k] = fmaxf(mx[k], mx[k + 4]);
+            const float tmax = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+            // The running max moves only when it grows by more than 2^8 (from
+            // -inf it always moves; -inf + 8 stays -inf).
+            const float m_cand = fmaxf(m_run, tmax * scale_log2);
+            const float m_new = m_cand > m_run + kTpRescaleLog2 ? m_cand : m_run;
+            const float alpha = m_new == -INFINITY ? 1.0f : exp2f(m_run - m_new);
+            const float neg_m = m_new == -INFINITY ? 0.0f : -m_new;
+            if (j > 0) {
+                // PV_g(j-1) done: P_g's buffer is free and O_g holds tiles < j.
+                if (!__all_sync(0xFFFFFFFFu, mbar_wait(smem_u32(&o_full[g]), (j - 1) & 1))) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                if (__any_sync(0xFFFFFFFFu, alpha < 1.0f)) {
+#pragma unroll 1
+                    for (int c = 0; c < HD / 32; ++c) {
+                        float ov[32];
+                        tmem_ld32_nowait(o_addr + c * 32, ov);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) ov[i] *= alpha;
+                        tmem_st32(o_addr + c * 32, ov);
+                    }
+                }
+            }
+            // Pass 2: p = 2^(s * scale_log2 - m_new) (a masked key gives 0)
+            // into P_g row r, K-major with 128-byte swizzle: keys 64h..64h+63
+            // in block h, 16-byte chunk c of the row at (c ^ (r & 7)).
+            float sums[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) sums[k] = 0.0f;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                float sc[64];
+                tmem_ld32_nowait(s_addr + h * 64, sc);
+                tmem_ld32_nowait(s_addr + h * 64 + 32, sc + 32);
+                tmem_wait_ld();
+                if (masked) {
+#pragma unroll
+                    for (int i = 0; i < 64; ++i) sc[i] = (h * 64 + i <= lim && h * 64 + i > wlo) ? sc[i] : -INFINITY;
+                }
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    uint32_t w[4];
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const float e0 = fast_exp2(fmaf(sc[8 * c + 2 * q], scale_log2, neg_m));
+                        const float e1 = fast_exp2(fmaf(sc[8 * c + 2 * q + 1], scale_log2, neg_m));
+                        sums[(4 * c + q) & 7] += e0 + e1;
+                        w[q] = pack_bf16(e0, e1);
+                    }
+                    uint4 *dst = reinterpret_cast<uint4 *>(p_row0 + h * (kTcRows * 128) + ((c ^ (r & 7)) << 4));
+                    *dst = make_uint4(w[0], w[1], w[2], w[3]);
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(smem_u32(&s_empty[sb]));
+#pragma unroll
+            for (int k = 0; k < 4; ++k) sums[k] += sums[k + 4];
+            const float rsum = (sums[0] + sums[1]) + (sums[2] + sums[3]);
+            l_run = l_run * alpha + rsum;
+            m_run = m_new;
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            mbar_arrive(smem_u32(&p_full[g]));
+        }
+        if (ok && n_tiles > 0) {
+            if (__all_sync(0xFFFFFFFFu, mbar_wait(smem_u32(&o_full[g]), (n_tiles - 1) & 1))) {
+                tc_fence_after();
+            } else {
+                ok = false;
+            }
+        }
+        const bool live = t <= t_last;
+        const long long rh = ((long long)split * p.T + t) * p.q_heads + head;
+        if (!ok) {
+            abort_s = 1;
+        } else if (n_tiles > 0) {
+            const float inv = l_run > 0.0f ? 1.0f / l_run : 0.0f;
+#pragma unroll 1
+            for (int c = 0; c < HD / 32; ++c) {
+                float ov[32];
+                tmem_ld32_nowait(o_addr + c * 32, ov);
+                tmem_wait_ld();
+                if (!live) continue;
+                if (p.splits > 1) {
+                    float4 *dst = reinterpret_cast<float4 *>(p.part_o + rh * HD + c * 32);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) dst[i] = make_float4(ov[4 * i], ov[4 * i + 1], ov[4 * i + 2], ov[4 * i + 3]);
+                } else {
+                    uint4 *dst = reinterpret_cast<uint4 *>(p.out + (long long)t * p.q_heads * HD + head * HD + c * 32);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        dst[i] = make_uint4(pack_bf16(ov[8 * i] * inv, ov[8 * i + 1] * inv),
+                                            pack_bf16(ov[8 * i + 2] * inv, ov[8 * i + 3] * inv),
+                                            pack_bf16(ov[8 * i + 4] * inv, ov[8 * i + 5] * inv),
+                                            pack_bf16(ov[8 * i + 6] * inv, ov[8 * i + 7] * inv));
+                    }
+                }
+            }
+            if (live && p.splits > 1) *reinterpret_cast<float2 *>(p.part_ml + rh * 2) = make_float2(m_run, l_run);
+        } else if (live) {
+            // A key split with no tiles: an empty partial (O = 0, m = -inf,
+            // l = 0) that the merge weighs by zero.
+            if (p.splits > 1) {
+                float4 *dst = reinterpret_cast<float4 *>(p.part_o + rh * HD);
+#pragma unroll
+                for (int i = 0; i < HD / 4; ++i) dst[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+                *reinterpret_cast<float2 *>(p.part_ml + rh * 2) = make_float2(-INFINITY, 0.0f);
+            } else {
+                uint4 *dst = reinterpret_cast<uint4 *>(p.out + (long long)t * p.q_heads * HD + head * HD);
+#pragma unroll
+                for (int i = 0; i < HD / 8; ++i) dst[i] = make_uint4(0u, 0u, 0u, 0u);
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (abort_s) {
+        // A wait gave up: let this CTA's copies and MMAs still in flight land
+        // before its shared memory and TMEM are released (bounded waits).
+        if (warp == 0 && lane == 0 && n_tiles > 0) {
+            mbar_wait(smem_u32(&q_full), 0);
+            for (int j = max(0, issued - kTpStages); j < issued; ++j) {
+                mbar_wait(smem_u32(&kv_full[j % kTpStages]), (j / kTpStages) & 1);
+            }
+        } else if (warp == 1 && lane == 0) {
+            umma_commit(smem_u32(&drain_bar));
+            mbar_wait(smem_u32(&drain_bar), 0);
+        }
+        tc_fence_before();
+        __syncthreads();
+        if (threadIdx.x == 0 && p.error) *p.error = 8;
+    }
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)kTcTmemCols));
+    }
+}
+
 }  // namespace cheetah
