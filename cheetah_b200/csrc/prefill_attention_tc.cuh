@@ -394,8 +394,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 // grow are multiplied by 1 (exact). The last tile's O is read back once,
 // normalised and stored. At head_dim 128: two K/V stages of 64 KB (Q 32 KB, ring
 // 128 KB, P 32 KB); at 64: three of 32 KB. The library launches it for
-// head_dim 128; head_dim 64 runs the kernel above (the two measure within 2%
-// of each other there, and the one above keeps no O rescale in TMEM).
+// head_dim 128; head_dim 64 runs prefill_attention_tc_pair_kernel below (two
+// query tiles per CTA), or the kernel above when that is switched off.
 template <int HD>
 struct Tc2 {
     static constexpr int kStages = HD == 64 ? 3 : 2;
