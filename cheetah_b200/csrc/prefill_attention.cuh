@@ -258,7 +258,10 @@ __global__ void __launch_bounds__(kPrefillWarps * kWarp, HD == 64 ? 2 : 1)
 }
 
 // Combine the key-range splits of prefill_attention_kernel: per (token, head)
-// O = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s, written as bf16.
+// O = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s, written as bf16. The
+// split loops are unrolled to kPrefillMaxSplits (guarded by p.splits) so a
+// thread's loads of every split are in flight together; the arithmetic runs
+// in split order.
 template <int HD>
 __global__ void prefill_merge_kernel(const PrefillAttnParams p) {
     pdl_wait();
@@ -268,17 +271,30 @@ __global__ void prefill_merge_kernel(const PrefillAttnParams p) {
          i += (long long)gridDim.x * blockDim.x) {
         const long long rh = i / (HD / 4);
         const int d4 = (int)(i % (HD / 4));
+        float2 ml[kPrefillMaxSplits];
+        float4 v[kPrefillMaxSplits];
+#pragma unroll
+        for (int s = 0; s < kPrefillMaxSplits; ++s) {
+            if (s < p.splits) {
+                ml[s] = *reinterpret_cast<const float2 *>(p.part_ml + ((long long)s * rows + rh) * 2);
+                v[s] = reinterpret_cast<const float4 *>(p.part_o + ((long long)s * rows + rh) * HD)[d4];
+            }
+        }
         float m = -INFINITY;
-        for (int s = 0; s < p.splits; ++s) m = fmaxf(m, p.part_ml[((long long)s * rows + rh) * 2]);
+#pragma unroll
+        for (int s = 0; s < kPrefillMaxSplits; ++s) {
+            if (s < p.splits) m = fmaxf(m, ml[s].x);
+        }
         float l = 0.0f;
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int s = 0; s < p.splits; ++s) {
-            const float ms = p.part_ml[((long long)s * rows + rh) * 2];
-            const float w = m == -INFINITY ? 0.0f : exp2f(ms - m);
-            l += w * p.part_ml[((long long)s * rows + rh) * 2 + 1];
-            const float4 v = reinterpret_cast<const float4 *>(p.part_o + ((long long)s * rows + rh) * HD)[d4];
-            acc.x = fmaf(w, v.x, acc.x); acc.y = fmaf(w, v.y, acc.y);
-            acc.z = fmaf(w, v.z, acc.z); acc.w = fmaf(w, v.w, acc.w);
+#pragma unroll
+        for (int s = 0; s < kPrefillMaxSplits; ++s) {
+            if (s < p.splits) {
+                const float w = m == -INFINITY ? 0.0f : exp2f(ml[s].x - m);
+                l += w * ml[s].y;
+                acc.x = fmaf(w, v[s].x, acc.x); acc.y = fmaf(w, v[s].y, acc.y);
+                acc.z = fmaf(w, v[s].z, acc.z); acc.w = fmaf(w, v[s].w, acc.w);
+            }
         }
         const float inv = l > 0.0f ? 1.0f / l : 0.0f;
         uint16_t *out = p.out + rh * HD + d4 * 4;
