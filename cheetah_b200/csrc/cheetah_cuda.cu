@@ -1970,8 +1970,9 @@ int launch_prefill_gemm(const CUtensorMap &a, const CUtensorMap &b, const CUtens
 }
 
 // Causal prefill attention over the paged bf16 cache (`ops.rs:1357-1421`
-// for each query row; the rows' own K/V are already appended): tensor-core
-// (tcgen05) kernel for head_dim 64, tensor-core mma kernel for 128. Key-range
+// for each query row; the rows' own K/V are already appended): tcgen05
+// kernels, two 128-row query tiles per CTA for head_dim 64 and one for 128
+// (CHEETAH_PREFILL_TC=0 selects the mma.sync kernel for both). Key-range
 // splits fill the SMs when the query rows alone do not; a merge kernel then
 // combines the partials (ap.part_o / ap.part_ml sized for kPrefillMaxSplits).
 int launch_prefill_attention(PrefillAttnParams ap, const CUtensorMap &q_map, const CUtensorMap &k_map,
