@@ -1,6 +1,7 @@
 """The synchronisation protocol of the two-tile prefill attention kernel
 (`prefill_attention_tc_pair_kernel`, `cheetah_b200/csrc/prefill_attention_tc.cuh`),
-checked on the CPU over random interleavings.
+checked on the CPU over random interleavings (and, more briefly, that of the
+one-tile kernels in the same file).
 
 The kernel's actors are modelled step for step in the order the kernel runs
 them: the TMA producer (four K/V stages), the MMA thread (S_A(0), S_B(0),
@@ -178,6 +179,104 @@ class Model:
                 except StopIteration:
                     live.remove(a)
         return False
+
+
+class SingleTileModel(Model):
+    """The one-query-tile kernels (`prefill_attention_tc_kernel`, head_dim 64,
+    three K/V stages; `prefill_attention_tc2_kernel<128>`, two stages): S
+    double-buffered by j & 1, the MMA thread issues S(j+1) before waiting for
+    P(j), then P.V(j), o_full and the stage's commit; the softmax group
+    releases S(j) right after reading it, waits for P.V(j-1) before touching
+    O and P, then releases P(j)."""
+
+    def __init__(self, n_tiles, rng, stages):
+        self.stages = stages
+        super().__init__(n_tiles, rng)
+        self.kv_full = [Barrier(f"kv_full[{s}]") for s in range(stages)]
+        self.kv_empty = [Barrier(f"kv_empty[{s}]") for s in range(stages)]
+        self.stage_tile = [None] * stages
+        self.s_full = [Barrier(f"s_full[{b}]") for b in range(2)]
+        self.s_empty = [Barrier(f"s_empty[{b}]") for b in range(2)]
+        self.s_tile = [None, None]
+        self.actors = [self.producer(), self.mma(), self.group(0)]
+
+    def producer(self):
+        self.tma.append(("q", None))
+        for j in range(self.n):
+            s = j % self.stages
+            yield from self.wait(self.kv_empty[s], j // self.stages - 1)
+            old = self.stage_tile[s]
+            assert old is None or not self.readers.get(old), f"stage {s} reloaded while tile {old} is read"
+            self.stage_tile[s] = j
+            self.tma.append(("kv", j))
+            yield
+
+    def issue_s(self, g, j):
+        sb = j & 1
+        yield from self.wait(self.kv_full[j % self.stages], j // self.stages)
+        yield from self.wait(self.s_empty[sb], (j >> 1) - 1)
+        assert self.s_tile[sb] is None, f"S buffer {sb} rewritten while S tile {self.s_tile[sb]} is unread"
+        self.s_tile[sb] = j
+        self.readers[j] = self.readers.get(j, 0) + 1
+        self.pipe.append(("s", 0, j, sb))
+
+    def mma(self):
+        yield from self.wait(self.q_full, 0)
+        yield from self.issue_s(0, 0)
+        for j in range(self.n):
+            if j + 1 < self.n:
+                yield from self.issue_s(0, j + 1)
+            yield from self.issue_pv(0, j)
+            self.pipe.append(("commit", None, j, None))
+            yield
+
+    def group(self, g):
+        for j in range(self.n):
+            sb = j & 1
+            yield from self.wait(self.s_full[sb], j >> 1)
+            assert self.s_tile[sb] == j
+            yield  # S read into registers
+            self.s_tile[sb] = None
+            self.s_empty[sb].complete()
+            yield  # softmax
+            if j > 0:
+                yield from self.wait(self.o_full[0], j - 1)
+            assert self.p_read[0] == j - 1, f"P overwritten while P.V({j - 1}) reads it"
+            yield  # O rescaled or folded, P written
+            self.p_full[0].complete()
+            yield
+        if self.n:
+            yield from self.wait(self.o_full[0], self.n - 1)
+
+    def step_pipe(self):
+        kind, g, j, sb = self.pipe.pop(0)
+        if kind == "s":
+            self.readers[j] -= 1
+            self.s_full[sb].complete()
+        elif kind == "pv":
+            self.readers[j] -= 1
+            self.p_read[0] = j
+            self.o_full[0].complete()
+        else:
+            assert not self.readers.get(j), f"stage of tile {j} released with readers in flight"
+            self.kv_empty[j % self.stages].complete()
+
+    def step_tma(self):
+        i = self.rng.randrange(len(self.tma))
+        kind, j = self.tma.pop(i)
+        if kind == "q":
+            self.q_full.complete()
+        else:
+            self.kv_full[j % self.stages].complete()
+
+
+@pytest.mark.parametrize("stages", [3, 2])
+@pytest.mark.parametrize("n_tiles", [1, 2, 3, 5, 8, 13])
+def test_single_tile_kernels_protocol(stages, n_tiles):
+    for seed in range(60):
+        m = SingleTileModel(n_tiles, random.Random(7000 * stages + 100 * n_tiles + seed), stages)
+        assert m.run(), f"no progress with {n_tiles} key tiles, {stages} stages (seed {seed})"
+        assert m.o_full[0].done == n_tiles
 
 
 @pytest.mark.parametrize("n_tiles", list(range(1, 13)))
