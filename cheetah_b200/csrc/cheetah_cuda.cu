@@ -1969,6 +1969,14 @@ int launch_prefill_gemm(const CUtensorMap &a, const CUtensorMap &b, const CUtens
     return launch_prefill_gemm_bn<EPI, 128>(a, b, b2, p, st, pdl, splits);
 }
 
+// Blocks of 256 threads for prefill_merge_kernel: one (row, head, 4 dims)
+// item per thread, capped at 8 blocks per SM (all resident; a larger grid
+// strides).
+inline int merge_blocks(const PrefillAttnParams &ap, int head_dim, int sms) {
+    const long long items = (long long)ap.T * ap.q_heads * (head_dim / 4);
+    return (int)std::max(1LL, std::min((items + 255) / 256, 8LL * sms));
+}
+
 // Causal prefill attention over the paged bf16 cache (`ops.rs:1357-1421`
 // for each query row; the rows' own K/V are already appended): tcgen05
 // kernels, two 128-row query tiles per CTA for head_dim 64 and one for 128
@@ -1991,7 +1999,7 @@ int launch_prefill_attention(PrefillAttnParams ap, const CUtensorMap &q_map, con
         CH_CUDA_TRY(launch_ex(prefill_attention_tc_pair_kernel, tgrid, dim3(kTpThreads), tsmem, st, pdl, q_map,
                               k_map, v_map, ap));
         if (ap.splits > 1) {
-            CH_CUDA_TRY(launch_ex(prefill_merge_kernel<64>, dim3(2 * sms), dim3(256), 0, st, pdl, ap));
+            CH_CUDA_TRY(launch_ex(prefill_merge_kernel<64>, dim3(merge_blocks(ap, 64, sms)), dim3(256), 0, st, pdl, ap));
         }
         return 0;
     }
@@ -2008,7 +2016,7 @@ int launch_prefill_attention(PrefillAttnParams ap, const CUtensorMap &q_map, con
         CH_CUDA_TRY(launch_ex(prefill_attention_tc_kernel, tgrid, dim3(kTcThreads), tsmem, st, pdl, q_map, k_map,
                               v_map, ap));
         if (ap.splits > 1) {
-            CH_CUDA_TRY(launch_ex(prefill_merge_kernel<64>, dim3(2 * sms), dim3(256), 0, st, pdl, ap));
+            CH_CUDA_TRY(launch_ex(prefill_merge_kernel<64>, dim3(merge_blocks(ap, 64, sms)), dim3(256), 0, st, pdl, ap));
         }
         return 0;
     }
@@ -2024,7 +2032,7 @@ int launch_prefill_attention(PrefillAttnParams ap, const CUtensorMap &q_map, con
         CH_CUDA_TRY(launch_ex(prefill_attention_tc2_kernel<128>, tgrid, dim3(kTcThreads), tsmem, st, pdl, q_map,
                               k_map, v_map, ap));
         if (ap.splits > 1) {
-            CH_CUDA_TRY(launch_ex(prefill_merge_kernel<128>, dim3(2 * sms), dim3(256), 0, st, pdl, ap));
+            CH_CUDA_TRY(launch_ex(prefill_merge_kernel<128>, dim3(merge_blocks(ap, 128, sms)), dim3(256), 0, st, pdl, ap));
         }
         return 0;
     }
@@ -2041,7 +2049,7 @@ int launch_prefill_attention(PrefillAttnParams ap, const CUtensorMap &q_map, con
         CH_CUDA_TRY(launch_ex(prefill_attention_kernel<64>, agrid, dim3(kPrefillWarps * kWarp), asmem, st, pdl,
                               k_map, v_map, ap));
         if (ap.splits > 1) {
-            CH_CUDA_TRY(launch_ex(prefill_merge_kernel<64>, dim3(2 * sms), dim3(256), 0, st, pdl, ap));
+            CH_CUDA_TRY(launch_ex(prefill_merge_kernel<64>, dim3(merge_blocks(ap, 64, sms)), dim3(256), 0, st, pdl, ap));
         }
     } else {
         CH_CUDA_TRY(cudaFuncSetAttribute(prefill_attention_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -2049,7 +2057,7 @@ int launch_prefill_attention(PrefillAttnParams ap, const CUtensorMap &q_map, con
         CH_CUDA_TRY(launch_ex(prefill_attention_kernel<128>, agrid, dim3(kPrefillWarps * kWarp), asmem, st, pdl,
                               k_map, v_map, ap));
         if (ap.splits > 1) {
-            CH_CUDA_TRY(launch_ex(prefill_merge_kernel<128>, dim3(2 * sms), dim3(256), 0, st, pdl, ap));
+            CH_CUDA_TRY(launch_ex(prefill_merge_kernel<128>, dim3(merge_blocks(ap, 128, sms)), dim3(256), 0, st, pdl, ap));
         }
     }
     return 0;
