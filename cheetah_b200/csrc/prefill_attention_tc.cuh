@@ -73,6 +73,31 @@ __device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, float *v) {
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// Pool rows of key tile `tile`'s two 64-key spans for KV head `kvh` (a span
+// never crosses a page: page_tokens is a multiple of 64). A span past the
+// chunk's last position `pos_last` holds only masked keys: it re-reads span 0
+// (always in range) so the K/V ring holds finite values. A page-table entry
+// out of range sets error 6 where its span holds visible keys.
+__device__ __forceinline__ void kv_tile_rows(const PrefillAttnParams &p, int tile, int kvh, int pos_last,
+                                             int (&rows)[2]) {
+#pragma unroll
+    for (int b = 0; b < 2; ++b) {
+        const int pos0 = tile * kTcKeys + b * 64;
+        const int pidx = pos0 / p.page_tokens;
+        const int page = pidx < p.max_pages ? p.page_table[pidx] : -1;
+        if (page < 0 || page >= p.num_pages) {
+            if (b == 0 || pos0 <= pos_last) {
+                if (p.error) *p.error = 6;
+            }
+            rows[b] = b == 0 ? (int)p.layer_row_offset : rows[0];
+        } else {
+            rows[b] = (int)(p.layer_row_offset + ((long long)page * p.kv_heads + kvh) * p.page_tokens +
+                            (pos0 - pidx * p.page_tokens));
+        }
+        if (b == 1 && pos0 > pos_last) rows[1] = rows[0];
+    }
+}
+
 __global__ void __launch_bounds__(kTcThreads, 1)
     prefill_attention_tc_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constant__ CUtensorMap k_map,
                                 const __grid_constant__ CUtensorMap v_map, const PrefillAttnParams p) {
@@ -155,26 +180,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     break;
                 }
                 const int tile = tile_lo + j;
-                // Rows of the pool for the tile's two 64-key boxes. A box past
-                // the chunk's last position holds only masked keys: it re-reads
-                // box 0 (always in range) so the ring holds finite values.
                 int rows[2];
-#pragma unroll
-                for (int b = 0; b < 2; ++b) {
-                    const int pos0 = tile * kTcKeys + b * 64;
-                    const int pidx = pos0 / p.page_tokens;
-                    const int page = pidx < p.max_pages ? p.page_table[pidx] : -1;
-                    if (page < 0 || page >= p.num_pages) {
-                        if (b == 0 || pos0 <= pos_last) {
-                            if (p.error) *p.error = 6;
-                        }
-                        rows[b] = b == 0 ? (int)p.layer_row_offset : rows[0];
-                    } else {
-                        rows[b] = (int)(p.layer_row_offset + ((long long)page * p.kv_heads + kvh) * p.page_tokens +
-                                        (pos0 - pidx * p.page_tokens));
-                    }
-                    if (b == 1 && pos0 > pos_last) rows[1] = rows[0];
-                }
+                kv_tile_rows(p, tile, kvh, pos_last, rows);
                 uint8_t *ks = ring + s * 2 * kTcKvBytes;
                 uint8_t *vs = ks + kTcKvBytes;
                 const uint32_t bar = smem_u32(&kv_full[s]);
@@ -505,26 +512,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     break;
                 }
                 const int tile = tile_lo + j;
-                // Pool rows of the tile's two 64-key spans (a span never
-                // crosses a page). A span past the chunk's last position holds
-                // only masked keys: it re-reads span 0 so the ring stays finite.
                 int rows[2];
-#pragma unroll
-                for (int b = 0; b < 2; ++b) {
-                    const int pos0 = tile * kTcKeys + b * 64;
-                    const int pidx = pos0 / p.page_tokens;
-                    const int page = pidx < p.max_pages ? p.page_table[pidx] : -1;
-                    if (page < 0 || page >= p.num_pages) {
-                        if (b == 0 || pos0 <= pos_last) {
-                            if (p.error) *p.error = 6;
-                        }
-                        rows[b] = b == 0 ? (int)p.layer_row_offset : rows[0];
-                    } else {
-                        rows[b] = (int)(p.layer_row_offset + ((long long)page * p.kv_heads + kvh) * p.page_tokens +
-                                        (pos0 - pidx * p.page_tokens));
-                    }
-                    if (b == 1 && pos0 > pos_last) rows[1] = rows[0];
-                }
+                kv_tile_rows(p, tile, kvh, pos_last, rows);
                 uint8_t *ks = ring + s * 2 * kTc2KvBytes;
                 uint8_t *vs = ks + kTc2KvBytes;
                 const uint32_t bar = smem_u32(&kv_full[s]);
@@ -883,25 +872,8 @@ __global__ void __launch_bounds__(kTpThreads, 1)
                     break;
                 }
                 const int tile = tile_lo + j;
-                // Rows of the pool for the tile's two 64-key boxes (a box past
-                // the chunk's last position re-reads box 0, as above).
                 int rows[2];
-#pragma unroll
-                for (int b = 0; b < 2; ++b) {
-                    const int pos0 = tile * kTcKeys + b * 64;
-                    const int pidx = pos0 / p.page_tokens;
-                    const int page = pidx < p.max_pages ? p.page_table[pidx] : -1;
-                    if (page < 0 || page >= p.num_pages) {
-                        if (b == 0 || pos0 <= pos_last) {
-                            if (p.error) *p.error = 6;
-                        }
-                        rows[b] = b == 0 ? (int)p.layer_row_offset : rows[0];
-                    } else {
-                        rows[b] = (int)(p.layer_row_offset + ((long long)page * p.kv_heads + kvh) * p.page_tokens +
-                                        (pos0 - pidx * p.page_tokens));
-                    }
-                    if (b == 1 && pos0 > pos_last) rows[1] = rows[0];
-                }
+                kv_tile_rows(p, tile, kvh, pos_last, rows);
                 uint8_t *ks = ring + s * 2 * kTpKvBytes;
                 uint8_t *vs = ks + kTpKvBytes;
                 const uint32_t bar = smem_u32(&kv_full[s]);
