@@ -1121,8 +1121,55 @@ def run_decode_7b(args):
     return 0
 
 
+def attention_trace(R, cfg, sms: int):
+    """Per-key-tile timeline of the two-tile prefill attention kernel from a
+    profiling build (`python -m cheetah_b200.build --define CHEETAH_ATTN_TRACE
+    --out cheetah_b200/libcheetah_cuda_attn_trace.so`, selected with
+    CHEETAH_CUDA_LIB): query block 0, head 0, split 0 of the last layer-0
+    launch of config 3 (the last chunk), in SM cycles since the CTA started."""
+    import ctypes
+    import statistics
+    lib = R.lib()
+    if not hasattr(lib, "cheetah_cuda_debug_attn_trace"):
+        raise SystemExit("prefill-attention-trace needs a library built with -DCHEETAH_ATTN_TRACE "
+                         "(python -m cheetah_b200.build --define CHEETAH_ATTN_TRACE --out <lib>; "
+                         "CHEETAH_CUDA_LIB=<lib>)")
+    buf = (ctypes.c_longlong * 256)()
+    if lib.cheetah_cuda_debug_attn_trace(buf) != 0:
+        raise SystemExit(lib.cheetah_cuda_last_error().decode())
+    ev = [list(buf[16 * j:16 * j + 16]) for j in range(16)]
+    # Split 0 of query block 0 in the last chunk (the launcher's split rule).
+    prefix, prompt, chunk = 2048, 4096, 512  # prefill_bench's config 3
+    offset = prefix + prompt - chunk
+    blocks = ((chunk + 255) // 256) * cfg["q_heads"]
+    key_tiles = (offset + chunk + 127) // 128
+    splits = max(1, min(8, sms // blocks, key_tiles // 2))
+    all_hi = (offset + 255) // 128 + 1
+    n = min(16, -(-all_hi // splits))
+    med = lambda xs: statistics.median(xs) if xs else None
+    rows = ev[:n]
+    return {
+        "launch": f"last chunk (positions {offset}..{offset + chunk - 1}), layer 0, query block 0, head 0, split 0 of {splits}",
+        "key_tiles": n,
+        "events": rows,
+        "event_names": ["A S landed", "A row max", "A O rescaled", "A P released", "B S landed", "B row max",
+                        "B O rescaled", "B P released", "MMA saw P_A", "MMA issued PV_A", "MMA issued S_B(j+1)",
+                        "MMA saw P_B", "MMA issued PV_B", "MMA issued S_A(j+2)", "producer issued tile", "-"],
+        "median_cycles": {
+            "tile_pair": med([rows[j + 1][0] - rows[j][0] for j in range(1, n - 1)]),
+            "A_max_pass": med([r[1] - r[0] for r in rows[1:]]),
+            "A_rescale": med([r[2] - r[1] for r in rows[1:]]),
+            "A_exp_pass": med([r[3] - r[2] for r in rows[1:]]),
+            "mma_issue_pv_a": med([r[9] - r[8] for r in rows[1:]]),
+            "mma_issue_s_b": med([r[10] - r[9] for r in rows[1:n - 1]]),
+            "mma_issue_pv_b": med([r[12] - r[11] for r in rows[1:]]),
+        },
+    }
+
+
 def run_op(args):
-    """`--workload prefill-0.5b | attention`: config 3 or config 2 alone."""
+    """`--workload prefill-0.5b | prefill-attention-trace | attention`: config 3
+    or config 2 alone."""
     import torch
     from cheetah_b200 import runtime as R
     from cheetah_b200.prepared import PreparedModel, resolve_config
@@ -1144,6 +1191,9 @@ def run_op(args):
                 "warmup": 1, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
                 "data": "synthetic (seeded random-init bf16 weights, uniform-random prompt ids)",
                 "config": {"workload": pre["workload"]}, "prefill": pre}
+        if args.workload == "prefill-attention-trace":
+            props = torch.cuda.get_device_properties(torch.cuda.current_device())
+            line["attention_trace"] = attention_trace(R, cfg, props.multi_processor_count)
     print(json.dumps(line), flush=True)
     return 0
 
@@ -1167,7 +1217,8 @@ def main():
     ap.add_argument("--prompt-7b", type=int, default=1024, help="decode-7b-* workloads: prompt tokens")
     ap.add_argument("--workload", default="default",
                     choices=["default", "decode-7b-q8", "decode-7b-q4", "decode-7b-bf16", "serve-0.5b",
-                             "prefill-0.5b", "attention", "attention-case", "gemv-q8", "gemv-q4",
+                             "prefill-0.5b", "prefill-attention-trace", "attention", "attention-case",
+                             "gemv-q8", "gemv-q4",
                              "batch-decode"])
     ap.add_argument("--rows", type=int, default=18944, help="gemv-q8/q4 case")
     ap.add_argument("--cols", type=int, default=3584, help="gemv-q8/q4 case")
@@ -1182,7 +1233,7 @@ def main():
         return run_reference(args)
     if args.workload.startswith("decode-7b"):
         return run_decode_7b(args)
-    if args.workload in ("prefill-0.5b", "attention"):
+    if args.workload in ("prefill-0.5b", "prefill-attention-trace", "attention"):
         return run_op(args)
     if args.workload in ("gemv-q8", "gemv-q4"):
         return case_gemv(args.workload.split("-")[1], args.rows, args.cols)

@@ -3100,6 +3100,15 @@ __attribute__((visibility("default"))) int cheetah_cuda_debug_mk_ptrace(unsigned
 }
 #endif
 
+#ifdef CHEETAH_ATTN_TRACE
+// Profiling builds only: copy the two-tile prefill attention kernel's
+// per-key-tile timeline (kAttnTraceTiles x kAttnTraceEvents cycle stamps).
+__attribute__((visibility("default"))) int cheetah_cuda_debug_attn_trace(long long *out) {
+    CH_CUDA_TRY(cudaMemcpyFromSymbol(out, cheetah::g_attn_trace, sizeof(cheetah::g_attn_trace)));
+    return 0;
+}
+#endif
+
 int cheetah_cuda_device_count(int *count) {
     CH_REQUIRE(count != nullptr, "cheetah_cuda_device_count: null argument");
     int n = 0;

@@ -769,6 +769,27 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 // at a time (the row max, then the exponentials), which keeps it within the
 // 168 registers a thread of a 10-warp CTA can have. Shared memory: Q_A, Q_B
 // (16 KB each), four 32 KB K/V stages, P_A, P_B (32 KB each): 225 KB.
+// Optional per-key-tile timeline of one CTA (query block 0, head 0, split 0
+// of the layer-0 launches; the last such launch's stamps remain), for
+// profiling builds (-DCHEETAH_ATTN_TRACE): clock64 cycles since the CTA
+// started. Events of tile j: 0-3 softmax group A (S landed, row max done,
+// O rescaled, P released), 4-7 the same for group B, 8 MMA thread saw P_A,
+// 9 issued P.V_A, 10 issued S_B(j+1), 11 saw P_B, 12 issued P.V_B, 13 issued
+// S_A(j+2), 14 producer issued tile j's loads.
+constexpr int kAttnTraceTiles = 16;
+constexpr int kAttnTraceEvents = 16;
+#ifdef CHEETAH_ATTN_TRACE
+__device__ long long g_attn_trace[kAttnTraceTiles][kAttnTraceEvents];
+#define ATTN_TRACE(cond, j, ev)                                                  \
+    do {                                                                         \
+        if ((cond) && (j) < kAttnTraceTiles) g_attn_trace[(j)][(ev)] = clock64() - trace_t0; \
+    } while (0)
+#else
+#define ATTN_TRACE(cond, j, ev) \
+    do {                        \
+    } while (0)
+#endif
+
 constexpr int kTpRows = 2 * kTcRows;  // query rows per CTA
 constexpr int kTpThreads = 320;       // producer, MMA, 2 x 4 softmax warps
 constexpr int kTpStages = 4;
@@ -824,6 +845,10 @@ __global__ void __launch_bounds__(kTpThreads, 1)
     const int tile_lo = all_lo + split * per_split;
     const int tile_hi = min(all_hi, tile_lo + per_split);
     const int n_tiles = max(0, tile_hi - tile_lo);
+#ifdef CHEETAH_ATTN_TRACE
+    const long long trace_t0 = clock64();
+    const bool trace = blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && p.layer_row_offset == 0;
+#endif
 
     if (threadIdx.x == 0) {
         mbar_init(smem_u32(&q_full), 1);
@@ -884,6 +909,7 @@ __global__ void __launch_bounds__(kTpThreads, 1)
                     tma_load_2d(smem_u32(vs + b * 64 * 128), &v_map, 0, rows[b], bar);
                 }
                 issued = j + 1;
+                ATTN_TRACE(trace, j, 14);
             }
         }
     } else if (warp == 1) {
@@ -911,6 +937,7 @@ __global__ void __launch_bounds__(kTpThreads, 1)
             // O_g += P_g(j) V_j.
             auto issue_pv = [&](int g, int j) -> bool {
                 if (!mbar_wait(smem_u32(&p_full[g]), j & 1)) return false;
+                ATTN_TRACE(trace, j, 8 + 3 * g);
                 tc_fence_after();
                 const int s = j % kTpStages;
                 const uint32_t v_addr = smem_u32(ring + s * 2 * kTpKvBytes + kTpKvBytes);
@@ -922,6 +949,7 @@ __global__ void __launch_bounds__(kTpThreads, 1)
                               umma_smem_desc_mn(v_addr + k * 2048), kIdescPV, (j > 0 || k > 0) ? 1u : 0u);
                 }
                 umma_commit(smem_u32(&o_full[g]));
+                ATTN_TRACE(trace, j, 9 + 3 * g);
                 return true;
             };
             // S_B(j+1) reuses S_A(j)'s buffer and S_A(j+2) S_B(j)'s: both are
@@ -930,9 +958,11 @@ __global__ void __launch_bounds__(kTpThreads, 1)
             for (int j = 0; ok && j < n_tiles; ++j) {
                 ok = issue_pv(0, j);
                 if (ok && j + 1 < n_tiles) ok = issue_s(1, j + 1);
+                ATTN_TRACE(trace, j, 10);
                 if (ok) ok = issue_pv(1, j);
                 if (ok) umma_commit(smem_u32(&kv_empty[j % kTpStages]));
                 if (ok && j + 2 < n_tiles) ok = issue_s(0, j + 2);
+                ATTN_TRACE(trace, j, 13);
             }
             if (!ok) abort_s = 1;
         }
@@ -960,6 +990,7 @@ __global__ void __launch_bounds__(kTpThreads, 1)
                 break;
             }
             tc_fence_after();
+            ATTN_TRACE(trace && lane == 0 && quad == 2, j, 4 * g);
             const int kp0 = (tile_lo + j) * kTcKeys;
             // Tiles wholly at or below the group's first position need no mask
             // (no window); otherwise key i is visible iff wlo < i <= lim.
@@ -992,6 +1023,7 @@ __global__ void __launch_bounds__(kTpThreads, 1)
             const float m_new = m_cand > m_run + kTpRescaleLog2 ? m_cand : m_run;
             const float alpha = m_new == -INFINITY ? 1.0f : exp2f(m_run - m_new);
             const float neg_m = m_new == -INFINITY ? 0.0f : -m_new;
+            ATTN_TRACE(trace && lane == 0 && quad == 2, j, 4 * g + 1);
             if (j > 0) {
                 // PV_g(j-1) done: P_g's buffer is free and O_g holds tiles < j.
                 if (!__all_sync(0xFFFFFFFFu, mbar_wait(smem_u32(&o_full[g]), (j - 1) & 1))) {
@@ -1011,6 +1043,7 @@ __global__ void __launch_bounds__(kTpThreads, 1)
                     }
                 }
             }
+            ATTN_TRACE(trace && lane == 0 && quad == 2, j, 4 * g + 2);
             // Pass 2: p = 2^(s * scale_log2 - m_new) (a masked key gives 0)
             // into P_g row r, K-major with 128-byte swizzle: keys 64h..64h+63
             // in block h, 16-byte chunk c of the row at (c ^ (r & 7)).
@@ -1050,6 +1083,7 @@ __global__ void __launch_bounds__(kTpThreads, 1)
             m_run = m_new;
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             mbar_arrive(smem_u32(&p_full[g]));
+            ATTN_TRACE(trace && lane == 0 && quad == 2, j, 4 * g + 3);
         }
         if (ok && n_tiles > 0) {
             if (__all_sync(0xFFFFFFFFu, mbar_wait(smem_u32(&o_full[g]), (n_tiles - 1) & 1))) {
